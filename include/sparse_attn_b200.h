@@ -1,0 +1,169 @@
+/*
+ * sparse_attn_b200.h - C ABI of the B200 (sm_100a) dynamic block-sparse prefill path.
+ *
+ * Drop-in native layer under the Python package `sm120_attn` (same module and function names as
+ * accion-intelligence/Qwen38-sparse-attn).  Every entry point takes raw device pointers, element
+ * strides and sizes, runs asynchronously on the given CUDA stream (a `cudaStream_t` passed as
+ * `void*`; NULL = legacy default stream), allocates nothing, and returns SA_OK or a negative
+ * SA_ERR_* code; `sa_last_error()` gives a message for the calling thread's last failure.
+ * Tensors are row-major with explicit element strides; bf16 data is passed as 16-bit words and
+ * e4m3 (float8_e4m3fn) data as bytes.
+ *
+ * Kernels that wait on barriers bound every wait (about 2 s of wall time).  When a wait expires
+ * the kernel writes SA_DEV_* bits into the caller's `status` word (device int32, may be NULL),
+ * stops, frees its tensor memory and returns; `sa_read_status` fetches and clears the word.
+ */
+#ifndef SPARSE_ATTN_B200_H
+#define SPARSE_ATTN_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SA_API __attribute__((visibility("default")))
+#else
+#define SA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------- */
+#define SA_OK 0
+#define SA_ERR_ARG (-1)          /* bad shape, size or argument combination              */
+#define SA_ERR_ALIGN (-2)        /* pointer or stride not aligned as the kernel requires  */
+#define SA_ERR_UNSUPPORTED (-3)  /* head_dim, block size or mode not implemented          */
+#define SA_ERR_CUDA (-4)         /* CUDA runtime error (launch, attribute, symbol)        */
+#define SA_ERR_TMA (-5)          /* TMA tensor-map encoding failed                        */
+#define SA_ERR_DEVICE (-6)       /* a kernel reported a device-side failure (status word) */
+
+/* bits a kernel may set in the device status word */
+#define SA_DEV_WAIT_Q 0x1        /* a wait for the query tile expired                     */
+#define SA_DEV_WAIT_KV 0x2       /* a wait for a key/value stage expired                  */
+#define SA_DEV_WAIT_S 0x4        /* a wait for the score (S) tile expired                 */
+#define SA_DEV_WAIT_P 0x8        /* a wait for the probability (P) tile expired           */
+#define SA_DEV_WAIT_O 0x10       /* a wait for the output accumulator expired             */
+#define SA_DEV_BAD_LIST 0x20     /* a block index in a list was out of range              */
+
+/* selection modes for sa_select */
+#define SA_SELECT_PER_HEAD 0     /* one row per (query head, q block): union=False         */
+#define SA_SELECT_KV_UNION 1     /* one row per (kv head, q block): union over the group   */
+#define SA_SELECT_PAIR_UNION 2   /* one row per (query head, pair of q blocks)             */
+
+SA_API int sa_version(void);
+SA_API const char* sa_last_error(void);
+
+/* Copy the device status word to the host (synchronises `stream`) and reset it to 0.
+ * Returns SA_OK and stores the word in *value. */
+SA_API int sa_read_status(int32_t* status, int32_t* value, void* stream);
+
+/*
+ * (a) Block summary.  Replaces the ATen pooling of
+ *   sm120_attn/sparse_prefill.py:437-446 (`_cached_block_means`: append the chunk's K block means
+ *   to the cache, partial boundary blocks averaged over the rows this chunk holds) and
+ *   sm120_attn/sparse_prefill.py:58-63 (`block_masks`: mean of the valid rows of each q block).
+ * x: bf16 [n, heads, head_dim] with rows at absolute positions pos0 .. pos0+n-1.  For every block
+ * b in [pos0/block, ceil((pos0+n)/block)) and head h writes the fp32 mean of its rows to
+ *   out[h*out_head_stride + (b - out_block0)*out_block_stride + d].
+ * The mean divides by the number of rows the block holds in x, or by `fixed_divisor` when it is
+ * > 0 (the reference's `km is None` path averages zero-padded blocks over BLOCK rows,
+ * sparse_prefill.py:166-168, :216-218).
+ * Optionally (q8 != NULL) also writes the e4m3 quantisation of every row read,
+ *   q8[r*q8_row_stride + h*q8_head_stride + d] = e4m3(bf16(x * inv_scale[h*inv_scale_stride]))
+ * (the glue's bf16-arithmetic quantisation, sparse_prefill.py:230), so one HBM pass serves both.
+ * head_dim % 8 == 0; x 16-byte aligned with strides multiples of 8 elements.
+ */
+SA_API int sa_block_means_bf16(const void* x, int64_t x_row_stride, int64_t x_head_stride, int n, int heads,
+                        int head_dim, int pos0, int block, float* out, int64_t out_head_stride,
+                        int64_t out_block_stride, int out_block0, uint8_t* q8, int64_t q8_row_stride,
+                        int64_t q8_head_stride, const float* inv_scale, int inv_scale_stride, int fixed_divisor,
+                        void* stream);
+
+/*
+ * (b) Block selection.  Replaces `SparsePrefill.block_masks` (sm120_attn/sparse_prefill.py:41-85)
+ * and the list build of sm120_attn/sparse_prefill.py:172-174 / :223-225.
+ * qm: fp32 [MB, num_heads, head_dim] pooled query blocks (block strides given), q block m sits at
+ * absolute block index qblk0 + m.  km: fp32 [num_kv_heads, nb_km, head_dim] cached key-block means;
+ * blocks nb_km .. nb_total-1 are scored as zero vectors (the driver's zero padding,
+ * sparse_prefill.py:219-221).  Per (head, q block): logits = qm.km * scale with future blocks
+ * (j > qblk0+m) at -inf, softmax, keep the smallest top set (ties: lower block id first) whose
+ * float64-accumulated mass rounded to fp32 reaches fp32(tau), force the diagonal and the sink
+ * block, clear the future.  Rows per `mode` (SA_SELECT_*): PER_HEAD row = h*MB + m; KV_UNION
+ * row = hk*MB + m; PAIR_UNION row = h*(MB/2) + t (MB even).
+ * Outputs (any may be NULL): counts[row]; lists[row*list_stride + i] = selected block ids in
+ * ascending order for i < counts[row] (entries past counts[row] are not written);
+ * masks[row*nb_total + j] = 0/1.
+ */
+SA_API int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_head_stride, const float* km,
+              int64_t km_head_stride, int64_t km_block_stride, int nb_km, int num_heads, int num_kv_heads,
+              int head_dim, int MB, int nb_total, int qblk0, float scale, float tau, int mode, int32_t* counts,
+              int32_t* lists, int64_t list_stride, uint8_t* masks, void* stream);
+
+/* scale modes of sa_quantize_e4m3 */
+#define SA_QUANT_MUL 0           /* e4m3(x * s)            fp32 multiply by s = 1/scale        */
+#define SA_QUANT_MUL_BF16 1      /* e4m3(bf16(x * s))      the glue, sparse_prefill.py:230-233 */
+#define SA_QUANT_DIV 2           /* e4m3(x / s)            fp32 division, kai_fa_fp8.py:327    */
+
+/*
+ * e4m3 quantisation of a bf16 [rows, heads, head_dim] tensor.  Replaces
+ * sm120_attn/sparse_prefill.py:230-233 (mode SA_QUANT_MUL_BF16 with s = 1/scale) and
+ * sm120_attn/kernels/kai_fa_fp8.py:325-328 (`quantize_e4m3`: mode SA_QUANT_DIV with s = scale).
+ * s (`scale`) is per head (stride 1) or one scalar (stride 0).  Conversion rounds to nearest even and
+ * saturates at +-448 (torch's cast gives NaN above 464; in-range values match bit for bit).
+ * transpose = 0: out[r*out_row_stride + h*out_head_stride + d];
+ * transpose = 1: out[h*out_head_stride + d*out_row_stride + r] (V^T, keys contiguous), rows
+ *                rows..rows_pad-1 written as zeros.
+ */
+SA_API int sa_quantize_e4m3(const void* x, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads,
+                     int head_dim, const float* scale, int scale_stride, int mode, uint8_t* out,
+                     int64_t out_row_stride, int64_t out_head_stride, int transpose, int rows_pad, void* stream);
+
+/* bf16 [rows, heads, head_dim] -> out[h*out_head_stride + d*out_d_stride + r] (V^T for the BF16
+ * kernel), rows .. rows_pad-1 zero. */
+SA_API int sa_transpose_bf16(const void* x, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads,
+                      int head_dim, void* out, int64_t out_head_stride, int64_t out_d_stride, int rows_pad,
+                      void* stream);
+
+/* amax over a bf16 [rows, heads, head_dim] tensor: out[h] (per_head = 1) or out[0] (per tensor).
+ * Replaces the `.abs().amax()` reductions of sm120_attn/sparse_prefill.py:227 / :465 and
+ * kai_fa_fp8.py:326. */
+SA_API int sa_absmax_bf16(const void* x, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads, int head_dim,
+                   int per_head, float* out, void* stream);
+
+/*
+ * (c) Block-sparse causal attention forward on tcgen05 tensor cores.  Replaces
+ * `attention_sm120_fp8_tma` / `attention_sm120_fp8` (sm120_attn/kernels/kai_fa_fp8_tma.py:447-490,
+ * kai_fa_fp8.py:331-375) for sa_attn_fwd_fp8 and `attention_sm120` (kai_fa_bf16.py:1206-1243) for
+ * sa_attn_fwd_bf16.
+ * q: [n_q, num_heads, head_dim]; k: [kv_len, num_kv_heads, head_dim]; vt: V transposed,
+ * vt[hk*vt_head_stride + d*vt_d_stride + key] (keys contiguous, NOT the reference's permuted key
+ * order); out: bf16 [n_q, num_heads, head_dim].  Element strides.  Query tile m (128 rows) covers
+ * q rows m*128 - q_front .. +127 (rows outside [0, n_q) read as zero, not written) at absolute
+ * positions q_offset + m*128 + r; a key at position j is visible when j <= position and
+ * j < kv_len.  Block lists (counts != NULL): tile m of head h walks
+ * lists[row*list_stride + i], i < counts[row], row = h*ceil((q_front+n_q)/128) + m, each entry a
+ * kv_block-key block (kv_block 64 or 128; q_block must be 128); counts == NULL walks every causal
+ * block.  FP8 scales: softmax uses softmax_scale*q_scale[h]*k_scale[hk] and the output is
+ * multiplied by v_scale[hk] (scale strides 0 = one scalar, 1 = per head); P is rounded to e4m3
+ * after scaling by 448 (kai_fa_fp8.py:248-253).  head_dim must be 128.
+ */
+SA_API int sa_attn_fwd_fp8(const uint8_t* q, int64_t q_row_stride, int64_t q_head_stride, const uint8_t* k,
+                    int64_t k_row_stride, int64_t k_head_stride, const uint8_t* vt, int64_t vt_head_stride,
+                    int64_t vt_d_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
+                    int num_heads, int num_kv_heads, int head_dim, int kv_len, int q_front, int q_offset,
+                    const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block, int kv_block,
+                    const float* q_scale, int q_scale_stride, const float* k_scale, int k_scale_stride,
+                    const float* v_scale, int v_scale_stride, float softmax_scale, int32_t* status, void* stream);
+
+SA_API int sa_attn_fwd_bf16(const void* q, int64_t q_row_stride, int64_t q_head_stride, const void* k,
+                     int64_t k_row_stride, int64_t k_head_stride, const void* vt, int64_t vt_head_stride,
+                     int64_t vt_d_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
+                     int num_heads, int num_kv_heads, int head_dim, int kv_len, int q_front, int q_offset,
+                     const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block, int kv_block,
+                     float softmax_scale, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSE_ATTN_B200_H */

@@ -1,0 +1,60 @@
+"""The C-ABI library loads without a GPU, exports every symbol include/*.h declares, and rejects bad
+arguments before touching the device."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / 'include').glob('*.h'):
+        names |= set(re.findall(r'^SA_API\s+(?:const\s+char\s*\*|int)\s+(sa_\w+)\s*\(', h.read_text(), flags=re.M))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    from sm120_attn import _native as N
+    L = N.lib()
+    declared = declared_symbols()
+    assert declared, 'no declarations parsed'
+    for name in declared:
+        assert hasattr(L, name), name
+    assert set(N.exported_symbols()) == declared
+    assert L.sa_version() == 1
+
+
+@pytest.mark.parametrize('call,code', [
+    (lambda L: L.sa_select(None, 0, 0, None, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0.0, 0.0, 0, None, None, 0, None, None), -1),
+    (lambda L: L.sa_block_means_bf16(None, 0, 0, 10, 2, 100, 0, 64, None, 0, 0, 0, None, 0, 0, None, 0, 0, None), -3),
+    (lambda L: L.sa_attn_fwd_fp8(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, 10, 8, 2, 64, 100, 0, 0, None, None,
+                                 0, 128, 64, None, 0, None, 0, None, 0, 1.0, None, None), -3),
+    (lambda L: L.sa_attn_fwd_bf16(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, 10, 8, 3, 128, 100, 0, 0, None,
+                                  None, 0, 128, 64, 1.0, None, None), -1),
+    (lambda L: L.sa_quantize_e4m3(None, 0, 0, 4, 2, 128, None, 0, 9, None, 0, 0, 0, 0, None), -1),
+])
+def test_argument_validation_without_gpu(call, code):
+    from sm120_attn import _native as N
+    L = N.lib()
+    assert call(L) == code
+    assert L.sa_last_error()
+
+
+def test_native_error_message():
+    from sm120_attn import _native as N
+    with pytest.raises(N.NativeError, match='bad sizes'):
+        N.call('sa_select', None, 0, 0, None, 0, 0, 0, 0, 0, 0, 0, 0, 0, ctypes.c_float(0), ctypes.c_float(0), 0,
+               None, None, 0, None, None)
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from sm120_attn import ops
+    x = torch.zeros(4, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match='CUDA'):
+        ops.absmax(x, per_head=True)

@@ -1,0 +1,287 @@
+"""Kernel parity on the GPU: every CUDA entry point against the numpy oracle on seeded inputs.
+
+Tolerances: integer / byte / index outputs bit-exact; block means rtol 1e-6 (fp32 sums in a different
+order); masks exact except the tau-boundary exemption of `oracle.compare_masks`; attention outputs
+rel-L2 3e-2 (FP8) / max-abs 2e-2 (BF16) against the fp32 reference on the same masks and operands,
+plus a tight check (rel-L2 1e-2) against the P-rounding model of the FP8 kernel.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+import synth
+
+pytestmark = pytest.mark.gpu
+
+DEV = 'cuda'
+
+
+def _ops():
+    from sm120_attn import ops
+    return ops
+
+
+def f32(t):
+    return t.float().cpu().numpy()
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+# ------------------------------------------------------------------------------------------------
+# kernel (a): block means, fused quantisation
+# ------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize('block', [64, 128])
+@pytest.mark.parametrize('heads,n,pos0', [(16, 1000, 3000), (2, 777, 64), (64, 256, 0)])
+def test_block_means(block, heads, n, pos0):
+    ops = _ops()
+    q, _, _, _ = synth.make_qkv(n, n + pos0, heads, heads, 128, q_start=pos0, seed=heads + n, with_v=False)
+    x = q.to(DEV)
+    b0 = pos0 // block
+    b1 = -(-(pos0 + n) // block)
+    out = torch.full((heads, b1 - b0, 128), float('nan'), device=DEV)
+    ops.block_means(x, pos0, block, out, b0)
+    _, ref = O.block_means(f32(q), pos0, block)
+    np.testing.assert_allclose(f32(out), ref, rtol=1e-6, atol=1e-7)
+    # fused e4m3 output (glue arithmetic), per-head scales
+    inv = torch.linspace(50.0, 90.0, heads, device=DEV)
+    q8 = torch.zeros(n, heads, 128, dtype=torch.uint8, device=DEV)
+    ops.block_means(x, pos0, block, out, b0, q8=q8, inv_scale=inv)
+    np.testing.assert_array_equal(q8.cpu().numpy(), O.quantize_glue(f32(q), inv.cpu().numpy()))
+
+
+def test_block_means_fixed_divisor():
+    ops = _ops()
+    _, k, _, _ = synth.make_qkv(8, 1000, 8, 2, 128, seed=3, with_v=False)
+    out = torch.zeros(2, 16, 128, device=DEV)
+    ops.block_means(k.to(DEV), 0, 64, out, 0, fixed_divisor=64)
+    kp = np.concatenate([f32(k), np.zeros((24, 2, 128), np.float32)])
+    _, ref = O.block_means(kp, 0, 64)
+    np.testing.assert_allclose(f32(out), ref, rtol=1e-6, atol=1e-7)
+
+
+def test_quantize_modes_bitexact():
+    from sm120_attn._native import SA_QUANT_DIV, SA_QUANT_MUL_BF16
+    ops = _ops()
+    q, k, v, _ = synth.make_qkv(300, 333, 4, 2, 128, seed=9, strength='strong')
+    xs = v.to(DEV)
+    s = 7.1 / 448.0
+    out = torch.empty(333, 2, 128, dtype=torch.uint8, device=DEV)
+    ops.quantize(xs, torch.tensor([1.0 / s], device=DEV), SA_QUANT_MUL_BF16, out)
+    np.testing.assert_array_equal(out.cpu().numpy(), O.quantize_glue(f32(v), np.float32(1.0 / s)))
+    bits, scale = O.quantize_per_tensor(f32(v))
+    ops.quantize(xs, torch.tensor([scale], device=DEV), SA_QUANT_DIV, out)
+    np.testing.assert_array_equal(out.cpu().numpy(), bits)
+    vt = torch.full((2, 128, 384), 7, dtype=torch.uint8, device=DEV)
+    ops.quantize(xs, torch.tensor([scale], device=DEV), SA_QUANT_DIV, vt, transpose=True, rows_pad=384)
+    ref_t = np.zeros((2, 128, 384), np.uint8)
+    ref_t[:, :, :333] = bits.transpose(1, 2, 0)
+    np.testing.assert_array_equal(vt.cpu().numpy(), ref_t)
+    # bf16 transpose
+    vtb = torch.full((2, 128, 384), 3.0, dtype=torch.bfloat16, device=DEV)
+    ops.transpose_bf16(xs, vtb, 384)
+    ref_b = np.zeros((2, 128, 384), np.float32)
+    ref_b[:, :, :333] = f32(v).transpose(1, 2, 0)
+    np.testing.assert_array_equal(f32(vtb), ref_b)
+
+
+def test_absmax():
+    ops = _ops()
+    q, _, _, _ = synth.make_qkv(517, 600, 8, 2, 128, seed=4, strength='strong')
+    x = q.to(DEV)
+    np.testing.assert_array_equal(ops.absmax(x, per_head=True).cpu().numpy(), np.abs(f32(q)).max(axis=(0, 2)))
+    assert ops.absmax(x, per_head=False).item() == np.abs(f32(q)).max()
+
+
+# ------------------------------------------------------------------------------------------------
+# kernel (b): selection
+# ------------------------------------------------------------------------------------------------
+SEL = [  # (block, kv, q_start, n, strength, H, Hk)
+    (128, 8192, 7168, 1024, 'unit', 64, 8),
+    (128, 8192, 7168, 1024, 'strong', 64, 8),
+    (64, 4096, 3072, 1024, 'strong', 8, 2),
+    (64, 4000, 3000, 1000, 'strong', 16, 2),
+    (128, 20000, 12000, 8000, 'strong', 8, 1),
+]
+
+
+@pytest.mark.parametrize('case', SEL, ids=[f'b{c[0]}_{c[4]}_{c[1]}_{c[5]}' for c in SEL])
+def test_select_matches_oracle(case):
+    from sm120_attn._native import SA_SELECT_KV_UNION, SA_SELECT_PAIR_UNION, SA_SELECT_PER_HEAD
+    ops = _ops()
+    block, kv, q_start, n, strength, H, Hk = case
+    q, k, _, _ = synth.make_qkv(n, kv, H, Hk, 128, block=block, q_start=q_start, seed=kv + n, strength=strength,
+                                with_v=False)
+    qs = q_start - q_start % block
+    _, kmr = O.block_means(f32(k), 0, block)
+    qm = O.q_block_means(f32(q), q_start, block)
+    MB, NB = qm.shape[0], kmr.shape[1]
+    if block == 64 and MB % 2:
+        qm = np.concatenate([qm, np.zeros((1, H, 128), np.float32)])
+        MB += 1
+    qm_d, km_d = torch.from_numpy(qm).to(DEV), torch.from_numpy(kmr).to(DEV)
+    nb_total = max(NB, qs // block + MB)
+    ref, aux = O.select_masks(qm, kmr, qs, block, H, Hk, 0.95, nb_total=nb_total, return_aux=True)
+    masks = torch.empty(H * MB, nb_total, dtype=torch.uint8, device=DEV)
+    counts = torch.empty(H * MB, dtype=torch.int32, device=DEV)
+    lists = torch.full((H * MB, nb_total), -1, dtype=torch.int32, device=DEV)
+    ops.select(qm_d, km_d, H, Hk, nb_total, qs // block, 128 ** -0.5, 0.95, SA_SELECT_PER_HEAD, counts=counts,
+               lists=lists, masks=masks)
+    got = masks.cpu().numpy().astype(bool).reshape(H, MB, nb_total)
+    nbad, unexplained = O.compare_masks(got, ref, aux, 0.95, Hk)
+    assert not unexplained, (nbad, unexplained[:8])
+    c, li = counts.cpu().numpy(), lists.cpu().numpy()
+    gm = got.reshape(H * MB, -1)
+    np.testing.assert_array_equal(c, gm.sum(1))
+    for r in range(H * MB):
+        np.testing.assert_array_equal(li[r, :c[r]], np.nonzero(gm[r])[0])
+    # kv-head union
+    um = torch.empty(Hk * MB, nb_total, dtype=torch.uint8, device=DEV)
+    ops.select(qm_d, km_d, H, Hk, nb_total, qs // block, 128 ** -0.5, 0.95, SA_SELECT_KV_UNION, masks=um)
+    np.testing.assert_array_equal(um.cpu().numpy().astype(bool).reshape(Hk, MB, -1),
+                                  got.reshape(Hk, H // Hk, MB, -1).any(1))
+    if block == 64:
+        pm = torch.empty(H * MB // 2, nb_total, dtype=torch.uint8, device=DEV)
+        ops.select(qm_d, km_d, H, Hk, nb_total, qs // block, 128 ** -0.5, 0.95, SA_SELECT_PAIR_UNION, masks=pm)
+        np.testing.assert_array_equal(pm.cpu().numpy().astype(bool).reshape(H, MB // 2, -1), O.pair_union(got))
+
+
+# ------------------------------------------------------------------------------------------------
+# kernel (c): attention
+# ------------------------------------------------------------------------------------------------
+def _lists_from_masks(masks):
+    counts, lists = O.masks_to_lists(masks)
+    return torch.from_numpy(counts).to(DEV), torch.from_numpy(lists).to(DEV)
+
+
+def _random_tile_masks(H, n_tiles, NB, q_pos_tile0, kv_block, density, seed):
+    """Per-head masks over 128-row tiles: random blocks plus the sink and every causal-diagonal block."""
+    rng = np.random.default_rng(seed)
+    m = rng.random((H, n_tiles, NB)) < density
+    for t in range(n_tiles):
+        lo = q_pos_tile0 + t * 128
+        hi = lo + 127
+        for b in range(NB):
+            if b * kv_block > hi:
+                m[:, t, b] = False
+            elif (b + 1) * kv_block - 1 >= lo:
+                m[:, t, b] = True
+        m[:, t, 0] = True
+    return m
+
+
+def _fp8_case(n, kv, H, Hk, seed, per_head=False):
+    q, k, v, _ = synth.make_qkv(n, kv, H, Hk, 128, seed=seed)
+    qf, kf, vf = f32(q), f32(k), f32(v)
+    if per_head:
+        sq = np.abs(qf).max(axis=(0, 2)) / 448.0
+        sk = np.abs(kf).max(axis=(0, 2)) / 448.0
+        sv = np.abs(vf).max(axis=(0, 2)) / 448.0
+    else:
+        sq, sk, sv = (np.array([np.abs(t).max() / 448.0]) for t in (qf, kf, vf))
+    q8 = O.quantize_glue(qf, (1.0 / sq).astype(np.float32))
+    k8 = O.quantize_glue(kf, (1.0 / sk).astype(np.float32))
+    v8 = O.quantize_glue(vf, (1.0 / sv).astype(np.float32))
+    return (q, k, v), (q8, k8, v8), (sq.astype(np.float32), sk.astype(np.float32), sv.astype(np.float32))
+
+
+def _run_fp8(q8, k8, v8, scales, kv_len, q_front, q_offset, counts=None, lists=None, kv_block=64):
+    ops = _ops()
+    n, H, D = q8.shape
+    Hk = k8.shape[1]
+    rows_pad = -(-kv_len // 128) * 128
+    vt = np.zeros((Hk, D, rows_pad), np.uint8)
+    vt[:, :, :kv_len] = v8[:kv_len].transpose(1, 2, 0)
+    out = torch.full((n, H, D), float('nan'), dtype=torch.bfloat16, device=DEV)
+    sq, sk, sv = (torch.from_numpy(np.asarray(s, np.float32)).to(DEV) for s in scales)
+    ops.attn_fp8(torch.from_numpy(q8).to(DEV), torch.from_numpy(k8).to(DEV), torch.from_numpy(vt).to(DEV), out,
+                 kv_len, q_front, q_offset, counts, lists, kv_block, sq, sk, sv, D ** -0.5)
+    ops.check_status(DEV)
+    return f32(out)
+
+
+def _deq(bits, s):
+    s = np.asarray(s, np.float32)
+    sc = s[None, :, None] if s.size > 1 else s.reshape(1, 1, 1)
+    return O.e4m3_decode(bits) * sc
+
+
+@pytest.mark.parametrize('n,kv,H,Hk,per_head', [(256, 1024, 4, 2, False), (100, 300, 4, 1, True),
+                                                (128, 128, 2, 2, False), (1000, 4032, 8, 2, True)])
+def test_attn_fp8_dense(n, kv, H, Hk, per_head):
+    _, (q8, k8, v8), scales = _fp8_case(n, kv, H, Hk, seed=n + kv, per_head=per_head)
+    out = _run_fp8(q8, k8, v8, scales, kv, 0, kv - n)
+    model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, kv - n, q_block=128, kv_block=128)
+    ref = O.attention_ref(_deq(q8, scales[0]), _deq(k8, scales[1]), _deq(v8, scales[2]), kv - n)
+    assert rel_l2(out, model) < 1e-2, rel_l2(out, model)
+    assert rel_l2(out, ref) < 3e-2, rel_l2(out, ref)
+
+
+@pytest.mark.parametrize('kv_block', [64, 128])
+@pytest.mark.parametrize('n,kv,q_front,density', [(512, 2048, 0, 0.3), (1000, 8192, 40, 0.2), (300, 1500, 77, 0.5)])
+def test_attn_fp8_sparse(kv_block, n, kv, q_front, density):
+    H, Hk = 8, 2
+    _, (q8, k8, v8), scales = _fp8_case(n, kv, H, Hk, seed=n + q_front, per_head=True)
+    q_pos0 = kv - n                                   # absolute position of q row 0
+    q_offset = q_pos0 - q_front                       # position of virtual row 0 of tile 0
+    n_tiles = -(-(q_front + n) // 128)
+    NB = -(-kv // kv_block)
+    masks = _random_tile_masks(H, n_tiles, NB, q_offset, kv_block, density, seed=n)
+    counts, lists = _lists_from_masks(masks)
+    out = _run_fp8(q8, k8, v8, scales, kv, q_front, q_offset, counts, lists, kv_block)
+    ref = O.attention_ref(_deq(q8, scales[0]), _deq(k8, scales[1]), _deq(v8, scales[2]), q_pos0, masks,
+                          q_block=128, kv_block=kv_block, q_front=q_front)
+    model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, q_pos0, counts.cpu().numpy(), lists.cpu().numpy(),
+                                         q_block=128, kv_block=kv_block, q_front=q_front)
+    assert rel_l2(out, model) < 1e-2, rel_l2(out, model)
+    assert rel_l2(out, ref) < 3e-2, rel_l2(out, ref)
+
+
+def test_attn_fp8_empty_rows_give_zeros():
+    H, Hk, n, kv = 2, 1, 256, 512
+    _, (q8, k8, v8), scales = _fp8_case(n, kv, H, Hk, seed=5)
+    counts = torch.zeros(H * 2, dtype=torch.int32, device=DEV)
+    lists = torch.zeros(H * 2, 4, dtype=torch.int32, device=DEV)
+    out = _run_fp8(q8, k8, v8, scales, kv, 0, kv - n, counts, lists, 128)
+    assert np.all(out == 0)
+
+
+def _run_bf16(q, k, v, kv_len, q_front, q_offset, counts=None, lists=None, kv_block=64):
+    ops = _ops()
+    n, H, D = q.shape
+    Hk = k.shape[1]
+    rows_pad = -(-kv_len // 128) * 128
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    vt = torch.empty(Hk, D, rows_pad, dtype=torch.bfloat16, device=DEV)
+    ops.transpose_bf16(vd[:kv_len], vt, rows_pad)
+    out = torch.full((n, H, D), float('nan'), dtype=torch.bfloat16, device=DEV)
+    ops.attn_bf16(qd, kd, vt, out, kv_len, q_front, q_offset, counts, lists, kv_block, D ** -0.5)
+    ops.check_status(DEV)
+    return f32(out)
+
+
+@pytest.mark.parametrize('n,kv,H,Hk', [(256, 1024, 4, 2), (100, 300, 4, 1), (2048, 2048, 2, 2)])
+def test_attn_bf16_dense(n, kv, H, Hk):
+    q, k, v, _ = synth.make_qkv(n, kv, H, Hk, 128, seed=n * 7 + kv)
+    out = _run_bf16(q, k, v, kv, 0, kv - n)
+    ref = O.attention_ref(f32(q), f32(k), f32(v), kv - n)
+    assert np.abs(out - ref).max() < 2e-2
+
+
+@pytest.mark.parametrize('kv_block', [64, 128])
+def test_attn_bf16_sparse(kv_block):
+    H, Hk, n, kv, q_front = 8, 2, 700, 4000, 30
+    q, k, v, _ = synth.make_qkv(n, kv, H, Hk, 128, seed=kv_block)
+    q_pos0 = kv - n
+    q_offset = q_pos0 - q_front
+    n_tiles = -(-(q_front + n) // 128)
+    NB = -(-kv // kv_block)
+    masks = _random_tile_masks(H, n_tiles, NB, q_offset, kv_block, 0.3, seed=kv_block)
+    counts, lists = _lists_from_masks(masks)
+    out = _run_bf16(q, k, v, kv, q_front, q_offset, counts, lists, kv_block)
+    ref = O.attention_ref(f32(q), f32(k), f32(v), q_pos0, masks, q_block=128, kv_block=kv_block, q_front=q_front)
+    assert np.abs(out - ref).max() < 2e-2
