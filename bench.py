@@ -1,0 +1,371 @@
+#!/usr/bin/env python
+"""Headline benchmark: sparse FP8 prefill attention on B200, TFLOPS on executed blocks.
+
+One step = one prefill chunk through the drop-in API `SparsePrefill.forward_sm120fp8` with the
+incremental block-mean cache (`_cached_block_means`): pool the chunk's keys into the cache
+(kernel a), pool + quantise the queries (kernel a), select blocks (kernel b), quantise K and V^T,
+block-sparse FP8 attention (kernel c).  Shape of BASELINE configs[1]: Q 8192 rows at offset 57344
+against 65536 keys, 64 query / 8 KV heads, head_dim 128, block 128, tau 0.95, seeded synthetic
+inputs with the benchmark's hot-block injection.  Inputs (q 134 MB, k/v 134 MB each) exceed the
+126 MB L2, so no flush is needed between steps.
+
+value = (sum over ranks of causal FLOPs x kept fraction) / (max over ranks of the device time of
+the K timed steps) - the reference's "sparse TFLOPS" definition (tests/test_fa_bf16.py:105-120).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+Multi-GPU: units are KV-head groups with no data-path collective.  Default `--scaling weak`: every
+rank owns 8 KV heads (64 query heads) of a problem with 8N KV heads, so per-GPU work is the 1-GPU
+workload at every N.  `--scaling strong` splits the 8 KV heads of one problem over the N GPUs.
+`--impl reference` times the reference algorithm's CPU restatement (oracle/, numpy) on the host
+cores on a bounded sample of the same workload (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT / 'qwen38-sparse-attn_b200', ROOT, ROOT / 'tests'):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+METRIC = 'sparse prefill attention TFLOPS (exec blocks) + prefill TTFT @64K/128K/256K, 1/2/4/8 B200'
+H_FULL, HK_FULL, D = 64, 8, 128
+N_Q, KV, BLOCK, TAU = 8192, 65536, 128, 0.95
+Q_START = KV - N_Q
+# Kernels of this package launched per step: K-chunk block means, Q block means + e4m3, selection,
+# K e4m3, V^T e4m3, attention.
+LAUNCHES_PER_STEP = 6
+# DRAM bytes of the attention kernel per launch from the ncu capture summarised in
+# profiles/attn_fwd_fp8_sparse_prefill.md (None until captured).
+ATTN_DRAM_BYTES = None
+
+
+def peaks():
+    f = ROOT / 'MEASURED_PEAKS.json'
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d['hbm_gbs']), float(d['bf16_tflops']), 'measured'
+    return 6650.0, 1590.0, 'fallback'
+
+
+def causal_flops(h, d, n, kv):
+    return 4.0 * h * d * n * (kv - n + (n + 1) / 2)
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--id={self.gpu}', f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '200'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == 'active':
+                    reasons.add(nm)
+        sm.sort()
+        return {'sm_mhz': sm[len(sm) // 2] if sm else None, 'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+def make_rank_inputs(hk, seed, strength, device):
+    import synth
+    q, k, v, _ = synth.make_qkv(N_Q, KV, hk * (H_FULL // HK_FULL), hk, D, block=BLOCK, q_start=Q_START, seed=seed,
+                                strength=strength, hot=6, device=device)
+    return q.contiguous(), k.contiguous(), v.contiguous()
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', timeout=timedelta(seconds=120), device_id=dev)
+    import sm120_attn.sparse_prefill as ksp
+    from sm120_attn import ops
+    ksp.BLOCK = BLOCK
+    if args.scaling == 'strong':
+        if HK_FULL % world:
+            raise SystemExit('strong scaling needs N to divide 8')
+        hk = HK_FULL // world
+    else:
+        hk = HK_FULL
+    h = hk * (H_FULL // HK_FULL)
+    q, k, v = make_rank_inputs(hk, 1000 + rank, args.strength, dev)
+    sp = ksp.SparsePrefill(h, hk, D, dev, tau=TAU, min_kv=0, min_q=0, kernel='sm120fp8')
+    out = torch.empty(N_Q, h, D, dtype=torch.bfloat16, device=dev)
+    layer = 'bench'
+    # request state before this chunk: history keys 0..Q_START are in the cache (built once, untimed)
+    ksp._KMEAN_CACHE.clear()
+    ksp._cached_block_means(layer, 0, k[:Q_START], 0, Q_START)
+    scales = ksp._cached_scales(layer, 0, q, k, v, 0)
+
+    def rewind():
+        e = ksp._KMEAN_CACHE[(layer, 0)]
+        e['last_kv'] = Q_START
+        e['nb'] = Q_START // BLOCK
+
+    def step(qq, kk_chunk):
+        km = ksp._cached_block_means(layer, 0, kk_chunk, Q_START, KV)
+        sp.forward_sm120fp8(qq, k, v, Q_START, out=out, km=km, scales=scales)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # ---------------- device-resident timed region
+    for _ in range(args.warmup):
+        rewind()
+        step(q, k[Q_START:])
+    sp.kernel_events = []
+    clocks = Clocks(local)
+    barrier()
+    clocks.start()
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.profile_range:
+        torch.cuda.profiler.start()
+    t0.record(stream)
+    for _ in range(args.steps):
+        rewind()
+        step(q, k[Q_START:])
+    t1.record(stream)
+    barrier()
+    if args.profile_range:
+        torch.cuda.profiler.stop()
+    clk = clocks.stop()
+    ms_total = t0.elapsed_time(t1)
+    attn_ms = [s.elapsed_time(e) for s, e in sp.kernel_events]
+    sp.kernel_events = None
+    kept_blocks = int(sp.last_counts.sum().item())
+    causal_blocks = h * ((Q_START // BLOCK) * (N_Q // BLOCK) + (N_Q // BLOCK) * (N_Q // BLOCK + 1) // 2)
+    kept = kept_blocks / causal_blocks
+    flops = causal_flops(h, D, N_Q, KV) * kept
+    tile_flops = kept_blocks * 4.0 * D * 128 * 128
+    # ---------------- end-to-end through the public API with pinned host buffers
+    q_h = q.cpu().pin_memory()
+    k_h = k[Q_START:].cpu().pin_memory()
+    v_h = v[Q_START:].cpu().pin_memory()
+    o_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_d = torch.empty_like(q)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        k[Q_START:].copy_(k_h, non_blocking=True)
+        v[Q_START:].copy_(v_h, non_blocking=True)
+        rewind()
+        step(q_d, k[Q_START:])
+        o_h.copy_(out, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    h2d = q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2
+    d2h = o_h.numel() * 2
+    ops.check_status(dev)
+    # ---------------- reductions over ranks
+    vals = torch.tensor([ms_total, e2e_ms, sum(attn_ms) / max(len(attn_ms), 1)], dtype=torch.float64, device=dev)
+    sums = torch.tensor([flops, tile_flops], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
+    ms_total, e2e_ms, attn_avg = vals.tolist()
+    flops_all, tile_all = sums.tolist()
+    hbm, bf16, how = peaks()
+    fp8_peak = 2.0 * bf16
+    value = flops_all * args.steps / (ms_total * 1e-3) / 1e12
+    e2e_val = flops_all * args.steps / (e2e_ms * 1e-3) / 1e12
+    achieved = (tile_all / world) / (attn_avg * 1e-3) / 1e12
+    line = {
+        'metric': METRIC,
+        'value': round(value, 2),
+        'unit': 'TFLOPS',
+        'n_gpus': world,
+        'steps': args.steps,
+        'warmup': args.warmup,
+        'ms_per_step': round(ms_total / args.steps, 4),
+        'higher_is_better': True,
+        'scaling': args.scaling,
+        'vs_baseline': None,
+        'dtype': 'fp8-e4m3 (fp32 accumulate, bf16 in/out)',
+        'data': 'synthetic (seeded N(0,1) q/k/v with sink + 6 hot blocks per KV head)',
+        'config': {
+            'workload': f'sparse FP8 prefill chunk (configs[1] shape): q {N_Q} @ {Q_START} vs {KV} keys, '
+                        f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection',
+            'global_batch': 1, 'seq_len': KV, 'chunk': N_Q,
+            'parallelism': f'kv-head shards x{world} ({args.scaling}), no collective on the data path',
+            'kept_fraction': round(kept, 4),
+            'l2': 'inputs larger than L2 (q 134 MB, k 134 MB, v 134 MB per GPU); no flush',
+        },
+        'roofline': {
+            'bound': 'tensor', 'kernel': 'attn_fwd_kernel<fp8>',
+            'achieved': round(achieved, 1), 'peak': round(fp8_peak, 1), 'unit': 'TFLOP/s',
+            'frac': round(achieved / fp8_peak, 4),
+            'peak_source': f'2 x {how} bf16 dense burst ({bf16} TF/s, MEASURED_PEAKS.json): B200 e4m3 dense rate is '
+                           'twice bf16',
+            'attn_ms_per_launch': round(attn_avg, 4),
+            'traffic': ATTN_DRAM_BYTES,
+        },
+        'e2e': {'value': round(e2e_val, 2), 'unit': 'TFLOPS', 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+                'ms_per_step': round(e2e_ms / args.steps, 4),
+                'path': 'pinned host q/k/v of the chunk -> SparsePrefill.forward_sm120fp8 -> pinned host output'},
+        'gpu_launches': LAUNCHES_PER_STEP * args.steps,
+        'clocks': clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line['cpu_baseline'] = cpu_baseline(args.strength)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_sample(strength, seconds_budget=20.0):
+    """Reference algorithm on the host (oracle/, numpy): selection + masked fp32 attention of the
+    last `rows` query rows of one KV-head group of the workload; returns (TFLOPS, description, threads)."""
+    import numpy as np
+    import torch
+    import oracle as O
+    import synth
+    torch.manual_seed(0)
+    hk, g = 1, H_FULL // HK_FULL
+    q, k, v, _ = synth.make_qkv(N_Q, KV, g * hk, hk, D, block=BLOCK, q_start=Q_START, seed=1000, strength=strength,
+                                hot=6)
+    qf, kf, vf = (t.float().numpy() for t in (q, k, v))
+    t_start = time.perf_counter()
+    kc = O.KMeanCacheOracle(BLOCK)
+    kc.update('cpu', 0, kf[:Q_START], 0, Q_START)
+    km = kc.update('cpu', 0, kf[Q_START:], Q_START, KV)
+    qm = O.q_block_means(qf, Q_START, BLOCK)
+    masks = O.select_masks(qm, km, Q_START, BLOCK, g * hk, hk, TAU)
+    t_sel = time.perf_counter() - t_start
+    rows = 256
+    done_rows, flops, t_attn = 0, 0.0, 0.0
+    n_blocks = N_Q // BLOCK
+    m = n_blocks - 1
+    while m >= 0 and t_attn < seconds_budget:
+        r0 = m * BLOCK
+        t0 = time.perf_counter()
+        O.attention_ref(qf[r0:r0 + BLOCK], kf, vf, Q_START + r0, masks[:, m:m + 1], q_block=BLOCK, kv_block=BLOCK)
+        t_attn += time.perf_counter() - t0
+        kept = masks[:, m].sum()
+        flops += 4.0 * D * BLOCK * BLOCK * kept
+        done_rows += BLOCK
+        m -= 1
+        if done_rows >= rows and t_attn > 2.0:
+            break
+    tflops = flops / (t_attn + t_sel * done_rows / N_Q) / 1e12
+    threads = torch.get_num_threads()
+    desc = (f'oracle (numpy fp32, BLAS threads) selection of 1 KV head x 8 query heads over the full chunk '
+            f'({t_sel:.2f} s) + masked fp32 attention of the last {done_rows} query rows x 8 heads '
+            f'({t_attn:.2f} s); selection time pro-rated to the sampled rows')
+    return tflops, desc, threads
+
+
+def cpu_baseline(strength):
+    val, desc, threads = cpu_sample(strength)
+    return {'value': round(val, 6), 'unit': 'TFLOPS', 'cores': os.cpu_count(), 'threads': threads, 'kind': 'port',
+            'sample': desc}
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    if rank != 0:
+        return
+    vals = []
+    desc, threads = '', 0
+    for _ in range(max(1, min(args.steps, 2))):
+        v, desc, threads = cpu_sample(args.strength, seconds_budget=10.0)
+        vals.append(v)
+    value = sum(vals) / len(vals)
+    line = {
+        'metric': METRIC, 'value': round(value, 6), 'unit': 'TFLOPS', 'impl': 'reference', 'n_gpus': world,
+        'steps': len(vals), 'warmup': 0, 'higher_is_better': True, 'scaling': args.scaling, 'vs_baseline': None,
+        'dtype': 'fp32', 'data': 'synthetic (seeded, same workload as the b200 arm)',
+        'config': {'workload': f'sparse prefill chunk (configs[1] shape): q {N_Q} @ {Q_START} vs {KV} keys, '
+                               f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection',
+                   'global_batch': 1, 'seq_len': KV, 'parallelism': 'host cores of rank 0'},
+        'cpu_baseline': {'value': round(value, 6), 'unit': 'TFLOPS', 'cores': os.cpu_count(), 'threads': threads,
+                         'kind': 'port', 'sample': desc},
+        'e2e': {'value': round(value, 6), 'unit': 'TFLOPS', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    ap.add_argument('--scaling', default='weak', choices=['weak', 'strong'])
+    ap.add_argument('--strength', default='unit', choices=['unit', 'strong'])
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--profile-range', action='store_true',
+                    help='bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)')
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == 'b200':
+        print('note: warmup raised to 3', file=sys.stderr)
+        args.warmup = 3
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == '__main__':
+    main()

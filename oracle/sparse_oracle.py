@@ -394,15 +394,17 @@ def attention_ref(q, k, v, q_pos0: int, masks=None, q_block: int = 64, kv_block:
 
 
 def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None, lists=None,
-                               q_block: int = 128, kv_block: int = 64, q_front: int = 0, tile: int = 128):
+                               q_block: int = 128, kv_block: int = 64, q_front: int = 0, tile: int = 128,
+                               key_tile: int = 64):
     """Numerical model of the block-sparse FP8 forward (kai_fa_fp8.py:248-292, kai_fa_fp8_tma.py:256-272).
 
-    Walks each (head, 128-row tile)'s block list from the last entry to the first, one
-    `tile`-key tile at a time (two 64-key blocks per tile when kv_block == 64), with the online
-    softmax in the exp2 domain, P scaled by 448 and rounded to e4m3 before the PV product, the row
-    sum over unrounded P, and `O * (sv / 448) / rowsum` (0 for an empty row).  Inputs are e4m3 bit
-    patterns q8 [n, H, D], k8 [N, Hk, D], v8 [N, Hk, D]; per-head scale arrays or scalars.
-    Dense when counts is None.  Returns fp32 [n, H, D].
+    Walks each (head, 128-row tile)'s block list from the last entry to the first in `key_tile`-key
+    steps (a 128-key block is split, upper half first), with the online softmax in the exp2 domain,
+    P scaled by 448 and rounded to e4m3 before the PV product, the row sum over unrounded P, and
+    `O * (sv / 448) / rowsum` (0 for an empty row).  The order and granularity of the walk set where
+    P is rounded, so they follow the CUDA kernel.  Inputs are e4m3 bit patterns q8 [n, H, D],
+    k8 [N, Hk, D], v8 [N, Hk, D]; per-head scale arrays or scalars.  Dense when counts is None.
+    Returns fp32 [n, H, D].
     """
     qv, kv, vv = (e4m3_decode(t).astype(np.float64) for t in (q8, k8, v8))
     n, H, D = qv.shape
@@ -415,7 +417,6 @@ def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None,
     qpos0 = q_pos0 - q_front                                 # absolute position of virtual row 0
     out = np.zeros((n, H, D), dtype=F32)
     log2e = 1.4426950408889634
-    per_tile = tile // kv_block
     for h in range(H):
         hk = h // g
         c = float(F32(D ** -0.5 * sq[h] * sk[hk] * log2e))
@@ -427,18 +428,18 @@ def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None,
             qt = np.zeros((tile, D))
             qt[valid_rows] = qv[rows[valid_rows], h]
             if counts is None:
-                nblk = min(-(-(qpos0 + (t + 1) * tile) // kv_block), -(-N // kv_block))
-                blks = list(range(nblk))
+                nkeys = min(qpos0 + (t + 1) * tile, N)
+                starts = list(range(0, nkeys, key_tile))[::-1]
             else:
                 r = h * (-(-(q_front + n) // q_block)) + (t * tile) // q_block
-                blks = [int(b) for b in lists[r, :counts[r]]]
-            blks = blks[::-1]
+                starts = []
+                for b in [int(x) for x in lists[r, :counts[r]]][::-1]:
+                    starts += list(range(b * kv_block, (b + 1) * kv_block, key_tile))[::-1]
             m = np.full(tile, -np.inf)
             l = np.zeros(tile)
             o = np.zeros((tile, D))
-            for s in range(0, len(blks), per_tile):
-                grp = blks[s:s + per_tile]
-                keys = np.concatenate([np.arange(b * kv_block, (b + 1) * kv_block) for b in grp])
+            for k0 in starts:
+                keys = np.arange(k0, k0 + key_tile)
                 kk = np.zeros((len(keys), D))
                 vk = np.zeros((len(keys), D))
                 inr = keys < N

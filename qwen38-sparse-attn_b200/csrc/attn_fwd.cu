@@ -25,34 +25,43 @@
 namespace sa {
 namespace {
 
-constexpr int KEY_NONE = 1 << 30;   // key base of an absent half tile: every key masked, TMA zero-fills
+constexpr int KEY_NONE = 1 << 30;   // key base of an absent tile: every key masked, TMA zero-fills
+constexpr int KEY_END = -1;         // stage descriptor after the last tile of a walk
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LOG2_448 = 8.807354922057604f;
 
 template <bool FP8>
 struct Cfg {
     static constexpr int E = FP8 ? 1 : 2;                 // bytes per operand element
-    static constexpr int D = 128;
-    static constexpr int BM = 128, BN = 128;
-    static constexpr int KST = 2;                         // K stages
-    static constexpr int VST = FP8 ? 2 : 1;               // V^T stages
+    static constexpr int D = 128;                         // head_dim
+    static constexpr int BM = 128;                        // query rows per tile (TMEM lanes)
+    static constexpr int BN = 64;                         // keys per S tile
+    static constexpr int NST = FP8 ? 4 : 2;               // K+V^T stages of BN keys
     static constexpr int UK = FP8 ? 32 : 16;              // MMA K per instruction
     static constexpr int QK_STEPS = D / UK;
     static constexpr int PV_STEPS = BN / UK;
     static constexpr int REG_ELEMS = 128 / E;             // head_dim elements per 128-byte swizzle row
     static constexpr int NREG = D / REG_ELEMS;            // swizzle regions along head_dim
-    static constexpr int REG_BYTES = 128 * 128;           // one region: 128 rows x 128 B
-    static constexpr int Q_BYTES = BM * D * E;
-    static constexpr int K_BYTES = BN * D * E;
-    static constexpr int VROW = 64 * E;                   // bytes per V^T row of a 64-key chunk
-    static constexpr int VCHUNK = D * VROW;               // one 64-key chunk of V^T
-    static constexpr int V_BYTES = 2 * VCHUNK;
-    static constexpr int SMEM_TILES = Q_BYTES + KST * K_BYTES + VST * V_BYTES;
+    static constexpr int Q_REG = BM * 128;                // bytes of one Q region (128 rows x 128 B)
+    static constexpr int K_REG = BN * 128;                // bytes of one K region (64 rows x 128 B)
+    static constexpr int Q_BYTES = NREG * Q_REG;
+    static constexpr int K_BYTES = NREG * K_REG;
+    static constexpr int VROW = BN * E;                   // bytes per V^T row (64 keys)
+    static constexpr int V_BYTES = D * VROW;
+    static constexpr int STAGE = K_BYTES + V_BYTES;
+    static constexpr int SMEM_TILES = Q_BYTES + NST * STAGE;
     static constexpr int SMEM_BYTES = SMEM_TILES + 1024 /*barriers*/ + 1024 /*alignment*/;
-    static constexpr uint32_t IDESC = instr_desc(128, 128, FP8 ? 0u : 1u);
+    static constexpr uint32_t FMT = FP8 ? 0u : 1u;
+    static constexpr uint32_t IDESC_QK = instr_desc(128, BN, FMT);
+    static constexpr uint32_t IDESC_PV = instr_desc(128, D, FMT);
     static constexpr uint32_t TMEM_COLS = 256;
-    static constexpr uint32_t S_COL = 0, O_COL = 128;
+    static constexpr uint32_t S_COL0 = 0;                 // S/P buffer b at S_COL0 + b * BN
+
+    static constexpr uint32_t O_COL = 128;
     static constexpr int THREADS = 192;
+    // Rescale O only when the running row max grows by more than this (log2 units).  bf16 P can
+    // exceed 1 safely; e4m3 P (scaled to 448) cannot, so the FP8 kernel rescales on every increase.
+    static constexpr float RESCALE_SLACK = FP8 ? 0.f : 8.f;
 };
 
 struct Params {
@@ -61,7 +70,7 @@ struct Params {
     int64_t list_stride;
     void* out;
     int64_t o_row_stride, o_head_stride;
-    int n_q, H, Hk, kv_len, q_front, q_offset, n_tiles, kv_block;
+    int n_q, H, Hk, kv_len, q_front, q_offset, n_tiles, kv_block, q_block, list_rows_per_head;
     const float* q_scale;
     const float* k_scale;
     const float* v_scale;
@@ -70,35 +79,102 @@ struct Params {
     int32_t* status;
 };
 
-struct Walk {
-    const int32_t* list;   // null: dense causal walk
-    int cnt;               // list entries
-    int ntiles;            // key tiles to walk
-    int nblk;              // dense: 128-key blocks
+// Sequence of 64-key tiles one (head, 128-row query tile) walks, from the last block-list entry
+// to the first like the reference (kai_fa_fp8_tma.py:149-162).  Modes: dense causal walk; one
+// list of 64- or 128-key blocks for the whole tile; two lists of 64-key blocks, one per 64-row
+// half of the tile (the BF16 path's 64-row query blocks), walked as their merged union with a
+// per-tile mask of the halves that selected the block.
+struct Walker {
+    const int32_t* a;
+    const int32_t* b;
+    int ia, ib;          // next list index (counting down)
+    int va, vb;          // cached list heads (-1 when exhausted)
+    int dense_next;      // dense: next 64-key tile base, counting down
     int kvb;
+    int half;            // 128-key blocks: which half of the current block comes next (1 = upper)
+    int mode;            // 0 dense, 1 one list, 2 two lists
+    bool bad;
+
+    __device__ __forceinline__ int load(const int32_t* p, int i) const { return i >= 0 ? __ldg(p + i) : -1; }
+
+    __device__ __forceinline__ bool next(int& kbase, uint32_t& rowmask) {
+        rowmask = 3u;
+        if (mode == 0) {
+            if (dense_next < 0) return false;
+            kbase = dense_next;
+            dense_next -= 64;
+            return true;
+        }
+        if (mode == 1) {
+            if (ia < 0) return false;
+            const int blk = __ldg(a + ia);
+            if (blk < 0 || blk >= KEY_NONE / kvb) {
+                bad = true;
+                kbase = KEY_NONE;
+            } else {
+                kbase = blk * kvb + (kvb == 128 ? half * 64 : 0);
+            }
+            if (kvb == 128 && half == 1) {
+                half = 0;
+            } else {
+                half = 1;
+                --ia;
+            }
+            return true;
+        }
+        if (va < 0 && vb < 0) return false;
+        const int blk = max(va, vb);
+        rowmask = (va == blk ? 1u : 0u) | (vb == blk ? 2u : 0u);
+        if (va == blk) { --ia; va = load(a, ia); }
+        if (vb == blk) { --ib; vb = load(b, ib); }
+        if (blk >= KEY_NONE / 64) {
+            bad = true;
+            kbase = KEY_NONE;
+        } else {
+            kbase = blk * 64;
+        }
+        return true;
+    }
 };
 
-__device__ __forceinline__ int sanitize_block(int b, int kvb, bool& bad) {
-    if (b < 0 || b >= KEY_NONE / kvb) {
-        bad = true;
-        return KEY_NONE;
-    }
-    return b * kvb;
-}
-
-// Key positions of the two 64-key halves of key tile t.
-__device__ __forceinline__ void tile_keys(const Walk& w, int t, int& kb0, int& kb1, bool& bad) {
-    if (!w.list) {
-        kb0 = (w.nblk - 1 - t) * 128;
-        kb1 = kb0 + 64;
-    } else if (w.kvb == 128) {
-        kb0 = sanitize_block(__ldg(w.list + (w.cnt - 1 - t)), 128, bad);
-        kb1 = kb0 == KEY_NONE ? KEY_NONE : kb0 + 64;
+__device__ __forceinline__ Walker make_walker(const Params& p, int h, int m) {
+    Walker w;
+    w.bad = false;
+    w.kvb = p.kv_block;
+    w.half = 1;
+    w.a = w.b = nullptr;
+    w.ia = w.ib = -1;
+    w.va = w.vb = -1;
+    w.dense_next = -1;
+    if (!p.counts) {
+        w.mode = 0;
+        const int last = p.q_offset + (m + 1) * 128;              // one past the tile's last position
+        const int keys = min(last, p.kv_len);
+        w.dense_next = keys > 0 ? ((keys + 63) / 64 - 1) * 64 : -1;
+    } else if (p.q_block == 128) {
+        w.mode = 1;
+        const int64_t row = static_cast<int64_t>(h) * p.list_rows_per_head + m;
+        w.a = p.lists + row * p.list_stride;
+        w.ia = max(__ldg(p.counts + row), 0) - 1;
     } else {
-        const int i = w.cnt - 1 - 2 * t;
-        kb0 = sanitize_block(__ldg(w.list + i), 64, bad);
-        kb1 = i >= 1 ? sanitize_block(__ldg(w.list + i - 1), 64, bad) : KEY_NONE;
+        w.mode = 2;
+        const int r0 = 2 * m, r1 = 2 * m + 1;
+        const int64_t row0 = static_cast<int64_t>(h) * p.list_rows_per_head + r0;
+        w.a = p.lists + row0 * p.list_stride;
+        w.ia = max(__ldg(p.counts + row0), 0) - 1;
+        if (r1 < p.list_rows_per_head) {
+            w.b = p.lists + (row0 + 1) * p.list_stride;
+            w.ib = max(__ldg(p.counts + row0 + 1), 0) - 1;
+        }
+        w.va = w.load(w.a, w.ia);
+        w.vb = w.b ? w.load(w.b, w.ib) : -1;
+        if (w.va < -1 || w.vb < -1) {   // negative entries: treat the list as exhausted
+            w.bad = true;
+            w.va = max(w.va, -1);
+            w.vb = max(w.vb, -1);
+        }
     }
+    return w;
 }
 
 template <bool FP8>
@@ -109,53 +185,42 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;
-    uint8_t* sK = sQ + C::Q_BYTES;
-    uint8_t* sV = sK + C::KST * C::K_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sV + C::VST * C::V_BYTES);
-    // barrier slots
+    uint8_t* sKV = sQ + C::Q_BYTES;                                // stage s: K at s*STAGE, V^T after it
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + C::NST * C::STAGE);
     uint64_t* bQ = bars;
-    uint64_t* bKf = bars + 1;
-    uint64_t* bKe = bKf + C::KST;
-    uint64_t* bVf = bKe + C::KST;
-    uint64_t* bVe = bVf + C::VST;
-    uint64_t* bS = bVe + C::VST;
-    uint64_t* bP = bS + 1;
-    uint64_t* bO = bP + 1;
-    uint64_t* bDrain = bO + 1;
+    uint64_t* bFull = bars + 1;
+    uint64_t* bEmpty = bFull + C::NST;
+    // Barrier phases: a parity wait is only unambiguous while the barrier is at most one phase ahead
+    // of its waiter, so the S and P hand-offs use one barrier per S/P buffer (tile t uses t & 1).
+    uint64_t* bS = bEmpty + C::NST;                                // [2] S(t) ready
+    uint64_t* bP = bS + 2;                                         // [2] P(t) written
+    uint64_t* bO = bP + 2;                                         // one phase per O += P V
+    uint64_t* bOF = bO + 1;                                        // single phase: last O += P V done
+    uint64_t* bDrain = bOF + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bDrain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    // Per-stage tile descriptor written by the producer before it arms the stage's full barrier:
+    // key base of the 64-key tile (KEY_END after the last tile) and the mask of query-row halves
+    // that selected it.  The MMA and softmax warps read it after waiting on that barrier, so only
+    // the producer walks the block lists in global memory.
+    volatile int* tile_kb = const_cast<int*>(reinterpret_cast<volatile int*>(abort_flag + 1));
+    volatile uint32_t* tile_rm = reinterpret_cast<volatile uint32_t*>(tile_kb + C::NST);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m = p.n_tiles - 1 - static_cast<int>(blockIdx.x);     // heavy (late) tiles first
+    const int m = p.n_tiles - 1 - static_cast<int>(blockIdx.x);     // late (heavier) tiles first
     const int h = blockIdx.y;
     const int g = p.H / p.Hk;
     const int hk = h / g;
 
-    Walk w;
-    w.kvb = p.kv_block;
-    if (p.counts) {
-        const int64_t row = static_cast<int64_t>(h) * p.n_tiles + m;
-        w.list = p.lists + row * p.list_stride;
-        w.cnt = max(__ldg(p.counts + row), 0);
-        w.nblk = 0;
-        w.ntiles = p.kv_block == 128 ? w.cnt : (w.cnt + 1) / 2;
-    } else {
-        w.list = nullptr;
-        w.cnt = 0;
-        const int last = p.q_offset + (m + 1) * 128;                 // one past the tile's last position
-        w.nblk = min((last + 127) / 128, (p.kv_len + 127) / 128);
-        w.nblk = max(w.nblk, 0);
-        w.ntiles = w.nblk;
-    }
-    const int T = w.ntiles;
-
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(bQ), 1);
-        for (int i = 0; i < C::KST; ++i) { mbar_init(smem_u32(bKf + i), 1); mbar_init(smem_u32(bKe + i), 1); }
-        for (int i = 0; i < C::VST; ++i) { mbar_init(smem_u32(bVf + i), 1); mbar_init(smem_u32(bVe + i), 1); }
+        for (int i = 0; i < C::NST; ++i) { mbar_init(smem_u32(bFull + i), 1); mbar_init(smem_u32(bEmpty + i), 1); }
         mbar_init(smem_u32(bS), 1);
+        mbar_init(smem_u32(bS + 1), 1);
         mbar_init(smem_u32(bP), 128);
+        mbar_init(smem_u32(bP + 1), 128);
         mbar_init(smem_u32(bO), 1);
+        mbar_init(smem_u32(bOF), 1);
         mbar_init(smem_u32(bDrain), 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -170,89 +235,124 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 4) {
-        // ---------------------------------------------------------------- TMA producer
-        if (lane == 0 && T > 0) {
-            tma_prefetch_desc(&tmQ);
-            tma_prefetch_desc(&tmK);
-            tma_prefetch_desc(&tmV);
-            int kpar[C::KST], vpar[C::VST];
-            bool kused[C::KST], vused[C::VST];
-            for (int i = 0; i < C::KST; ++i) { kpar[i] = 0; kused[i] = false; }
-            for (int i = 0; i < C::VST; ++i) { vpar[i] = 0; vused[i] = false; }
-            bool bad = false;
-            mbar_arrive_expect_tx(smem_u32(bQ), C::Q_BYTES);
-            const int qrow0 = m * 128 - p.q_front;
-            for (int r = 0; r < C::NREG; ++r)
-                tma_load_3d(smem_u32(sQ + r * C::REG_BYTES), &tmQ, smem_u32(bQ), r * C::REG_ELEMS, h, qrow0);
-            for (int t = 0; t < T; ++t) {
-                int kb0, kb1;
-                tile_keys(w, t, kb0, kb1, bad);
-                const int ks = t % C::KST;
-                if (!mbar_wait(smem_u32(bKe + ks), ((t / C::KST) & 1) ^ 1, abort_flag, p.status, SA_DEV_WAIT_KV)) break;
-                uint8_t* kdst = sK + ks * C::K_BYTES;
-                mbar_arrive_expect_tx(smem_u32(bKf + ks), C::K_BYTES);
-                for (int r = 0; r < C::NREG; ++r) {
-                    tma_load_3d(smem_u32(kdst + r * C::REG_BYTES), &tmK, smem_u32(bKf + ks), r * C::REG_ELEMS, hk, kb0);
-                    tma_load_3d(smem_u32(kdst + r * C::REG_BYTES + 64 * 128), &tmK, smem_u32(bKf + ks),
-                                r * C::REG_ELEMS, hk, kb1);
-                }
-                kpar[ks] = (t / C::KST) & 1;
-                kused[ks] = true;
-                const int vs = t % C::VST;
-                if (!mbar_wait(smem_u32(bVe + vs), ((t / C::VST) & 1) ^ 1, abort_flag, p.status, SA_DEV_WAIT_KV)) break;
-                uint8_t* vdst = sV + vs * C::V_BYTES;
-                mbar_arrive_expect_tx(smem_u32(bVf + vs), C::V_BYTES);
-                tma_load_3d(smem_u32(vdst), &tmV, smem_u32(bVf + vs), kb0, 0, hk);
-                tma_load_3d(smem_u32(vdst + C::VCHUNK), &tmV, smem_u32(bVf + vs), kb1, 0, hk);
-                vpar[vs] = (t / C::VST) & 1;
-                vused[vs] = true;
+        // ---------------------------------------------------------------- TMA producer (warp-uniform;
+        // one elected lane issues)
+        {
+            Walker w = make_walker(p, h, m);
+            int kb;
+            uint32_t rm;
+            bool have = w.next(kb, rm);
+            int par[C::NST];
+            bool used[C::NST];
+            for (int i = 0; i < C::NST; ++i) { par[i] = 0; used[i] = false; }
+            if (have && elect_one()) {
+                tma_prefetch_desc(&tmK);
+                tma_prefetch_desc(&tmV);
+                mbar_arrive_expect_tx(smem_u32(bQ), C::Q_BYTES);
+                const int qrow0 = m * 128 - p.q_front;
+                for (int r = 0; r < C::NREG; ++r)
+                    tma_load_3d(smem_u32(sQ + r * C::Q_REG), &tmQ, smem_u32(bQ), r * C::REG_ELEMS, h, qrow0);
             }
+            __syncwarp();
+            for (int t = 0;; ++t, have = w.next(kb, rm)) {
+                const int st = t % C::NST;
+                if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bEmpty + st), ((t / C::NST) & 1) ^ 1, abort_flag,
+                                                        p.status, SA_DEV_WAIT_KV)))
+                    break;
+                if (!have) {                                          // end of the walk
+                    if (elect_one()) {
+                        tile_kb[st] = KEY_END;
+                        mbar_arrive(smem_u32(bFull + st));
+                    }
+                    __syncwarp();
+                    break;
+                }
+                uint8_t* dst = sKV + st * C::STAGE;
+                if (elect_one()) {
+                    tile_kb[st] = kb;
+                    tile_rm[st] = rm;
+                    mbar_arrive_expect_tx(smem_u32(bFull + st), C::STAGE);
+                    for (int r = 0; r < C::NREG; ++r)
+                        tma_load_3d(smem_u32(dst + r * C::K_REG), &tmK, smem_u32(bFull + st), r * C::REG_ELEMS, hk, kb);
+                    tma_load_3d(smem_u32(dst + C::K_BYTES), &tmV, smem_u32(bFull + st), kb, 0, hk);
+                }
+                __syncwarp();
+                par[st] = (t / C::NST) & 1;
+                used[st] = true;
+            }
+            if (w.bad && lane == 0 && p.status) atomicOr(p.status, SA_DEV_BAD_LIST);
             if (*abort_flag) {
                 // let the copies already issued land before the CTA can exit
                 mbar_drain(smem_u32(bQ), 0);
-                for (int i = 0; i < C::KST; ++i)
-                    if (kused[i]) mbar_drain(smem_u32(bKf + i), kpar[i]);
-                for (int i = 0; i < C::VST; ++i)
-                    if (vused[i]) mbar_drain(smem_u32(bVf + i), vpar[i]);
+                for (int i = 0; i < C::NST; ++i)
+                    if (used[i]) mbar_drain(smem_u32(bFull + i), par[i]);
             }
         }
         __syncwarp();
     } else if (warp == 5) {
-        // ---------------------------------------------------------------- MMA issuer
-        if (lane == 0 && T > 0) {
-            const uint32_t tS = tmem + C::S_COL, tO = tmem + C::O_COL;
+        // ---------------------------------------------------------------- MMA issuer (warp-uniform;
+        // one elected lane issues each tcgen05.mma / commit)
+        {
             const uint32_t q_base = smem_u32(sQ);
-            bool ok = mbar_wait(smem_u32(bQ), 0, abort_flag, p.status, SA_DEV_WAIT_Q);
-            for (int t = 0; ok && t < T; ++t) {
-                const int ks = t % C::KST;
-                if (!mbar_wait(smem_u32(bKf + ks), (t / C::KST) & 1, abort_flag, p.status, SA_DEV_WAIT_KV)) break;
+            bool ok = true, q_ready = false;
+            int t = 0;
+            // S(t) = Q K_t^T into S buffer t&1, then O += P(t-1) V_{t-1}: QK of the next tile runs
+            // on the tensor cores while the softmax warps work on the current one.
+            auto issue_pv = [&](int u) -> bool {
+                if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bP + (u & 1)), (u >> 1) & 1, abort_flag, p.status,
+                                                        SA_DEV_WAIT_P)))
+                    return false;
                 tc_fence_after();
-                const uint32_t k_base = smem_u32(sK + ks * C::K_BYTES);
+                const int su = u % C::NST;
+                const uint32_t v_base = smem_u32(sKV + su * C::STAGE + C::K_BYTES);
+                const uint32_t a_tm = tmem + C::S_COL0 + (u & 1) * C::BN;
+                if (elect_one()) {
 #pragma unroll
-                for (int s = 0; s < C::QK_STEPS; ++s) {
-                    const uint32_t off = (s / 4) * C::REG_BYTES + (s % 4) * 32;
-                    mma_ss<FP8>(tS, smem_desc_kmajor(q_base + off, 128), smem_desc_kmajor(k_base + off, 128), C::IDESC,
-                                s > 0 ? 1u : 0u);
+                    for (int s = 0; s < C::PV_STEPS; ++s)
+                        mma_ts<FP8>(tmem + C::O_COL, a_tm + s * 8, smem_desc_kmajor(v_base + s * 32, C::VROW),
+                                    C::IDESC_PV, (u > 0 || s > 0) ? 1u : 0u);
+                    tc_commit(smem_u32(bEmpty + su));
+                    tc_commit(smem_u32(bO));
                 }
-                tc_commit(smem_u32(bS));
-                tc_commit(smem_u32(bKe + ks));
-                if (!mbar_wait(smem_u32(bP), t & 1, abort_flag, p.status, SA_DEV_WAIT_P)) break;
-                const int vs = t % C::VST;
-                if (!mbar_wait(smem_u32(bVf + vs), (t / C::VST) & 1, abort_flag, p.status, SA_DEV_WAIT_KV)) break;
+                __syncwarp();
+                return true;
+            };
+            for (;; ++t) {
+                const int st = t % C::NST;
+                if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bFull + st), (t / C::NST) & 1, abort_flag, p.status,
+                                                        SA_DEV_WAIT_KV))) {
+                    ok = false;
+                    break;
+                }
+                if (tile_kb[st] == KEY_END) break;
+                if (!q_ready) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bQ), 0, abort_flag, p.status, SA_DEV_WAIT_Q))) {
+                        ok = false;
+                        break;
+                    }
+                    q_ready = true;
+                }
                 tc_fence_after();
-                const uint32_t v_base = smem_u32(sV + vs * C::V_BYTES);
-                constexpr int STEPS_PER_CHUNK = 64 / C::UK;
+                const uint32_t k_base = smem_u32(sKV + st * C::STAGE);
+                if (elect_one()) {
 #pragma unroll
-                for (int s = 0; s < C::PV_STEPS; ++s) {
-                    const uint32_t off = (s / STEPS_PER_CHUNK) * C::VCHUNK + (s % STEPS_PER_CHUNK) * 32;
-                    mma_ts<FP8>(tO, tS + s * 8, smem_desc_kmajor(v_base + off, C::VROW), C::IDESC,
-                                (t > 0 || s > 0) ? 1u : 0u);
+                    for (int s = 0; s < C::QK_STEPS; ++s) {
+                        const uint32_t qoff = (s / 4) * C::Q_REG + (s % 4) * 32;
+                        const uint32_t koff = (s / 4) * C::K_REG + (s % 4) * 32;
+                        mma_ss<FP8>(tmem + C::S_COL0 + (t & 1) * C::BN, smem_desc_kmajor(q_base + qoff, 128),
+                                    smem_desc_kmajor(k_base + koff, 128), C::IDESC_QK, s > 0 ? 1u : 0u);
+                    }
+                    tc_commit(smem_u32(bS + (t & 1)));
                 }
-                tc_commit(smem_u32(bVe + vs));
+                __syncwarp();
+                if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
             }
-            tc_commit(smem_u32(bO));
+            if (ok && t >= 1) ok = issue_pv(t - 1);
+            if (ok && t >= 1 && elect_one()) tc_commit(smem_u32(bOF));
+            __syncwarp();
             if (*abort_flag) {
-                tc_commit(smem_u32(bDrain));
+                if (elect_one()) tc_commit(smem_u32(bDrain));
+                __syncwarp();
                 mbar_drain(smem_u32(bDrain), 0);
             }
         }
@@ -261,10 +361,11 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         // ---------------------------------------------------------------- softmax + epilogue (warps 0-3)
         const int r = threadIdx.x;                                   // query row within the tile
         const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-        const uint32_t tS = tmem + lane_off + C::S_COL;
         const uint32_t tO = tmem + lane_off + C::O_COL;
         const int qpos = p.q_offset + m * 128 + r;
         const int qpos_min = p.q_offset + m * 128;
+        const int vis = min(qpos, p.kv_len - 1);                     // visible keys: position <= vis
+        const uint32_t my_half = r >= 64 ? 2u : 1u;
         float sl2, out_scale;
         if constexpr (FP8) {
             sl2 = p.softmax_scale * __ldg(p.q_scale + h * p.qss) * __ldg(p.k_scale + hk * p.kss) * LOG2E;
@@ -275,93 +376,116 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         }
         const float pbias = FP8 ? LOG2_448 : 0.f;
         float m_run = -INFINITY, l_run = 0.f;
-        bool ok = true, bad = false;
-        for (int t = 0; t < T; ++t) {
-            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bS), t & 1, abort_flag, p.status, SA_DEV_WAIT_S));
+        bool ok = true;
+        int t = 0;
+        for (;; ++t) {
+            const int st = t % C::NST;
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bFull + st), (t / C::NST) & 1, abort_flag, p.status,
+                                                   SA_DEV_WAIT_KV));
+            if (!ok) break;
+            const int kb = tile_kb[st];
+            if (kb == KEY_END) break;
+            const uint32_t rm = tile_rm[st];
+            const int b = t & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bS + b), (t >> 1) & 1, abort_flag, p.status, SA_DEV_WAIT_S));
             if (!ok) break;
             tc_fence_after();
-            float x[128];
+            const uint32_t tS = tmem + lane_off + C::S_COL0 + b * C::BN;
+            float x[64];
             {
-                uint32_t u[128];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
+                uint32_t u[64];
+                tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(u));
+                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 128; ++i) x[i] = __uint_as_float(u[i]);
+                for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(u[i]);
             }
-            int kb0, kb1;
-            tile_keys(w, t, kb0, kb1, bad);
-            const bool need_mask = (max(kb0, kb1) + 63 > qpos_min) || (max(kb0, kb1) + 63 >= p.kv_len);
-            if (need_mask) {
-                const int lim = min(qpos, p.kv_len - 1);            // visible keys: kpos <= lim
+            if (rm != 3u || kb + 63 > qpos_min || kb + 63 >= p.kv_len) {
+                const int lim = (rm & my_half) ? vis - kb : -1;      // visible columns: c <= lim
 #pragma unroll
-                for (int c = 0; c < 128; ++c) {
-                    const int kpos = (c < 64 ? kb0 : kb1 - 64) + c;
-                    if (kpos > lim) x[c] = -INFINITY;
-                }
+                for (int c = 0; c < 64; ++c)
+                    if (c > lim) x[c] = -INFINITY;
             }
-            float mx = x[0];
+            float mx;
+            {
+                float a[8];
 #pragma unroll
-            for (int c = 1; c < 128; ++c) mx = fmaxf(mx, x[c]);
-            const float m_new = fmaxf(m_run, mx * sl2);
+                for (int i = 0; i < 8; ++i) a[i] = fmax3(x[i], x[8 + i], x[16 + i]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], x[24 + i], x[32 + i]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], x[40 + i], x[48 + i]);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) a[i] = fmaxf(a[i], x[56 + i]);
+                mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+            }
+            // running max used for the exponentials; grows (with an O rescale) only past the slack
+            const float cand = mx * sl2;
+            const bool grow = cand > m_run + C::RESCALE_SLACK || m_run == -INFINITY;
+            const float m_new = grow ? fmaxf(m_run, cand) : m_run;
             const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
             const float alpha = ex2_approx(m_run - m_use);
-            const float bias = pbias - m_use;
-            float rs = 0.f;
+            const float2 sl2v = make_float2(sl2, sl2), biasv = make_float2(pbias - m_use, pbias - m_use);
+            float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                             make_float2(0.f, 0.f)};
+            auto exp_pair = [&](int c) -> float2 {
+                const float2 e = ffma2(make_float2(x[c], x[c + 1]), sl2v, biasv);
+                const float2 pr = make_float2(ex2_approx(e.x), ex2_approx(e.y));
+                acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pr);
+                return pr;
+            };
             if constexpr (FP8) {
-                // 32 keys -> 8 columns of 4 e4m3 values (key 4c+i in byte i of column c)
+                // 64 keys -> 16 columns of 4 e4m3 values (key 4c+i in byte i of column c)
+                uint32_t pk[16];
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
-                    uint32_t pk[8];
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const float* xc = x + ch * 32 + 4 * c;
-                        const float p0 = ex2_approx(fmaf(xc[0], sl2, bias));
-                        const float p1 = ex2_approx(fmaf(xc[1], sl2, bias));
-                        const float p2 = ex2_approx(fmaf(xc[2], sl2, bias));
-                        const float p3 = ex2_approx(fmaf(xc[3], sl2, bias));
-                        rs += (p0 + p1) + (p2 + p3);
-                        pk[c] = static_cast<uint32_t>(pack_e4m3x2(p0, p1)) |
-                                (static_cast<uint32_t>(pack_e4m3x2(p2, p3)) << 16);
-                    }
-                    tmem_st8(tS + ch * 8, pk);
+                for (int c = 0; c < 16; ++c) {
+                    const float2 p01 = exp_pair(4 * c);
+                    const float2 p23 = exp_pair(4 * c + 2);
+                    pk[c] = static_cast<uint32_t>(pack_e4m3x2(p01.x, p01.y)) |
+                            (static_cast<uint32_t>(pack_e4m3x2(p23.x, p23.y)) << 16);
                 }
+                tmem_st16(tS, pk);
             } else {
-                // 32 keys -> 16 columns of 2 bf16 values (key 2c+i in half i of column c)
+                // 64 keys -> 32 columns of 2 bf16 values (key 2c+i in half i of column c)
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {
+                for (int hh = 0; hh < 2; ++hh) {
                     uint32_t pk[16];
 #pragma unroll
                     for (int c = 0; c < 16; ++c) {
-                        const float p0 = ex2_approx(fmaf(x[ch * 32 + 2 * c], sl2, bias));
-                        const float p1 = ex2_approx(fmaf(x[ch * 32 + 2 * c + 1], sl2, bias));
-                        rs += p0 + p1;
-                        pk[c] = pack_bf16x2(p0, p1);
+                        const float2 pr = exp_pair(32 * hh + 2 * c);
+                        pk[c] = pack_bf16x2(pr.x, pr.y);
                     }
-                    tmem_st16(tS + ch * 16, pk);
+                    tmem_st16(tS + 16 * hh, pk);
                 }
             }
-            l_run = l_run * alpha + rs;
+            const float2 s01 = fadd2(acc[0], acc[1]), s23 = fadd2(acc[2], acc[3]);
+            l_run = l_run * alpha + ((s01.x + s01.y) + (s23.x + s23.y));
             m_run = m_new;
-            if (t > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {     // O rescale (PV of tile t-1 is complete)
-#pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t u[32];
-                    tmem_ld32(tO + c * 32, u);
-                    tmem_wait_ld();
+            if (t > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
+                // O rescale: wait until O += P(t-1) V_{t-1} has completed, then scale in TMEM.  S(t)
+                // being complete implies O += P(t-2) V_{t-2} is, so the barrier is at most one phase
+                // behind and the parity wait is unambiguous.
+                ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bO), (t - 1) & 1, abort_flag, p.status, SA_DEV_WAIT_O));
+                if (!ok) break;
+                tc_fence_after();
+                uint32_t u[128];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-                    tmem_st32(tO + c * 32, u);
-                }
+                for (int c = 0; c < 4; ++c) tmem_ld32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 128; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tmem_st32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(smem_u32(bP));
+            mbar_arrive(smem_u32(bP + b));
         }
-        if (bad && r == 0 && p.status) atomicOr(p.status, SA_DEV_BAD_LIST);
+        const int T = t;
         // ---------------------------------------------------------------- epilogue
+        // (the per-PV barrier cannot be used here: the MMA warp may still be two PVs behind)
         const bool have_o = __all_sync(0xffffffffu, ok && T > 0 &&
-                                       mbar_wait(smem_u32(bO), 0, abort_flag, p.status, SA_DEV_WAIT_O));
+                                       mbar_wait(smem_u32(bOF), 0, abort_flag, p.status, SA_DEV_WAIT_O));
         if (have_o) tc_fence_after();
         const float inv = (have_o && l_run > 0.f) ? out_scale / l_run : 0.f;
         const int qrow = m * 128 + r - p.q_front;
@@ -444,7 +568,9 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
         return fail(SA_ERR_ARG, "%s: bad sizes", name);
     if (counts && (!lists || (kv_block != 64 && kv_block != 128) || list_stride < 1))
         return fail(SA_ERR_ARG, "%s: block lists need lists, kv_block 64|128", name);
-    if (counts && q_block != 128) return fail(SA_ERR_UNSUPPORTED, "%s: q_block %d (only 128)", name, q_block);
+    if (counts && q_block != 128 && !(q_block == 64 && kv_block == 64))
+        return fail(SA_ERR_UNSUPPORTED, "%s: q_block %d with kv_block %d (q_block 128, or 64 with kv_block 64)",
+                    name, q_block, kv_block);
     if (!q || !k || !vt || !out) return fail(SA_ERR_ARG, "%s: null pointer", name);
     if (FP8 && (!qsc || !ksc || !vsc)) return fail(SA_ERR_ARG, "%s: null scale pointer", name);
     auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
@@ -458,8 +584,8 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     int rc;
     const CUtensorMapSwizzle sw128 = CU_TENSOR_MAP_SWIZZLE_128B;
     if ((rc = encode3d(&tmQ, FP8, q, D, H, n_q > 0 ? n_q : 1, qhs * E, qrs * E, C::REG_ELEMS, 1, 128, sw128, "q"))) return rc;
-    if ((rc = encode3d(&tmK, FP8, k, D, Hk, kv_len, khs * E, krs * E, C::REG_ELEMS, 1, 64, sw128, "k"))) return rc;
-    if ((rc = encode3d(&tmV, FP8, vt, kv_len, D, Hk, vtds * E, vths * E, 64, 128, 1,
+    if ((rc = encode3d(&tmK, FP8, k, D, Hk, kv_len, khs * E, krs * E, C::REG_ELEMS, 1, C::BN, sw128, "k"))) return rc;
+    if ((rc = encode3d(&tmV, FP8, vt, kv_len, D, Hk, vtds * E, vths * E, C::BN, 128, 1,
                        FP8 ? CU_TENSOR_MAP_SWIZZLE_64B : sw128, "v^T")))
         return rc;
     Params p;
@@ -476,7 +602,9 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     p.q_front = q_front;
     p.q_offset = q_offset;
     p.n_tiles = n_tiles;
-    p.kv_block = counts ? kv_block : 128;
+    p.kv_block = counts ? kv_block : 64;
+    p.q_block = counts ? q_block : 128;
+    p.list_rows_per_head = counts ? (q_front + n_q + p.q_block - 1) / p.q_block : 0;
     p.q_scale = qsc;
     p.k_scale = ksc;
     p.v_scale = vsc;

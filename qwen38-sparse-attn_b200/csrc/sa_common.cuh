@@ -33,6 +33,18 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// One lane of a converged warp (elect.sync): tcgen05.mma / commit / TMA issue is predicated on it
+// while the surrounding address and descriptor arithmetic stays warp-uniform.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\t"
+        "elect.sync r|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -62,6 +74,48 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x on the FMA pipe (Cody-Waite range reduction + minimax polynomial), so a share of the
+// softmax exponentials can bypass the MUFU unit.  x = n + f with n = rint(x) taken from the low
+// mantissa bits of x + 1.5*2^23, f in [-0.5, 0.5]; 2^f ~ c0 + f(c1 + f(c2 + f c3)) with
+// coefficients from a Lawson (iteratively reweighted least squares) minimax fit of the relative
+// error on [-0.5, 0.5] (max rel. error 7.5e-5); 2^n is added to the exponent field.  x is clamped
+// at -120, below which the result (< 2^-119) is irrelevant next to the row maximum's term of ~1.
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -120.f);
+    const float magic = 12582912.f;            // 1.5 * 2^23
+    const float y = x + magic;
+    const float f = x - (y - magic);
+    float p = fmaf(0.0551716685f, f, 0.242611125f);
+    p = fmaf(p, f, 0.693260968f);
+    p = fmaf(p, f, 0.999928057f);
+    return __int_as_float(__float_as_int(p) + __float_as_int(y) * 8388608);
+}
+
+// Packed fp32x2 arithmetic (one instruction for two lanes' worth of work on sm_100).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 // ------------------------------------------------------------------------------------------

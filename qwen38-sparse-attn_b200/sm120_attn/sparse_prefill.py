@@ -54,6 +54,16 @@ class SparsePrefill:
         self.stats = {'calls': 0, 'blocks_total': 0, 'blocks_kept': 0, 'plan_ms': 0.0, 'run_ms': 0.0, 'select_ms': 0.0}
         self._kept_acc = None
         self.timing = False
+        # Optional list: when set, every forward appends (start, end) CUDA events recorded on the
+        # launching stream around the attention kernel (profiling without host syncs).
+        self.kernel_events = None
+
+    def _attn_events(self):
+        if self.kernel_events is None:
+            return None, None
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self.kernel_events.append((s, e))
+        return s, e
 
     def eligible(self, q_len: int, kv_len: int) -> bool:
         return q_len >= self.min_q and kv_len >= self.min_kv
@@ -157,7 +167,12 @@ class SparsePrefill:
         vt = torch.empty(self.Hk, self.D, rows_pad, dtype=torch.bfloat16, device=dev)
         ops.transpose_bf16(v[:kv_len], vt, rows_pad)
         o, copy_back = self._out(out, n, dev)
+        ev0, ev1 = self._attn_events()
+        if ev0 is not None:
+            ev0.record()
         ops.attn_bf16(q, k[:kv_len], vt, o, kv_len, front, qs, counts, lists, B, self.scale, q_block=B)
+        if ev1 is not None:
+            ev1.record()
         t2 = self._tick()
         if self.timing:
             self.stats['select_ms'] += t1 - t0
@@ -214,7 +229,13 @@ class SparsePrefill:
         t1 = self._tick()
         o, copy_back = self._out(out, n, dev)
         sc = torch.tensor([sq, sk, sv], dtype=torch.float32).to(dev, non_blocking=True)
+        ev0, ev1 = self._attn_events()
+        if ev0 is not None:
+            ev0.record()
         ops.attn_fp8(q8, k8, vt8, o, kv_len, front, qs, counts, lists, B, sc[0:1], sc[1:2], sc[2:3], self.scale)
+        if ev1 is not None:
+            ev1.record()
+        self.last_counts = counts
         t2 = self._tick()
         if self.timing:
             self.stats['select_ms'] += t1 - t0

@@ -215,7 +215,7 @@ def _deq(bits, s):
 def test_attn_fp8_dense(n, kv, H, Hk, per_head):
     _, (q8, k8, v8), scales = _fp8_case(n, kv, H, Hk, seed=n + kv, per_head=per_head)
     out = _run_fp8(q8, k8, v8, scales, kv, 0, kv - n)
-    model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, kv - n, q_block=128, kv_block=128)
+    model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, kv - n, q_block=128, kv_block=64)
     ref = O.attention_ref(_deq(q8, scales[0]), _deq(k8, scales[1]), _deq(v8, scales[2]), kv - n)
     assert rel_l2(out, model) < 1e-2, rel_l2(out, model)
     assert rel_l2(out, ref) < 3e-2, rel_l2(out, ref)
@@ -285,3 +285,59 @@ def test_attn_bf16_sparse(kv_block):
     out = _run_bf16(q, k, v, kv, q_front, q_offset, counts, lists, kv_block)
     ref = O.attention_ref(f32(q), f32(k), f32(v), q_pos0, masks, q_block=128, kv_block=kv_block, q_front=q_front)
     assert np.abs(out - ref).max() < 2e-2
+
+
+def _random_row_masks(H, n_rows_blocks, NB, q_pos_block0, q_block, kv_block, density, seed):
+    """Per-head masks over q_block-row query blocks: random blocks plus the sink and diagonal blocks."""
+    rng = np.random.default_rng(seed)
+    m = rng.random((H, n_rows_blocks, NB)) < density
+    for t in range(n_rows_blocks):
+        lo = q_pos_block0 + t * q_block
+        hi = lo + q_block - 1
+        for b in range(NB):
+            if b * kv_block > hi:
+                m[:, t, b] = False
+            elif (b + 1) * kv_block - 1 >= lo:
+                m[:, t, b] = True
+        m[:, t, 0] = True
+    return m
+
+
+@pytest.mark.parametrize('n,kv,q_front', [(700, 4000, 30), (1000, 3000, 0), (64, 2048, 17)])
+def test_attn_bf16_sparse_64row_lists(n, kv, q_front):
+    """Two 64-row block lists per 128-row tile (the BF16 path with BLOCK=64, kai_fa_bf16.py lists)."""
+    H, Hk = 8, 2
+    q, k, v, _ = synth.make_qkv(n, kv, H, Hk, 128, seed=n + kv)
+    q_pos0 = kv - n
+    q_offset = q_pos0 - q_front
+    nb64 = -(-(q_front + n) // 64)
+    NB = -(-kv // 64)
+    masks = _random_row_masks(H, nb64, NB, q_offset, 64, 64, 0.3, seed=n)
+    counts, lists = _lists_from_masks(masks)
+    ops = _ops()
+    rows_pad = -(-kv // 128) * 128
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    vt = torch.empty(Hk, 128, rows_pad, dtype=torch.bfloat16, device=DEV)
+    ops.transpose_bf16(vd, vt, rows_pad)
+    out = torch.full((n, H, 128), float('nan'), dtype=torch.bfloat16, device=DEV)
+    ops.attn_bf16(qd, kd, vt, out, kv, q_front, q_offset, counts, lists, 64, 128 ** -0.5, q_block=64)
+    ops.check_status(DEV)
+    ref = O.attention_ref(f32(q), f32(k), f32(v), q_pos0, masks, q_block=64, kv_block=64, q_front=q_front)
+    assert np.abs(f32(out) - ref).max() < 2e-2
+
+
+def test_attn_fp8_list_with_future_padding_block():
+    """A list entry past kv_len (the FP8 driver's padded diagonal block) contributes nothing."""
+    H, Hk, n, kv = 2, 1, 200, 1000
+    _, (q8, k8, v8), scales = _fp8_case(n, kv, H, Hk, seed=3)
+    q_pos0 = kv - n
+    front = q_pos0 % 128
+    q_offset = q_pos0 - front
+    n_tiles = -(-(front + n) // 128)
+    NB = -(-(q_offset + n_tiles * 128) // 64)              # covers the padded query range
+    masks = _random_tile_masks(H, n_tiles, NB, q_offset, 64, 0.4, seed=2)
+    counts, lists = _lists_from_masks(masks)
+    out = _run_fp8(q8, k8, v8, scales, kv, front, q_offset, counts, lists, 64)
+    ref = O.attention_ref(_deq(q8, scales[0]), _deq(k8, scales[1]), _deq(v8, scales[2]), q_pos0, masks,
+                          q_block=128, kv_block=64, q_front=front)
+    assert rel_l2(out, ref) < 3e-2
