@@ -137,13 +137,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
 }
 
+#ifndef SA_WAIT_SUSPEND_NS
+#define SA_WAIT_SUSPEND_NS 1000000u   // try_wait suspend-time hint: a waiting warp sleeps (up to 1 ms)
+#endif                                // until the phase completes instead of re-issuing polls
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+        : "=r"(ok) : "r"(bar), "r"(parity), "r"(SA_WAIT_SUSPEND_NS) : "memory");
     return ok != 0;
 }
 
@@ -156,7 +160,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63u) == 0) {
+        if ((i & 7u) == 0) {
             if (*abort_flag) return false;
             if (globaltimer() - t0 > SA_WAIT_TIMEOUT_NS) {
                 *abort_flag = 1;

@@ -1,0 +1,189 @@
+"""Host-side logic of the drop-in `sm120_attn.sparse_prefill` on CPU: knobs, eligibility gates, and the
+bookkeeping of the block-mean and scale caches (sparse_prefill.py:358-469, :472-499).
+
+The CUDA entry points are replaced, inside these tests only, by oracle-backed fakes that write into CPU
+tensors; the product itself has no CPU path.
+"""
+from __future__ import annotations
+
+import json
+import types
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+import synth
+
+
+@pytest.fixture
+def ksp(monkeypatch):
+    import sm120_attn.sparse_prefill as m
+    from sm120_attn import ops
+
+    def fake_block_means(x, pos0, block, out, out_block0, q8=None, inv_scale=None, fixed_divisor=0):
+        b0, means = O.block_means(x.float().numpy(), pos0, block)
+        if fixed_divisor:
+            n = x.shape[0]
+            for i in range(means.shape[1]):
+                b = b0 + i
+                rows = min(pos0 + n, (b + 1) * block) - max(pos0, b * block)
+                means[:, i] *= np.float32(rows) / np.float32(fixed_divisor)
+        out[:, b0 - out_block0:b0 - out_block0 + means.shape[1]] = torch.from_numpy(means)
+
+    def fake_absmax(x, per_head, out=None):
+        a = x.float().abs()
+        return a.amax(dim=(0, 2)) if per_head else a.amax().reshape(1)
+
+    monkeypatch.setattr(ops, 'block_means', fake_block_means)
+    monkeypatch.setattr(ops, 'absmax', fake_absmax)
+    m._KMEAN_CACHE.clear()
+    m._SCALE_CACHE.clear()
+    old_block = m.BLOCK
+    yield m
+    m.BLOCK = old_block
+    m._KMEAN_CACHE.clear()
+    m._SCALE_CACHE.clear()
+
+
+def test_config_env_and_json(monkeypatch, tmp_path, capsys):
+    import sm120_attn.sparse_prefill as m
+    cfg = tmp_path / 'cfg.json'
+    cfg.write_text(json.dumps({'tau': 0.9, 'min_kv': 4096, 'kernel': 'sm120', 'enabled': 'false'}))
+    monkeypatch.setenv('SM120_SPARSE_CONFIG', str(cfg))
+    monkeypatch.setenv('SM120_SPARSE_TAU', '0.85')
+    for k in ('SM120_SPARSE_ATTN', 'SM120_SPARSE_MIN_KV', 'SM120_SPARSE_MIN_Q', 'SM120_SPARSE_KERNEL',
+              'SM120_SPARSE_FP8_PIPELINE'):
+        monkeypatch.delenv(k, raising=False)
+    monkeypatch.setattr(m, '_CONFIG', None)
+    c = m.config()
+    assert c == {'enabled': False, 'tau': 0.85, 'min_kv': 4096, 'min_q': 1024, 'kernel': 'sm120', 'fp8_pipeline': 'tma'}
+    assert 'config' in capsys.readouterr().out
+    assert m.config() is c                                           # cached
+    monkeypatch.setattr(m, '_CONFIG', None)
+    monkeypatch.delenv('SM120_SPARSE_CONFIG')
+    monkeypatch.delenv('SM120_SPARSE_TAU')
+    c = m.config()
+    assert c['enabled'] is True and c['tau'] == 0.95 and c['min_kv'] == 8192 and c['kernel'] == 'sm120fp8'
+    monkeypatch.setattr(m, '_CONFIG', None)
+
+
+def test_kernel_knob_validation():
+    import sm120_attn.sparse_prefill as m
+    assert m.SparsePrefill(8, 2, 128, 'cpu', kernel='fp8').kernel == 'sm120fp8'
+    assert m.SparsePrefill(8, 2, 128, 'cpu', kernel='bf16').kernel == 'sm120'
+    with pytest.raises(ValueError):
+        m.SparsePrefill(8, 2, 128, 'cpu', kernel='flashinfer')
+    with pytest.raises(ValueError):
+        m.SparsePrefill(8, 2, 128, 'cpu', fp8_pipeline='other')
+    sp = m.SparsePrefill(8, 2, 128, 'cpu', min_kv=100, min_q=10)
+    assert sp.eligible(10, 100) and not sp.eligible(9, 100) and not sp.eligible(10, 99)
+    assert sp.kept_fraction() is None
+    assert sp.stats == {'calls': 0, 'blocks_total': 0, 'blocks_kept': 0, 'plan_ms': 0.0, 'run_ms': 0.0, 'select_ms': 0.0}
+
+
+def _meta(qlens, kvlens, page=16, causal=True):
+    qsl = np.concatenate([[0], np.cumsum(qlens)]).astype(np.int32)
+    npages = [-(-k // page) for k in kvlens]
+    bt = torch.zeros(len(qlens), max(npages), dtype=torch.int32)
+    nxt = 0
+    for r, p in enumerate(npages):
+        bt[r, :p] = torch.arange(nxt, nxt + p)
+        nxt += p
+    return types.SimpleNamespace(causal=causal, max_query_len=int(max(qlens)), max_seq_len=int(max(kvlens)),
+                                 query_start_loc=torch.from_numpy(qsl), seq_lens=torch.tensor(kvlens, dtype=torch.int32),
+                                 block_table=bt)
+
+
+@pytest.mark.parametrize('case', ['disabled', 'noncausal', 'window', 'short_q', 'short_kv', 'no_eligible'])
+def test_try_sparse_forward_gates(monkeypatch, case):
+    import sm120_attn.sparse_prefill as m
+    monkeypatch.setattr(m, '_CONFIG', {'enabled': case != 'disabled', 'tau': 0.95, 'min_kv': 8192, 'min_q': 1024,
+                                       'kernel': 'sm120fp8', 'fp8_pipeline': 'tma'})
+    monkeypatch.setattr(torch.cuda, 'is_current_stream_capturing', lambda: False)
+    impl = types.SimpleNamespace(sliding_window=(-1, -1) if case != 'window' else (128, 0), scale=0.1)
+    if case == 'short_q':
+        meta = _meta([512], [16384])
+    elif case == 'short_kv':
+        meta = _meta([2048], [4096])
+    elif case == 'no_eligible':
+        meta = _meta([2048, 1], [4096, 20000])           # max lengths pass, no single request qualifies
+    else:
+        meta = _meta([2048], [16384], causal=(case != 'noncausal'))
+    q = torch.zeros(int(meta.query_start_loc[-1]), 8, 128)
+    assert m.try_sparse_forward(impl, q, q, None, None, q, meta) is False
+
+
+def test_cached_block_means_bookkeeping(ksp):
+    B = 64
+    ksp.BLOCK = B
+    _, k, _, _ = synth.make_qkv(16, 3000, 8, 2, 128, block=B, seed=3, with_v=False)
+    kc = O.KMeanCacheOracle(B)
+    for q_start, n in ((0, 1000), (1000, 1500), (2500, 500)):
+        km = ksp._cached_block_means('L', 5, k[q_start:q_start + n], q_start, q_start + n)
+        ref = kc.update('L', 5, k[q_start:q_start + n].float().numpy(), q_start, q_start + n)
+        np.testing.assert_allclose(km.numpy(), ref, rtol=1e-6, atol=1e-7)
+        assert ksp._KMEAN_CACHE[('L', 5)]['last_kv'] == q_start + n
+    # discontinuity without history -> RuntimeError; with history -> rebuild
+    with pytest.raises(RuntimeError):
+        ksp._cached_block_means('L', 5, k[100:200], 100, 200)
+    km = ksp._cached_block_means('L', 6, k[1000:2000], 1000, 2000, key_all=k[:2000])
+    ref = O.KMeanCacheOracle(B).update('L', 6, k[1000:2000].float().numpy(), 1000, 2000, key_all=k[:2000].float().numpy())
+    np.testing.assert_allclose(km.numpy(), ref, rtol=1e-6, atol=1e-7)
+
+
+def test_cached_block_means_eviction_and_growth(ksp):
+    ksp.BLOCK = 64
+    _, k, _, _ = synth.make_qkv(16, 256, 8, 2, 128, seed=4, with_v=False)
+    for page in range(ksp._KMEAN_MAX_ENTRIES + 3):
+        ksp._cached_block_means('E', page, k[:64], 0, 64)
+    assert len(ksp._KMEAN_CACHE) == ksp._KMEAN_MAX_ENTRIES
+    assert ('E', 0) not in ksp._KMEAN_CACHE and ('E', 2) not in ksp._KMEAN_CACHE and ('E', 3) in ksp._KMEAN_CACHE
+    e = ksp._KMEAN_CACHE[('E', 3)]
+    cap = e['km'].shape[1]
+    e['last_kv'] = cap * 64                                          # pretend the request reached the capacity
+    e['nb'] = cap
+    ksp._cached_block_means('E', 3, k[:128], cap * 64, cap * 64 + 128)
+    assert ksp._KMEAN_CACHE[('E', 3)]['km'].shape[1] == 2 * cap
+
+
+def test_cached_scales_bookkeeping(ksp):
+    q, k, v, _ = synth.make_qkv(512, 2048, 8, 2, 128, block=64, seed=31)
+    sc = O.ScaleCacheOracle()
+    s0 = ksp._cached_scales('L', 3, q, k[:1536], v[:1536], 1024)
+    s1 = ksp._cached_scales('L', 3, q, k[:2048], v[:2048] * 2, 1536)      # continuity: reused
+    s2 = ksp._cached_scales('L', 3, q * 4, k, v, 1000)                     # discontinuity: fresh
+    r0 = sc.update('L', 3, q.float().numpy(), k[:1536].float().numpy(), v[:1536].float().numpy(), 1024)
+    r1 = sc.update('L', 3, q.float().numpy(), k[:2048].float().numpy(), (v[:2048] * 2).float().numpy(), 1536)
+    r2 = sc.update('L', 3, (q * 4).float().numpy(), k.float().numpy(), v.float().numpy(), 1000)
+    np.testing.assert_allclose(np.array([s0, s1, s2]), np.array([r0, r1, r2]), rtol=1e-12)
+    assert s0 == s1 and s2 != s1
+    assert ksp._SCALE_CACHE[('L', 3)]['last_kv'] == 1000 + 512
+
+
+def test_block_masks_rejects_unpadded_input(ksp):
+    sp = ksp.SparsePrefill(8, 2, 128, 'cpu')
+    ksp.BLOCK = 64
+    with pytest.raises(AssertionError):
+        sp.block_masks(torch.zeros(100, 8, 128, dtype=torch.bfloat16), None, 64,
+                       km=torch.zeros(2, 4, 128))
+
+
+def test_reference_helper_matches_oracle():
+    """`sparse_prefill.reference` (head-major K, per-KV-head masks) against the oracle."""
+    import sm120_attn.sparse_prefill as m
+    old = m.BLOCK
+    m.BLOCK = 64
+    try:
+        q, k, v, _ = synth.make_qkv(100, 300, 4, 2, 128, seed=8)
+        masks = torch.ones(2, 2, 5, dtype=torch.bool)
+        masks[:, :, 1] = False
+        out = m.reference(q, k.transpose(0, 1), v.transpose(0, 1), 200, masks)
+        hm = masks.numpy().repeat(2, 0)
+        # the reference expands masks over rows starting at row 0 of q (no front padding)
+        ref = O.attention_ref(q.float().numpy(), k.float().numpy(), v.float().numpy(), 200, hm, q_block=64,
+                              kv_block=64)
+        np.testing.assert_allclose(out.numpy(), ref, rtol=1e-4, atol=2e-5)
+    finally:
+        m.BLOCK = old
