@@ -43,9 +43,9 @@ Q_START = KV - N_Q
 # Kernels of this package launched per step: K-chunk block means, Q block means + e4m3, selection,
 # K e4m3, V^T e4m3, attention.
 LAUNCHES_PER_STEP = 6
-# DRAM bytes of the attention kernel per launch from the ncu capture summarised in
-# profiles/attn_fwd_fp8_sparse_prefill.md (None until captured).
-ATTN_DRAM_BYTES = None
+# DRAM bytes (read + write) of one attention launch of this workload, from the ncu capture summarised
+# in profiles/attn_fwd_fp8_sparse_prefill.md (213.8 MB read + 106.4 MB written).
+ATTN_DRAM_BYTES = 320225280
 
 
 def peaks():
@@ -158,14 +158,15 @@ def run_b200(args):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    # ---------------- device-resident timed region
+    # ---------------- device-resident timed region (clocks sampled from warm-up through the e2e run,
+    # since one timed region is shorter than a few nvidia-smi sampling periods)
+    clocks = Clocks(local)
+    clocks.start()
     for _ in range(args.warmup):
         rewind()
         step(q, k[Q_START:])
     sp.kernel_events = []
-    clocks = Clocks(local)
     barrier()
-    clocks.start()
     stream = torch.cuda.current_stream(dev)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if args.profile_range:
@@ -178,7 +179,6 @@ def run_b200(args):
     barrier()
     if args.profile_range:
         torch.cuda.profiler.stop()
-    clk = clocks.stop()
     ms_total = t0.elapsed_time(t1)
     attn_ms = [s.elapsed_time(e) for s, e in sp.kernel_events]
     sp.kernel_events = None
@@ -212,6 +212,7 @@ def run_b200(args):
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
     h2d = q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2
     d2h = o_h.numel() * 2
     ops.check_status(dev)
@@ -349,7 +350,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=10)
+    ap.add_argument('--steps', type=int, default=20)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
     ap.add_argument('--scaling', default='weak', choices=['weak', 'strong'])
