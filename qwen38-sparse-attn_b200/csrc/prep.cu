@@ -218,15 +218,18 @@ extern "C" int sa_block_means_bf16(const void* x, int64_t x_row_stride, int64_t 
     const int b0 = pos0 / block;
     const int b1 = (pos0 + n + block - 1) / block;
     if (b0 < out_block0) return fail(SA_ERR_ARG, "sa_block_means_bf16: first block %d < out_block0 %d", b0, out_block0);
+    // Launch shape: enough CTAs for >= 4 per SM and ~2048 threads per SM of independent 16-byte row
+    // streams.  Fewer heads per CTA first (more CTAs), then row groups (more loads in flight per block).
     const int cols = head_dim / 8;
-    int hpc = std::max(1, 256 / cols);
-    hpc = std::min(hpc, heads);
+    const int nblk = b1 - b0;
+    int hpc = std::min(std::max(1, 256 / cols), heads);
+    while (hpc > 1 && static_cast<long long>(nblk) * ((heads + hpc - 1) / hpc) < 4ll * num_sms()) hpc = (hpc + 1) / 2;
     const int tx = hpc * cols;
     const int nhg = (heads + hpc - 1) / hpc;
-    const long long ctas = static_cast<long long>(b1 - b0) * nhg;
-    const long long target = 2ll * num_sms() * 1024;
+    const long long ctas = static_cast<long long>(nblk) * nhg;
+    const long long target = 2048ll * num_sms();
     int rg = 1;
-    while (rg < 8 && ctas * tx * rg < target && tx * rg * 2 <= 1024 && (rg * 2) <= block) rg *= 2;
+    while (rg < 16 && (ctas * tx * rg < target || tx * rg < 128) && tx * rg * 2 <= 1024 && rg * 2 <= block / 4) rg *= 2;
     dim3 grid(b1 - b0, nhg), blk(tx, rg);
     const size_t smem = rg > 1 ? static_cast<size_t>(rg - 1) * tx * 8 * sizeof(float) : 0;
     if (smem > 48 * 1024) cudaFuncSetAttribute(block_means_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -112,6 +112,81 @@ __device__ void select_row(float* L, int nbc, float tau_f, uint32_t* bits, int l
     }
 }
 
+// Register-resident variant of select_row for rows of at most 32*NPL blocks: lane l holds blocks
+// l, l+32, ...; identical arithmetic (fp32 softmax, float64 sums, bisection, tie order).
+template <int NPL>
+__device__ void select_row_regs(const float* L, int nbc, float tau_f, uint32_t* bits, int lane) {
+    float p[NPL];
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const int j = lane + 32 * c;
+        p[c] = j < nbc ? L[j] : -INFINITY;
+    }
+    float mx = p[0];
+#pragma unroll
+    for (int c = 1; c < NPL; ++c) mx = fmaxf(mx, p[c]);
+    mx = warp_max_f(mx);
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        p[c] = (lane + 32 * c < nbc) ? expf(p[c] - mx) : 0.f;
+        s += p[c];
+    }
+    s = warp_sum_f(s);
+    double tot = 0.0;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        p[c] = (lane + 32 * c < nbc) ? __fdiv_rn(p[c], s) : -1.f;   // -1: not a block of this row
+        tot += p[c] > 0.f ? static_cast<double>(p[c]) : 0.0;
+    }
+    tot = warp_sum_d(tot);
+    if (!(static_cast<float>(tot) >= tau_f)) {
+#pragma unroll
+        for (int c = 0; c < NPL; ++c) {
+            const uint32_t b = __ballot_sync(0xffffffffu, lane + 32 * c < nbc);
+            if (lane == 0 && b) atomicOr(&bits[c], b);
+        }
+        return;
+    }
+    uint32_t lo = 0u, hi = 0x3F800001u;
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + ((hi - lo) >> 1);
+        const float v = __uint_as_float(mid);
+        double m = 0.0;
+#pragma unroll
+        for (int c = 0; c < NPL; ++c) m += p[c] >= v ? static_cast<double>(p[c]) : 0.0;
+        m = warp_sum_d(m);
+        if (static_cast<float>(m) >= tau_f) lo = mid; else hi = mid;
+    }
+    const float vstar = __uint_as_float(lo);
+    double above = 0.0;
+    int ties = 0;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        above += p[c] > vstar ? static_cast<double>(p[c]) : 0.0;
+        ties += (p[c] == vstar);
+    }
+    above = warp_sum_d(above);
+    ties = warp_sum_i(ties);
+    int kt = ties;
+    double acc = above;
+    for (int k = 1; k <= ties; ++k) {
+        acc += static_cast<double>(vstar);
+        if (static_cast<float>(acc) >= tau_f) { kt = k; break; }
+    }
+    int seen = 0;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const bool tie = p[c] == vstar;
+        const uint32_t tb = __ballot_sync(0xffffffffu, tie);
+        const int rank = seen + __popc(tb & ((1u << lane) - 1u));
+        const bool keep = p[c] > vstar || (tie && rank < kt);
+        const uint32_t kb = __ballot_sync(0xffffffffu, keep);
+        if (lane == 0 && kb) atomicOr(&bits[c], kb);
+        seen += __popc(tb);
+    }
+}
+
 __global__ void __launch_bounds__(SEL_THREADS) select_kernel(
     const float* __restrict__ qm, int64_t qbs, int64_t qhs, const float* __restrict__ km, int64_t khs, int64_t kbs,
     int nb_km, int H, int Hk, int D, int MB, int nb_total, int qblk0, float scale, float tau_f, int mode,
@@ -164,7 +239,10 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel(
         }
         __syncthreads();
         for (int i = warp; i < g; i += SEL_WARPS) {
-            select_row(logit + static_cast<size_t>(i) * nbp, nbc, tau_f, bits + i * nbw, lane);
+            float* L = logit + static_cast<size_t>(i) * nbp;
+            if (nbc <= 128) select_row_regs<4>(L, nbc, tau_f, bits + i * nbw, lane);
+            else if (nbc <= 512) select_row_regs<16>(L, nbc, tau_f, bits + i * nbw, lane);
+            else select_row(L, nbc, tau_f, bits + i * nbw, lane);
             __syncwarp();
             if (lane == 0) {
                 if (gi < nb_total) atomicOr(&bits[i * nbw + (gi >> 5)], 1u << (gi & 31));   // diagonal
