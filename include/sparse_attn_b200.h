@@ -112,17 +112,12 @@ SA_API int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_head_s
  * saturates at +-448 (torch's cast gives NaN above 464; in-range values match bit for bit).
  * transpose = 0: out[r*out_row_stride + h*out_head_stride + d];
  * transpose = 1: out[h*out_head_stride + d*out_row_stride + r] (V^T, keys contiguous), rows
- *                rows..rows_pad-1 written as zeros.
+ *                rows..rows_pad-1 written as zeros.  This is the reference's pre-quantised vT8
+ *                layout before its key permutation; the attention entry points take V untransposed.
  */
 SA_API int sa_quantize_e4m3(const void* x, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads,
                      int head_dim, const float* scale, int scale_stride, int mode, uint8_t* out,
                      int64_t out_row_stride, int64_t out_head_stride, int transpose, int rows_pad, void* stream);
-
-/* bf16 [rows, heads, head_dim] -> out[h*out_head_stride + d*out_d_stride + r] (V^T for the BF16
- * kernel), rows .. rows_pad-1 zero. */
-SA_API int sa_transpose_bf16(const void* x, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads,
-                      int head_dim, void* out, int64_t out_head_stride, int64_t out_d_stride, int rows_pad,
-                      void* stream);
 
 /* amax over a bf16 [rows, heads, head_dim] tensor: out[h] (per_head = 1) or out[0] (per tensor).
  * Replaces the `.abs().amax()` reductions of sm120_attn/sparse_prefill.py:227 / :465 and
@@ -135,9 +130,8 @@ SA_API int sa_absmax_bf16(const void* x, int64_t x_row_stride, int64_t x_head_st
  * `attention_sm120_fp8_tma` / `attention_sm120_fp8` (sm120_attn/kernels/kai_fa_fp8_tma.py:447-490,
  * kai_fa_fp8.py:331-375) for sa_attn_fwd_fp8 and `attention_sm120` (kai_fa_bf16.py:1206-1243) for
  * sa_attn_fwd_bf16.
- * q: [n_q, num_heads, head_dim]; k: [kv_len, num_kv_heads, head_dim]; vt: V transposed,
- * vt[hk*vt_head_stride + d*vt_d_stride + key] (keys contiguous, NOT the reference's permuted key
- * order); out: bf16 [n_q, num_heads, head_dim].  Element strides.  Query tile m (128 rows) covers
+ * q: [n_q, num_heads, head_dim]; k, v: [kv_len, num_kv_heads, head_dim] (the natural NHD layout:
+ * no transposed or key-permuted V is needed); out: bf16 [n_q, num_heads, head_dim].  Element strides.  Query tile m (128 rows) covers
  * q rows m*128 - q_front .. +127 (rows outside [0, n_q) read as zero, not written) at absolute
  * positions q_offset + m*128 + r; a key at position j is visible when j <= position and
  * j < kv_len.  Block lists (counts != NULL): tile m of head h walks
@@ -148,16 +142,16 @@ SA_API int sa_absmax_bf16(const void* x, int64_t x_row_stride, int64_t x_head_st
  * after scaling by 448 (kai_fa_fp8.py:248-253).  head_dim must be 128.
  */
 SA_API int sa_attn_fwd_fp8(const uint8_t* q, int64_t q_row_stride, int64_t q_head_stride, const uint8_t* k,
-                    int64_t k_row_stride, int64_t k_head_stride, const uint8_t* vt, int64_t vt_head_stride,
-                    int64_t vt_d_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
+                    int64_t k_row_stride, int64_t k_head_stride, const uint8_t* v, int64_t v_row_stride,
+                    int64_t v_head_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
                     int num_heads, int num_kv_heads, int head_dim, int kv_len, int q_front, int q_offset,
                     const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block, int kv_block,
                     const float* q_scale, int q_scale_stride, const float* k_scale, int k_scale_stride,
                     const float* v_scale, int v_scale_stride, float softmax_scale, int32_t* status, void* stream);
 
 SA_API int sa_attn_fwd_bf16(const void* q, int64_t q_row_stride, int64_t q_head_stride, const void* k,
-                     int64_t k_row_stride, int64_t k_head_stride, const void* vt, int64_t vt_head_stride,
-                     int64_t vt_d_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
+                     int64_t k_row_stride, int64_t k_head_stride, const void* v, int64_t v_row_stride,
+                     int64_t v_head_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
                      int num_heads, int num_kv_heads, int head_dim, int kv_len, int q_front, int q_offset,
                      const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block, int kv_block,
                      float softmax_scale, int32_t* status, void* stream);

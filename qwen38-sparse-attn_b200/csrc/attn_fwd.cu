@@ -1,9 +1,10 @@
 // Kernel (c): block-sparse causal FlashAttention forward on sm_100a tensor cores.
+// Q, K and V are read in their natural [rows, heads, head_dim] layout (V as an MN-major operand).
 //
 // One CTA per (128-row query tile, query head); two CTAs share an SM (each holds 256 of the 512
 // tensor-memory columns), so one CTA's softmax overlaps the other's MMAs.  Warp roles:
 //   warps 0-3  softmax + epilogue: thread r owns query row r = TMEM lane r
-//   warp 4     TMA producer: Q once, then K and V^T tiles of each walked key tile into
+//   warp 4     TMA producer: Q once, then K and V tiles of each walked key tile into
 //              mbarrier-guarded stage rings (no multicast)
 //   warp 5     TMEM allocator and single-thread tcgen05.mma issuer
 // Per key tile t (128 keys: one 128-key block or two 64-key blocks of the block list, walked from
@@ -11,7 +12,7 @@
 //   S  = Q K^T            tcgen05.mma, A and B from shared memory, fp32 accumulator in TMEM
 //   softmax (online, exp2 domain, scale folded: kai_fa_fp8.py:76-77) -> P written back into the S
 //   columns of TMEM (e4m3 after scaling by 448, or bf16); O rescaled in TMEM when the row max grows
-//   O += P V              tcgen05.mma, A = P from TMEM, B = V^T tile from shared memory
+//   O += P V              tcgen05.mma, A = P from TMEM, B = V tile from shared memory (MN-major)
 // Epilogue: O * out_scale / rowsum -> bf16 (0 for a row with no visible key, kai_fa_fp8.py:259-264).
 // Every mbarrier wait is bounded (sa_common.cuh); on expiry the CTA drains its copies and MMAs,
 // frees TMEM and exits with a status bit set.
@@ -46,14 +47,15 @@ struct Cfg {
     static constexpr int K_REG = BN * 128;                // bytes of one K region (64 rows x 128 B)
     static constexpr int Q_BYTES = NREG * Q_REG;
     static constexpr int K_BYTES = NREG * K_REG;
-    static constexpr int VROW = BN * E;                   // bytes per V^T row (64 keys)
-    static constexpr int V_BYTES = D * VROW;
+    static constexpr int V_REG = BN * 128;                // one V region: 64 keys x 128 B of head_dim
+    static constexpr int V_BYTES = NREG * V_REG;          // V tile [64 keys][128 d], d contiguous
     static constexpr int STAGE = K_BYTES + V_BYTES;
     static constexpr int SMEM_TILES = Q_BYTES + NST * STAGE;
     static constexpr int SMEM_BYTES = SMEM_TILES + 1024 /*barriers*/ + 1024 /*alignment*/;
     static constexpr uint32_t FMT = FP8 ? 0u : 1u;
     static constexpr uint32_t IDESC_QK = instr_desc(128, BN, FMT);
-    static constexpr uint32_t IDESC_PV = instr_desc(128, D, FMT);
+    // P.V: B = V tile read MN-major (d contiguous), so V is consumed in its natural layout
+    static constexpr uint32_t IDESC_PV = instr_desc(128, D, FMT) | (1u << 16);
     static constexpr uint32_t TMEM_COLS = 256;
     static constexpr uint32_t S_COL0 = 0;                 // S/P buffer b at S_COL0 + b * BN
 
@@ -272,9 +274,11 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                     tile_kb[st] = kb;
                     tile_rm[st] = rm;
                     mbar_arrive_expect_tx(smem_u32(bFull + st), C::STAGE);
-                    for (int r = 0; r < C::NREG; ++r)
+                    for (int r = 0; r < C::NREG; ++r) {
                         tma_load_3d(smem_u32(dst + r * C::K_REG), &tmK, smem_u32(bFull + st), r * C::REG_ELEMS, hk, kb);
-                    tma_load_3d(smem_u32(dst + C::K_BYTES), &tmV, smem_u32(bFull + st), kb, 0, hk);
+                        tma_load_3d(smem_u32(dst + C::K_BYTES + r * C::V_REG), &tmV, smem_u32(bFull + st),
+                                    r * C::REG_ELEMS, hk, kb);
+                    }
                 }
                 __syncwarp();
                 par[st] = (t / C::NST) & 1;
@@ -307,10 +311,13 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                 const uint32_t v_base = smem_u32(sKV + su * C::STAGE + C::K_BYTES);
                 const uint32_t a_tm = tmem + C::S_COL0 + (u & 1) * C::BN;
                 if (elect_one()) {
+                    // K step s covers keys UK*s.. of the tile: UK rows of 128 B, a whole number of
+                    // 8-row swizzle atoms; head_dim blocks of 128 B are V_REG apart
 #pragma unroll
                     for (int s = 0; s < C::PV_STEPS; ++s)
-                        mma_ts<FP8>(tmem + C::O_COL, a_tm + s * 8, smem_desc_kmajor(v_base + s * 32, C::VROW),
-                                    C::IDESC_PV, (u > 0 || s > 0) ? 1u : 0u);
+                        mma_ts<FP8>(tmem + C::O_COL, a_tm + s * 8,
+                                    smem_desc_mnmajor(v_base + s * C::UK * 128, C::V_REG), C::IDESC_PV,
+                                    (u > 0 || s > 0) ? 1u : 0u);
                     tc_commit(smem_u32(bEmpty + su));
                     tc_commit(smem_u32(bO));
                 }
@@ -556,8 +563,8 @@ int encode3d(CUtensorMap* map, bool fp8, const void* base, uint64_t d0, uint64_t
 }
 
 template <bool FP8>
-int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t krs, int64_t khs, const void* vt,
-                int64_t vths, int64_t vtds, void* out, int64_t ors, int64_t ohs, int n_q, int H, int Hk, int D, int kv_len,
+int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t krs, int64_t khs, const void* v,
+                int64_t vrs, int64_t vhs, void* out, int64_t ors, int64_t ohs, int n_q, int H, int Hk, int D, int kv_len,
                 int q_front, int q_offset, const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block,
                 int kv_block, const float* qsc, int qss, const float* ksc, int kss, const float* vsc, int vss,
                 float softmax_scale, int32_t* status, cudaStream_t stream) {
@@ -571,12 +578,12 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     if (counts && q_block != 128 && !(q_block == 64 && kv_block == 64))
         return fail(SA_ERR_UNSUPPORTED, "%s: q_block %d with kv_block %d (q_block 128, or 64 with kv_block 64)",
                     name, q_block, kv_block);
-    if (!q || !k || !vt || !out) return fail(SA_ERR_ARG, "%s: null pointer", name);
+    if (!q || !k || !v || !out) return fail(SA_ERR_ARG, "%s: null pointer", name);
     if (FP8 && (!qsc || !ksc || !vsc)) return fail(SA_ERR_ARG, "%s: null scale pointer", name);
     auto a16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
     const int E = C::E;
-    if (!a16(q) || !a16(k) || !a16(vt) || !a16(out) || (qrs * E) % 16 || (qhs * E) % 16 || (krs * E) % 16 ||
-        (khs * E) % 16 || (vths * E) % 16 || (vtds * E) % 16 || (ors * 2) % 16 || (ohs * 2) % 16)
+    if (!a16(q) || !a16(k) || !a16(v) || !a16(out) || (qrs * E) % 16 || (qhs * E) % 16 || (krs * E) % 16 ||
+        (khs * E) % 16 || (vrs * E) % 16 || (vhs * E) % 16 || (ors * 2) % 16 || (ohs * 2) % 16)
         return fail(SA_ERR_ALIGN, "%s: pointers must be 16-byte aligned and strides multiples of 16 bytes", name);
     if (n_q == 0) return SA_OK;
     const int n_tiles = (q_front + n_q + 127) / 128;
@@ -585,9 +592,7 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     const CUtensorMapSwizzle sw128 = CU_TENSOR_MAP_SWIZZLE_128B;
     if ((rc = encode3d(&tmQ, FP8, q, D, H, n_q > 0 ? n_q : 1, qhs * E, qrs * E, C::REG_ELEMS, 1, 128, sw128, "q"))) return rc;
     if ((rc = encode3d(&tmK, FP8, k, D, Hk, kv_len, khs * E, krs * E, C::REG_ELEMS, 1, C::BN, sw128, "k"))) return rc;
-    if ((rc = encode3d(&tmV, FP8, vt, kv_len, D, Hk, vtds * E, vths * E, C::BN, 128, 1,
-                       FP8 ? CU_TENSOR_MAP_SWIZZLE_64B : sw128, "v^T")))
-        return rc;
+    if ((rc = encode3d(&tmV, FP8, v, D, Hk, kv_len, vhs * E, vrs * E, C::REG_ELEMS, 1, C::BN, sw128, "v"))) return rc;
     Params p;
     p.counts = counts;
     p.lists = lists;
@@ -630,28 +635,28 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
 }  // namespace sa
 
 extern "C" int sa_attn_fwd_fp8(const uint8_t* q, int64_t q_row_stride, int64_t q_head_stride, const uint8_t* k,
-                               int64_t k_row_stride, int64_t k_head_stride, const uint8_t* vt, int64_t vt_head_stride,
-                               int64_t vt_d_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
+                               int64_t k_row_stride, int64_t k_head_stride, const uint8_t* v, int64_t v_row_stride,
+                               int64_t v_head_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
                                int num_heads, int num_kv_heads, int head_dim, int kv_len, int q_front, int q_offset,
                                const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block,
                                int kv_block, const float* q_scale, int q_scale_stride, const float* k_scale,
                                int k_scale_stride, const float* v_scale, int v_scale_stride, float softmax_scale,
                                int32_t* status, void* stream) {
-    return sa::launch_attn<true>(q, q_row_stride, q_head_stride, k, k_row_stride, k_head_stride, vt, vt_head_stride,
-                                 vt_d_stride, out, o_row_stride, o_head_stride, n_q, num_heads, num_kv_heads, head_dim,
+    return sa::launch_attn<true>(q, q_row_stride, q_head_stride, k, k_row_stride, k_head_stride, v, v_row_stride,
+                                 v_head_stride, out, o_row_stride, o_head_stride, n_q, num_heads, num_kv_heads, head_dim,
                                  kv_len, q_front, q_offset, counts, lists, list_stride, q_block, kv_block, q_scale,
                                  q_scale_stride, k_scale, k_scale_stride, v_scale, v_scale_stride, softmax_scale, status,
                                  static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sa_attn_fwd_bf16(const void* q, int64_t q_row_stride, int64_t q_head_stride, const void* k,
-                                int64_t k_row_stride, int64_t k_head_stride, const void* vt, int64_t vt_head_stride,
-                                int64_t vt_d_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
+                                int64_t k_row_stride, int64_t k_head_stride, const void* v, int64_t v_row_stride,
+                                int64_t v_head_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
                                 int num_heads, int num_kv_heads, int head_dim, int kv_len, int q_front, int q_offset,
                                 const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block,
                                 int kv_block, float softmax_scale, int32_t* status, void* stream) {
-    return sa::launch_attn<false>(q, q_row_stride, q_head_stride, k, k_row_stride, k_head_stride, vt, vt_head_stride,
-                                  vt_d_stride, out, o_row_stride, o_head_stride, n_q, num_heads, num_kv_heads, head_dim,
+    return sa::launch_attn<false>(q, q_row_stride, q_head_stride, k, k_row_stride, k_head_stride, v, v_row_stride,
+                                  v_head_stride, out, o_row_stride, o_head_stride, n_q, num_heads, num_kv_heads, head_dim,
                                   kv_len, q_front, q_offset, counts, lists, list_stride, q_block, kv_block, nullptr, 0,
                                   nullptr, 0, nullptr, 0, softmax_scale, status, static_cast<cudaStream_t>(stream));
 }

@@ -1,5 +1,5 @@
-// Memory-bound preparation kernels: block means (kernel a), e4m3 quantisation, V^T transposes
-// and absmax reductions.  All are HBM-streaming kernels: 16-byte vector loads along head_dim,
+// Memory-bound preparation kernels: block means (kernel a), e4m3 quantisation (row-major, or
+// transposed into the V^T layout of the reference's pre-quantised inputs) and absmax reductions.  All are HBM-streaming kernels: 16-byte vector loads along head_dim,
 // coalesced across a warp, rows walked by each thread with several loads in flight.
 #include <algorithm>
 
@@ -117,7 +117,7 @@ __global__ void quant_rows_kernel(const uint16_t* __restrict__ x, int64_t xrs, i
     }
 }
 
-// Tile transpose [64 rows x D] of one head -> out[h][d][r0..r0+63].  ELEM_OUT = 1 (e4m3) or 2 (bf16).
+// Tile transpose [64 rows x D] of one head -> out[h][d][r0..r0+63].  ELEM_OUT = 1 (e4m3).
 template <int ELEM_OUT>
 __global__ void transpose_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64_t xhs, int rows, int D,
                                  const float* __restrict__ scale, int iss, int mode, uint8_t* __restrict__ out,
@@ -270,23 +270,6 @@ extern "C" int sa_quantize_e4m3(const void* x, int64_t x_row_stride, int64_t x_h
                                                 head_dim, scale, scale_stride, mode, out, out_head_stride,
                                                 out_row_stride, rows_pad);
     return check_launch("transpose_kernel<e4m3>");
-}
-
-extern "C" int sa_transpose_bf16(const void* x, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads,
-                                 int head_dim, void* out, int64_t out_head_stride, int64_t out_d_stride, int rows_pad,
-                                 void* stream) {
-    if (rows < 0 || heads <= 0 || head_dim % 8) return fail(SA_ERR_ARG, "sa_transpose_bf16: bad sizes");
-    if (!x || !out) return fail(SA_ERR_ARG, "sa_transpose_bf16: null pointer");
-    if (!aligned16(x) || x_row_stride % 8 || x_head_stride % 8 || !aligned16(out) || out_head_stride % 8 ||
-        out_d_stride % 8 || rows_pad % 64 || rows_pad < rows)
-        return fail(SA_ERR_ALIGN, "sa_transpose_bf16: alignment / rows_pad %% 64");
-    if (rows_pad == 0) return SA_OK;
-    const size_t smem = static_cast<size_t>(head_dim) * (128 + 16);
-    dim3 grid(rows_pad / 64, heads);
-    transpose_kernel<2><<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint16_t*>(x), x_row_stride, x_head_stride, rows, head_dim, nullptr, 0, 0,
-        static_cast<uint8_t*>(out), out_head_stride, out_d_stride, rows_pad);
-    return check_launch("transpose_kernel<bf16>");
 }
 
 extern "C" int sa_absmax_bf16(const void* x, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads,

@@ -306,6 +306,14 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t saddr, int row_byt
            (layout << 61);
 }
 
+// Shared-memory descriptor for an MN-major operand tile with 128B swizzle: rows of 128 bytes along
+// the MN dimension, one row per K index; 8-row groups (1024 B) along K are the stride offset, and
+// successive 128-byte MN column blocks are `mn_block_bytes` apart (leading offset).
+__device__ __forceinline__ uint64_t smem_desc_mnmajor(uint32_t saddr, uint32_t mn_block_bytes) {
+    return (static_cast<uint64_t>((saddr >> 4) & 0x3FFFu)) | (static_cast<uint64_t>((mn_block_bytes >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
 // Instruction descriptor: fp32 accumulator, A/B K-major, A/B format (bf16 = 1, e4m3 = 0).
 __host__ __device__ constexpr uint32_t instr_desc(int M, int N, uint32_t ab_format) {
     return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (static_cast<uint32_t>(N >> 3) << 17) |

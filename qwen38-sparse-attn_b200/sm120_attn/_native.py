@@ -29,7 +29,6 @@ SIGNATURES = {
     'sa_select': [_p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _f32, _i32, _p, _p,
                   _i64, _p, _p],
     'sa_quantize_e4m3': [_p, _i64, _i64, _i32, _i32, _i32, _p, _i32, _i32, _p, _i64, _i64, _i32, _i32, _p],
-    'sa_transpose_bf16': [_p, _i64, _i64, _i32, _i32, _i32, _p, _i64, _i64, _i32, _p],
     'sa_absmax_bf16': [_p, _i64, _i64, _i32, _i32, _i32, _i32, _p, _p],
     'sa_attn_fwd_fp8': [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32,
                         _i32, _i32, _p, _p, _i64, _i32, _i32, _p, _i32, _p, _i32, _p, _i32, _f32, _p, _p],

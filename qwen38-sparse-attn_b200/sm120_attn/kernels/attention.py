@@ -7,10 +7,10 @@ kai_fa_fp8.py:331-375 and kai_fa_fp8_tma.py:447-490.  Behind them is one tcgen05
 num_threads, s_pipeline, pingpong, prefetch) are validated and otherwise have no effect, except
 that m_block / n_block give the row and key granularity of caller-supplied block lists.
 
-V is consumed transposed with keys contiguous.  The reference's FP8 drivers take V^T with its key
-order permuted inside each 32-key block (VT_KEY_PERM, for its mma.sync register layout); these
-drivers undo that permutation for `prequant` inputs so callers can pass exactly what they passed
-before.
+The kernel reads V in its natural [kv, Hk, D] layout.  The reference's FP8 drivers take `prequant`
+V as V^T with its key order permuted inside each 32-key block (VT_KEY_PERM, for its mma.sync
+register layout); these drivers undo the permutation and the transpose for `prequant` inputs so
+callers can pass exactly what they passed before.
 """
 from __future__ import annotations
 
@@ -77,11 +77,10 @@ def quantize_e4m3(x):
     return out.view(x.shape), float(scale_t.item())
 
 
-def _quantize_vt(v, scale: float, rows_pad: int):
-    Hk, D = v.shape[1], v.shape[2]
-    vt = torch.empty(Hk, D, rows_pad, dtype=torch.float8_e4m3fn, device=v.device)
-    ops.quantize(v, _scalar(scale, v.device), SA_QUANT_DIV, vt.view(torch.uint8), transpose=True, rows_pad=rows_pad)
-    return vt
+def _quantize(x, scale: float):
+    out = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    ops.quantize(x, _scalar(scale, x.device), SA_QUANT_DIV, out)
+    return out
 
 
 def _lists_args(counts, lists):
@@ -117,11 +116,9 @@ def attention_sm120(q, k, v, q_offset=None, *, causal=True, m_block=64, n_block=
         out = torch.empty_like(q)
     if not causal:
         q_offset = max(q_offset, kv_len)              # every key visible to every row
-    rows_pad = -(-kv_len // 64) * 64
-    vt = torch.empty(Hk, D, rows_pad, dtype=torch.bfloat16, device=v.device)
-    ops.transpose_bf16(v[:kv_len], vt, rows_pad)
+    v = v if v.stride(-1) == 1 else v.contiguous()
     counts, lists = _lists_args(counts, lists)
-    ops.attn_bf16(q, k, vt, out, kv_len, 0, q_offset, counts, lists, n_block, D ** -0.5, q_block=m_block)
+    ops.attn_bf16(q, k, v, out, kv_len, 0, q_offset, counts, lists, n_block, D ** -0.5, q_block=m_block)
     return out
 
 
@@ -143,19 +140,19 @@ def attention_sm120_fp8(q, k, v, q_offset=None, *, causal=True, out=None, counts
         v3 = v if v.stride(-1) == 1 else v.contiguous()
         amax = ops.absmax(v3, per_head=False).clamp_min_(1e-6)
         sv = float((amax / 448.0).item())
-        vt8 = _quantize_vt(v3, sv, -(-kv_len // 64) * 64)
+        v8 = _quantize(v3, sv)
         kv_keys = kv_len
     else:
         q8, sq, k8, sk, vT8, sv = prequant
-        vt8 = _unpermute_vt_keys(vT8)
         kv_keys = k8.shape[0]
+        v8 = _unpermute_vt_keys(vT8)[:, :, :kv_keys].permute(2, 0, 1).contiguous()
     if not causal:
         q_offset = max(q_offset, kv_keys)
     if out is None:
         out = torch.empty(n, H, D, dtype=torch.bfloat16, device=q.device)
     counts, lists = _lists_args(counts, lists)
     dev = q.device
-    ops.attn_fp8(q8.view(torch.uint8), k8.view(torch.uint8), vt8.view(torch.uint8), out, kv_keys, 0, q_offset,
+    ops.attn_fp8(q8.view(torch.uint8), k8.view(torch.uint8), v8.view(torch.uint8), out, kv_keys, 0, q_offset,
                  counts, lists, 64, _scalar(sq, dev), _scalar(sk, dev), _scalar(sv, dev), D ** -0.5, q_block=m_block)
     return out
 

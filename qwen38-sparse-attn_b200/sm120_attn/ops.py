@@ -93,14 +93,6 @@ def quantize(x, scale, mode: int, out, transpose: bool = False, rows_pad: int = 
                out.stride(0), out.stride(1), 0, 0, _stream(x.device))
 
 
-def transpose_bf16(x, out, rows_pad: int):
-    """x [rows, heads, D] bf16 -> out [heads, D, rows_pad] bf16 (zero padded)."""
-    _need_cuda('transpose_bf16', x, out)
-    rows, heads, D = x.shape
-    N.call('sa_transpose_bf16', _p(x), x.stride(0), x.stride(1), rows, heads, D, _p(out), out.stride(0),
-           out.stride(1), rows_pad, _stream(x.device))
-
-
 def absmax(x, per_head: bool, out=None):
     _need_cuda('absmax', x, out)
     rows, heads, D = x.shape
@@ -111,28 +103,32 @@ def absmax(x, per_head: bool, out=None):
     return out
 
 
-def attn_fp8(q8, k8, vt8, out, kv_len: int, q_front: int, q_offset: int, counts, lists, kv_block: int,
+def attn_fp8(q8, k8, v8, out, kv_len: int, q_front: int, q_offset: int, counts, lists, kv_block: int,
              q_scale, k_scale, v_scale, softmax_scale: float, q_block: int = 128):
-    """Block-sparse (counts/lists) or dense causal FP8 attention; see sa_attn_fwd_fp8."""
-    _need_cuda('attn_fp8', q8, k8, vt8, out, counts, lists, q_scale, k_scale, v_scale)
+    """Block-sparse (counts/lists) or dense causal FP8 attention; see sa_attn_fwd_fp8.
+
+    q8 [n, H, D], k8 / v8 [kv, Hk, D] e4m3 bytes (last dim contiguous), out [n, H, D] bf16."""
+    _need_cuda('attn_fp8', q8, k8, v8, out, counts, lists, q_scale, k_scale, v_scale)
     n, H, D = q8.shape
     Hk = k8.shape[1]
     st = status_word(q8.device)
-    N.call('sa_attn_fwd_fp8', _p(q8), q8.stride(0), q8.stride(1), _p(k8), k8.stride(0), k8.stride(1), _p(vt8),
-           vt8.stride(0), vt8.stride(1), _p(out), out.stride(0), out.stride(1), n, H, Hk, D, kv_len, q_front,
+    N.call('sa_attn_fwd_fp8', _p(q8), q8.stride(0), q8.stride(1), _p(k8), k8.stride(0), k8.stride(1), _p(v8),
+           v8.stride(0), v8.stride(1), _p(out), out.stride(0), out.stride(1), n, H, Hk, D, kv_len, q_front,
            q_offset, _p(counts), _p(lists), lists.stride(0) if lists is not None else 0, q_block, kv_block,
            _p(q_scale), 0 if q_scale.numel() == 1 else 1, _p(k_scale), 0 if k_scale.numel() == 1 else 1,
            _p(v_scale), 0 if v_scale.numel() == 1 else 1, float(softmax_scale), _p(st), _stream(q8.device))
 
 
-def attn_bf16(q, k, vt, out, kv_len: int, q_front: int, q_offset: int, counts, lists, kv_block: int,
+def attn_bf16(q, k, v, out, kv_len: int, q_front: int, q_offset: int, counts, lists, kv_block: int,
               softmax_scale: float, q_block: int = 128):
-    """Block-sparse (counts/lists) or dense causal BF16 attention; see sa_attn_fwd_bf16."""
-    _need_cuda('attn_bf16', q, k, vt, out, counts, lists)
+    """Block-sparse (counts/lists) or dense causal BF16 attention; see sa_attn_fwd_bf16.
+
+    q [n, H, D], k / v [kv, Hk, D] bf16 (last dim contiguous), out [n, H, D] bf16."""
+    _need_cuda('attn_bf16', q, k, v, out, counts, lists)
     n, H, D = q.shape
     Hk = k.shape[1]
     st = status_word(q.device)
-    N.call('sa_attn_fwd_bf16', _p(q), q.stride(0), q.stride(1), _p(k), k.stride(0), k.stride(1), _p(vt),
-           vt.stride(0), vt.stride(1), _p(out), out.stride(0), out.stride(1), n, H, Hk, D, kv_len, q_front,
+    N.call('sa_attn_fwd_bf16', _p(q), q.stride(0), q.stride(1), _p(k), k.stride(0), k.stride(1), _p(v),
+           v.stride(0), v.stride(1), _p(out), out.stride(0), out.stride(1), n, H, Hk, D, kv_len, q_front,
            q_offset, _p(counts), _p(lists), lists.stride(0) if lists is not None else 0, q_block, kv_block,
            float(softmax_scale), _p(st), _stream(q.device))

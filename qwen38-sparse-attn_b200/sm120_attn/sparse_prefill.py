@@ -163,14 +163,11 @@ class SparsePrefill:
         ops.select(qm, km, self.H, self.Hk, NB, qs // B, self.scale, self.tau, SA_SELECT_PER_HEAD,
                    counts=counts, lists=lists)
         t1 = self._tick()
-        rows_pad = _cdiv(kv_len, 128) * 128
-        vt = torch.empty(self.Hk, self.D, rows_pad, dtype=torch.bfloat16, device=dev)
-        ops.transpose_bf16(v[:kv_len], vt, rows_pad)
         o, copy_back = self._out(out, n, dev)
         ev0, ev1 = self._attn_events()
         if ev0 is not None:
             ev0.record()
-        ops.attn_bf16(q, k[:kv_len], vt, o, kv_len, front, qs, counts, lists, B, self.scale, q_block=B)
+        ops.attn_bf16(q, k[:kv_len], v[:kv_len], o, kv_len, front, qs, counts, lists, B, self.scale, q_block=B)
         if ev1 is not None:
             ev1.record()
         t2 = self._tick()
@@ -223,16 +220,15 @@ class SparsePrefill:
                    SA_SELECT_PAIR_UNION if B == 64 else SA_SELECT_PER_HEAD, counts=counts, lists=lists)
         k8 = torch.empty(kv_len, self.Hk, self.D, dtype=torch.uint8, device=dev)
         ops.quantize(k[:kv_len], inv[1:2], SA_QUANT_MUL_BF16, k8)
-        rows_pad = _cdiv(kv_len, 128) * 128
-        vt8 = torch.empty(self.Hk, self.D, rows_pad, dtype=torch.uint8, device=dev)
-        ops.quantize(v[:kv_len], inv[2:3], SA_QUANT_MUL_BF16, vt8, transpose=True, rows_pad=rows_pad)
+        v8 = torch.empty(kv_len, self.Hk, self.D, dtype=torch.uint8, device=dev)
+        ops.quantize(v[:kv_len], inv[2:3], SA_QUANT_MUL_BF16, v8)
         t1 = self._tick()
         o, copy_back = self._out(out, n, dev)
         sc = torch.tensor([sq, sk, sv], dtype=torch.float32).to(dev, non_blocking=True)
         ev0, ev1 = self._attn_events()
         if ev0 is not None:
             ev0.record()
-        ops.attn_fp8(q8, k8, vt8, o, kv_len, front, qs, counts, lists, B, sc[0:1], sc[1:2], sc[2:3], self.scale)
+        ops.attn_fp8(q8, k8, v8, o, kv_len, front, qs, counts, lists, B, sc[0:1], sc[1:2], sc[2:3], self.scale)
         if ev1 is not None:
             ev1.record()
         self.last_counts = counts

@@ -81,12 +81,6 @@ def test_quantize_modes_bitexact():
     ref_t = np.zeros((2, 128, 384), np.uint8)
     ref_t[:, :, :333] = bits.transpose(1, 2, 0)
     np.testing.assert_array_equal(vt.cpu().numpy(), ref_t)
-    # bf16 transpose
-    vtb = torch.full((2, 128, 384), 3.0, dtype=torch.bfloat16, device=DEV)
-    ops.transpose_bf16(xs, vtb, 384)
-    ref_b = np.zeros((2, 128, 384), np.float32)
-    ref_b[:, :, :333] = f32(v).transpose(1, 2, 0)
-    np.testing.assert_array_equal(f32(vtb), ref_b)
 
 
 def test_absmax():
@@ -193,12 +187,9 @@ def _run_fp8(q8, k8, v8, scales, kv_len, q_front, q_offset, counts=None, lists=N
     ops = _ops()
     n, H, D = q8.shape
     Hk = k8.shape[1]
-    rows_pad = -(-kv_len // 128) * 128
-    vt = np.zeros((Hk, D, rows_pad), np.uint8)
-    vt[:, :, :kv_len] = v8[:kv_len].transpose(1, 2, 0)
     out = torch.full((n, H, D), float('nan'), dtype=torch.bfloat16, device=DEV)
     sq, sk, sv = (torch.from_numpy(np.asarray(s, np.float32)).to(DEV) for s in scales)
-    ops.attn_fp8(torch.from_numpy(q8).to(DEV), torch.from_numpy(k8).to(DEV), torch.from_numpy(vt).to(DEV), out,
+    ops.attn_fp8(torch.from_numpy(q8).to(DEV), torch.from_numpy(k8).to(DEV), torch.from_numpy(v8[:kv_len]).to(DEV), out,
                  kv_len, q_front, q_offset, counts, lists, kv_block, sq, sk, sv, D ** -0.5)
     ops.check_status(DEV)
     return f32(out)
@@ -254,12 +245,9 @@ def _run_bf16(q, k, v, kv_len, q_front, q_offset, counts=None, lists=None, kv_bl
     ops = _ops()
     n, H, D = q.shape
     Hk = k.shape[1]
-    rows_pad = -(-kv_len // 128) * 128
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
-    vt = torch.empty(Hk, D, rows_pad, dtype=torch.bfloat16, device=DEV)
-    ops.transpose_bf16(vd[:kv_len], vt, rows_pad)
     out = torch.full((n, H, D), float('nan'), dtype=torch.bfloat16, device=DEV)
-    ops.attn_bf16(qd, kd, vt, out, kv_len, q_front, q_offset, counts, lists, kv_block, D ** -0.5)
+    ops.attn_bf16(qd, kd, vd[:kv_len], out, kv_len, q_front, q_offset, counts, lists, kv_block, D ** -0.5)
     ops.check_status(DEV)
     return f32(out)
 
@@ -315,12 +303,9 @@ def test_attn_bf16_sparse_64row_lists(n, kv, q_front):
     masks = _random_row_masks(H, nb64, NB, q_offset, 64, 64, 0.3, seed=n)
     counts, lists = _lists_from_masks(masks)
     ops = _ops()
-    rows_pad = -(-kv // 128) * 128
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
-    vt = torch.empty(Hk, 128, rows_pad, dtype=torch.bfloat16, device=DEV)
-    ops.transpose_bf16(vd, vt, rows_pad)
     out = torch.full((n, H, 128), float('nan'), dtype=torch.bfloat16, device=DEV)
-    ops.attn_bf16(qd, kd, vt, out, kv, q_front, q_offset, counts, lists, 64, 128 ** -0.5, q_block=64)
+    ops.attn_bf16(qd, kd, vd, out, kv, q_front, q_offset, counts, lists, 64, 128 ** -0.5, q_block=64)
     ops.check_status(DEV)
     ref = O.attention_ref(f32(q), f32(k), f32(v), q_pos0, masks, q_block=64, kv_block=64, q_front=q_front)
     assert np.abs(f32(out) - ref).max() < 2e-2
