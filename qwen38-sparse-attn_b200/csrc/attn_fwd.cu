@@ -19,6 +19,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <climits>
 #include <mutex>
 
 #include "sa_common.cuh"
@@ -85,14 +86,16 @@ struct Params {
 // to the first like the reference (kai_fa_fp8_tma.py:149-162).  Modes: dense causal walk; one
 // list of 64- or 128-key blocks for the whole tile; two lists of 64-key blocks, one per 64-row
 // half of the tile (the BF16 path's 64-row query blocks), walked as their merged union with a
-// per-tile mask of the halves that selected the block.
+// per-tile mask of the halves that selected the block.  The producer and every softmax thread
+// run the same walk; list heads are loaded one step ahead, so a step never waits on its load.
 struct Walker {
     const int32_t* a;
     const int32_t* b;
-    int ia, ib;          // next list index (counting down)
+    int ia, ib;          // list index of the cached head (counting down)
     int va, vb;          // cached list heads (-1 when exhausted)
     int dense_next;      // dense: next 64-key tile base, counting down
     int kvb;
+    int blk_lim;         // block ids at or above this are invalid (their key base would overflow)
     int half;            // 128-key blocks: which half of the current block comes next (1 = upper)
     int mode;            // 0 dense, 1 one list, 2 two lists
     bool bad;
@@ -109,8 +112,8 @@ struct Walker {
         }
         if (mode == 1) {
             if (ia < 0) return false;
-            const int blk = __ldg(a + ia);
-            if (blk < 0 || blk >= KEY_NONE / kvb) {
+            const int blk = va;
+            if (blk < 0 || blk >= blk_lim) {
                 bad = true;
                 kbase = KEY_NONE;
             } else {
@@ -121,6 +124,7 @@ struct Walker {
             } else {
                 half = 1;
                 --ia;
+                va = load(a, ia);
             }
             return true;
         }
@@ -143,6 +147,7 @@ __device__ __forceinline__ Walker make_walker(const Params& p, int h, int m) {
     Walker w;
     w.bad = false;
     w.kvb = p.kv_block;
+    w.blk_lim = KEY_NONE / p.kv_block;
     w.half = 1;
     w.a = w.b = nullptr;
     w.ia = w.ib = -1;
@@ -158,6 +163,7 @@ __device__ __forceinline__ Walker make_walker(const Params& p, int h, int m) {
         const int64_t row = static_cast<int64_t>(h) * p.list_rows_per_head + m;
         w.a = p.lists + row * p.list_stride;
         w.ia = max(__ldg(p.counts + row), 0) - 1;
+        w.va = w.load(w.a, w.ia);
     } else {
         w.mode = 2;
         const int r0 = 2 * m, r1 = 2 * m + 1;
@@ -202,11 +208,9 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bDrain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     // Per-stage tile descriptor written by the producer before it arms the stage's full barrier:
-    // key base of the 64-key tile (KEY_END after the last tile) and the mask of query-row halves
-    // that selected it.  The MMA and softmax warps read it after waiting on that barrier, so only
-    // the producer walks the block lists in global memory.
+    // key base of the 64-key tile, KEY_END after the last tile.  The MMA warp reads it after
+    // waiting on that barrier.
     volatile int* tile_kb = const_cast<int*>(reinterpret_cast<volatile int*>(abort_flag + 1));
-    volatile uint32_t* tile_rm = reinterpret_cast<volatile uint32_t*>(tile_kb + C::NST);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m = p.n_tiles - 1 - static_cast<int>(blockIdx.x);     // late (heavier) tiles first
@@ -272,7 +276,6 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                 uint8_t* dst = sKV + st * C::STAGE;
                 if (elect_one()) {
                     tile_kb[st] = kb;
-                    tile_rm[st] = rm;
                     mbar_arrive_expect_tx(smem_u32(bFull + st), C::STAGE);
                     for (int r = 0; r < C::NREG; ++r) {
                         tma_load_3d(smem_u32(dst + r * C::K_REG), &tmK, smem_u32(bFull + st), r * C::REG_ELEMS, hk, kb);
@@ -296,15 +299,44 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     } else if (warp == 5) {
         // ---------------------------------------------------------------- MMA issuer (warp-uniform;
         // one elected lane issues each tcgen05.mma / commit)
+        //
+        // Issue order: S(0), S(1), then for each tile u: O += P(u) V_u immediately followed by
+        // S(u+2) = Q K_{u+2}^T into the S buffer P(u) was just read from (the tcgen05 operations of
+        // one CTA execute in issue order).  The critical path of the pipeline is P(u) written ->
+        // S(u+2) ready, so with three or more stages the wait for tile u+2's K and V is taken before
+        // the wait for P(u) and only the two issues sit on that path.  With two stages tile u+2
+        // reuses tile u's stage, which only O += P(u) V_u releases, so there it waits afterwards.
         {
+            constexpr bool EARLY_FETCH = C::NST >= 3;
             const uint32_t q_base = smem_u32(sQ);
-            bool ok = true, q_ready = false;
-            int t = 0;
-            // S(t) = Q K_t^T into S buffer t&1, then O += P(t-1) V_{t-1}: QK of the next tile runs
-            // on the tensor cores while the softmax warps work on the current one.
+            bool ok = true;
+            int T = INT_MAX;                                          // tiles in the walk, once known
+            auto fetch = [&](int t) -> bool {                         // wait for tile t's stage
+                const int st = t % C::NST;
+                if (!__all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bFull + st), (t / C::NST) & 1, abort_flag,
+                                                             p.status, SA_DEV_WAIT_KV)))
+                    return false;
+                if (tile_kb[st] == KEY_END) T = t;
+                return true;
+            };
+            auto issue_qk = [&](int t) {
+                tc_fence_after();
+                const uint32_t k_base = smem_u32(sKV + (t % C::NST) * C::STAGE);
+                if (elect_one()) {
+#pragma unroll
+                    for (int s = 0; s < C::QK_STEPS; ++s) {
+                        const uint32_t qoff = (s / 4) * C::Q_REG + (s % 4) * 32;
+                        const uint32_t koff = (s / 4) * C::K_REG + (s % 4) * 32;
+                        mma_ss<FP8>(tmem + C::S_COL0 + (t & 1) * C::BN, smem_desc_kmajor(q_base + qoff, 128),
+                                    smem_desc_kmajor(k_base + koff, 128), C::IDESC_QK, s > 0 ? 1u : 0u);
+                    }
+                    tc_commit(smem_u32(bS + (t & 1)));
+                }
+                __syncwarp();
+            };
             auto issue_pv = [&](int u) -> bool {
-                if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bP + (u & 1)), (u >> 1) & 1, abort_flag, p.status,
-                                                        SA_DEV_WAIT_P)))
+                if (!__all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bP + (u & 1)), (u >> 1) & 1, abort_flag,
+                                                             p.status, SA_DEV_WAIT_P)))
                     return false;
                 tc_fence_after();
                 const int su = u % C::NST;
@@ -324,38 +356,21 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                 __syncwarp();
                 return true;
             };
-            for (;; ++t) {
-                const int st = t % C::NST;
-                if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bFull + st), (t / C::NST) & 1, abort_flag, p.status,
-                                                        SA_DEV_WAIT_KV))) {
-                    ok = false;
-                    break;
-                }
-                if (tile_kb[st] == KEY_END) break;
-                if (!q_ready) {
-                    if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bQ), 0, abort_flag, p.status, SA_DEV_WAIT_Q))) {
-                        ok = false;
-                        break;
-                    }
-                    q_ready = true;
-                }
-                tc_fence_after();
-                const uint32_t k_base = smem_u32(sKV + st * C::STAGE);
-                if (elect_one()) {
-#pragma unroll
-                    for (int s = 0; s < C::QK_STEPS; ++s) {
-                        const uint32_t qoff = (s / 4) * C::Q_REG + (s % 4) * 32;
-                        const uint32_t koff = (s / 4) * C::K_REG + (s % 4) * 32;
-                        mma_ss<FP8>(tmem + C::S_COL0 + (t & 1) * C::BN, smem_desc_kmajor(q_base + qoff, 128),
-                                    smem_desc_kmajor(k_base + koff, 128), C::IDESC_QK, s > 0 ? 1u : 0u);
-                    }
-                    tc_commit(smem_u32(bS + (t & 1)));
-                }
-                __syncwarp();
-                if (t >= 1 && !issue_pv(t - 1)) { ok = false; break; }
+            ok = fetch(0);
+            if (ok && T > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bQ), 0, abort_flag, p.status, SA_DEV_WAIT_Q));
+                if (ok) issue_qk(0);
+                if (ok) ok = fetch(1);
+                if (ok && T > 1) issue_qk(1);
             }
-            if (ok && t >= 1) ok = issue_pv(t - 1);
-            if (ok && t >= 1 && elect_one()) tc_commit(smem_u32(bOF));
+            for (int u = 0; ok && u < T; ++u) {
+                const int nx = u + 2;
+                if (EARLY_FETCH && T > nx && !(ok = fetch(nx))) break;
+                if (!(ok = issue_pv(u))) break;
+                if (!EARLY_FETCH && T > nx && !(ok = fetch(nx))) break;
+                if (T > nx) issue_qk(nx);
+            }
+            if (ok && T > 0 && elect_one()) tc_commit(smem_u32(bOF));
             __syncwarp();
             if (*abort_flag) {
                 if (elect_one()) tc_commit(smem_u32(bDrain));
@@ -385,14 +400,17 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         int t = 0;
+        // The softmax threads walk the block lists themselves (the same walk as the producer's), one
+        // tile ahead, instead of waiting on the stage barrier for the producer's tile descriptor.
+        Walker walk = make_walker(p, h, m);
+        int kb_next;
+        uint32_t rm_next;
+        bool have_next = walk.next(kb_next, rm_next);
         for (;; ++t) {
-            const int st = t % C::NST;
-            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bFull + st), (t / C::NST) & 1, abort_flag, p.status,
-                                                   SA_DEV_WAIT_KV));
-            if (!ok) break;
-            const int kb = tile_kb[st];
-            if (kb == KEY_END) break;
-            const uint32_t rm = tile_rm[st];
+            if (!have_next) break;
+            const int kb = kb_next;
+            const uint32_t rm = rm_next;
+            have_next = walk.next(kb_next, rm_next);
             const int b = t & 1;
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bS + b), (t >> 1) & 1, abort_flag, p.status, SA_DEV_WAIT_S));
             if (!ok) break;
@@ -437,7 +455,11 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                              make_float2(0.f, 0.f)};
             auto exp_pair = [&](int c) -> float2 {
                 const float2 e = ffma2(make_float2(x[c], x[c + 1]), sl2v, biasv);
-                const float2 pr = make_float2(ex2_approx(e.x), ex2_approx(e.y));
+                // FP8: one pair in eight on the FMA pipe, easing the MUFU unit (exp2_poly's 7.5e-5
+                // relative error is far below e4m3's rounding)
+                const bool on_fma = FP8 && ((c >> 1) & 7) == 7;
+                const float2 pr = on_fma ? make_float2(exp2_poly(e.x), exp2_poly(e.y))
+                                         : make_float2(ex2_approx(e.x), ex2_approx(e.y));
                 acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pr);
                 return pr;
             };

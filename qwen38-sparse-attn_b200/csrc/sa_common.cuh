@@ -141,6 +141,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 #define SA_WAIT_SUSPEND_NS 1000000u   // try_wait suspend-time hint: a waiting warp sleeps (up to 1 ms)
 #endif                                // until the phase completes instead of re-issuing polls
 
+// Poll without a suspend hint: the cheapest test of a phase that has usually completed already.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -156,10 +167,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // false at once when another thread of the CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* status, int code) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 7u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - t0 > SA_WAIT_TIMEOUT_NS) {
+                *abort_flag = 1;
+                if (status) atomicOr(status, code);
+                return false;
+            }
+        }
+    }
+}
+
+// Same bound, polling without the suspend hint: for a latency-critical waiter (the MMA issuer)
+// whose wake-up after a suspension would sit on the pipeline's critical path.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                               int* status, int code) {
+    if (mbar_test(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_test(bar, parity)) return true;
         if ((i & 7u) == 0) {
             if (*abort_flag) return false;
             if (globaltimer() - t0 > SA_WAIT_TIMEOUT_NS) {
@@ -211,6 +241,12 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy (tensor cores,
+// TMA) before the hand-off that lets them be read.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  :: "r"(bar) : "memory");
