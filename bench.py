@@ -127,13 +127,16 @@ def run_b200(args):
         dist.init_process_group('nccl', timeout=timedelta(seconds=120), device_id=dev)
     import sm120_attn.sparse_prefill as ksp
     from sm120_attn import ops
+    from sm120_attn.shard import kv_head_range, reduce_over_ranks
     ksp.BLOCK = BLOCK
     if args.scaling == 'strong':
-        if HK_FULL % world:
-            raise SystemExit('strong scaling needs N to divide 8')
-        hk = HK_FULL // world
+        try:
+            lo, hi = kv_head_range(rank, world, HK_FULL)     # this rank's KV heads of the one problem
+        except ValueError as e:
+            raise SystemExit(f'strong scaling: {e}')
+        hk = hi - lo
     else:
-        hk = HK_FULL
+        hk = HK_FULL                                         # every rank runs a full problem
     h = hk * (H_FULL // HK_FULL)
     q, k, v = make_rank_inputs(hk, 1000 + rank, args.strength, dev)
     sp = ksp.SparsePrefill(h, hk, D, dev, tau=TAU, min_kv=0, min_q=0, kernel='sm120fp8')
@@ -217,13 +220,8 @@ def run_b200(args):
     d2h = o_h.numel() * 2
     ops.check_status(dev)
     # ---------------- reductions over ranks
-    vals = torch.tensor([ms_total, e2e_ms, sum(attn_ms) / max(len(attn_ms), 1)], dtype=torch.float64, device=dev)
-    sums = torch.tensor([flops, tile_flops], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
-    ms_total, e2e_ms, attn_avg = vals.tolist()
-    flops_all, tile_all = sums.tolist()
+    (ms_total, e2e_ms, attn_avg), (flops_all, tile_all) = reduce_over_ranks(
+        [ms_total, e2e_ms, sum(attn_ms) / max(len(attn_ms), 1)], [flops, tile_flops], device=dev)
     hbm, bf16, how = peaks()
     fp8_peak = 2.0 * bf16
     value = flops_all * args.steps / (ms_total * 1e-3) / 1e12

@@ -1,0 +1,72 @@
+"""Worker for the two-rank gloo test of KV-head sharding (imported by spawned processes)."""
+from __future__ import annotations
+
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+for p in (str(ROOT), str(ROOT / 'qwen38-sparse-attn_b200'), str(ROOT / 'tests')):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+N, KV, H, HK, D, BLOCK, TAU = 200, 1024, 8, 2, 128, 64, 0.95
+
+
+def _shard_problem(rank, world):
+    """Full problem built identically on every rank; returns it and this rank's result on its shard."""
+    import numpy as np
+    import oracle as O
+    import synth
+    from sm120_attn.shard import head_ranges
+    q, k, v, _ = synth.make_qkv(N, KV, H, HK, D, block=BLOCK, seed=11, strength='strong')
+    q, k, v = (t.float().numpy() for t in (q, k, v))
+    q_start = KV - N
+    (q_lo, q_hi), (kv_lo, kv_hi) = head_ranges(rank, world, H, HK)
+    qs = q_start - q_start % BLOCK
+
+    def select(qq, kk, h, hk):
+        qm = O.q_block_means(qq, q_start, BLOCK)
+        _, km = O.block_means(kk, 0, BLOCK)
+        return O.select_masks(qm, km, qs, BLOCK, h, hk, TAU)
+
+    masks = select(q[:, q_lo:q_hi], k[:, kv_lo:kv_hi], q_hi - q_lo, kv_hi - kv_lo)
+    out = O.attention_ref(q[:, q_lo:q_hi], k[:, kv_lo:kv_hi], v[:, kv_lo:kv_hi], q_start, masks,
+                          q_block=BLOCK, kv_block=BLOCK, q_front=q_start % BLOCK)
+    full = (q, k, v, select, q_start)
+    return full, masks, out, (q_lo, q_hi)
+
+
+def run(rank, world, port, result_dir):
+    import numpy as np
+    import oracle as O
+    import torch
+    import torch.distributed as dist
+    from sm120_attn.shard import reduce_over_ranks
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        (q, k, v, select, q_start), masks, out, (q_lo, q_hi) = _shard_problem(rank, world)
+        # gather every rank's shard: masks [H/world, MB, NB] and outputs [n, H/world, D]
+        mt = torch.from_numpy(masks.astype(np.uint8))
+        ot = torch.from_numpy(out)
+        mg = [torch.empty_like(mt) for _ in range(world)]
+        og = [torch.empty_like(ot) for _ in range(world)]
+        dist.all_gather(mg, mt)
+        dist.all_gather(og, ot)
+        masks_all = torch.cat(mg, 0).numpy().astype(bool)
+        out_all = torch.cat(og, 1).numpy()
+        # the unsharded problem on one rank must give the same masks bit for bit and the same output
+        ref_masks = select(q, k, H, HK)
+        ref_out = O.attention_ref(q, k, v, q_start, ref_masks, q_block=BLOCK, kv_block=BLOCK,
+                                  q_front=q_start % BLOCK)
+        assert np.array_equal(masks_all, ref_masks), 'sharded selection differs from the full problem'
+        assert np.array_equal(out_all, ref_out), 'sharded attention differs from the full problem'
+        # measurement reduction: slowest rank's times, summed work
+        slow, tot = reduce_over_ranks([1.0 + rank, 5.0 - rank], [10.0 * (rank + 1)])
+        assert slow == [float(world), 5.0] and tot == [10.0 * world * (world + 1) / 2], (slow, tot)
+        Path(result_dir, f'ok{rank}').write_text('ok')
+    finally:
+        dist.destroy_process_group()
