@@ -20,6 +20,15 @@ rank owns 8 KV heads (64 query heads) of a problem with 8N KV heads, so per-GPU 
 workload at every N.  `--scaling strong` splits the 8 KV heads of one problem over the N GPUs.
 `--impl reference` times the reference algorithm's CPU restatement (oracle/, numpy) on the host
 cores on a bounded sample of the same workload (rank 0 only).
+
+`--workload` selects the other measured configurations (the default line is the headline):
+  dense      dense causal FP8 attention (tau = 1, no block lists), per-head e4m3 scales, same shape;
+             TFLOPS of the causal FLOPs against the FP8 tensor peak
+  selection  the selection path alone: K-chunk block means into the cache, Q pooling, block
+             selection to CSR lists; GB/s of its algorithmic bytes against the HBM peak
+  chunked    a 262144-token prefill in 32 chunks of 8192 through the drop-in API with the block-mean
+             and scale caches carried across chunks (sink + local window + 16 hot blocks per KV head);
+             TFLOPS on executed blocks over the whole prefill, ms per chunk in `config`
 """
 from __future__ import annotations
 
@@ -272,6 +281,268 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def _rank_env():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', timeout=timedelta(seconds=120), device_id=dev)
+    return world, rank, local, dev
+
+
+def _timed(fn, steps, dev, world, before=None):
+    """Device time (ms) of `steps` calls of fn on the current stream, barrier + synchronize on both sides."""
+    import torch
+    import torch.distributed as dist
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+    barrier()
+    stream = torch.cuda.current_stream(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        if before is not None:
+            before()
+        fn()
+    t1.record(stream)
+    barrier()
+    return t0.elapsed_time(t1)
+
+
+def _kernel_ms(fn, dev, reps=5):
+    """Average device time of one call of fn alone (CUDA events on the launching stream)."""
+    import torch
+    stream = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    a.record(stream)
+    for _ in range(reps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) / reps
+
+
+def _dense(args, h, hk, dev, rank):
+    """Config 3: dense causal FP8 attention, per-head scales, no lists."""
+    import torch
+    from sm120_attn import ops
+    from sm120_attn._native import SA_QUANT_DIV
+    from sm120_attn.kernels import attention_sm120_fp8
+    q, k, v = make_rank_inputs(hk, 2000 + rank, args.strength, dev)
+    scl = [ops.absmax(t, per_head=True).clamp_min_(1e-6) / 448.0 for t in (q, k, v)]
+    q8, k8, v8 = (torch.empty(t.shape, dtype=torch.uint8, device=dev) for t in (q, k, v))
+    for t, s8, sc in zip((q, k, v), (q8, k8, v8), scl):
+        ops.quantize(t, sc, SA_QUANT_DIV, s8)
+    out = torch.empty(N_Q, h, D, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        ops.attn_fp8(q8, k8, v8, out, KV, 0, Q_START, None, None, 64, scl[0], scl[1], scl[2], D ** -0.5)
+    for _ in range(args.warmup):
+        step()
+    ms = _timed(step, args.steps, dev, int(os.environ.get('WORLD_SIZE', '1')))
+    flops = causal_flops(h, D, N_Q, KV)
+    # e2e: the drop-in driver on host tensors (per-tensor scales, quantised on the device)
+    q_h, k_h, v_h = (t.cpu().pin_memory() for t in (q, k, v))
+    o_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    qd, kd, vd = (torch.empty_like(t) for t in (q, k, v))
+
+    def e2e():
+        for d_, h_ in ((qd, q_h), (kd, k_h), (vd, v_h)):
+            d_.copy_(h_, non_blocking=True)
+        attention_sm120_fp8(qd, kd, vd, Q_START, out=out)
+        o_h.copy_(out, non_blocking=True)
+    e2e()
+    e2e_ms = _timed(e2e, args.steps, dev, int(os.environ.get('WORLD_SIZE', '1')))
+    ops.check_status(dev)
+    return {'ms': ms, 'e2e_ms': e2e_ms, 'work': flops, 'unit': 'TFLOPS', 'scale': 1e12,
+            'kernel': 'attn_fwd_kernel<fp8>', 'kernel_ms': ms / args.steps, 'kernel_work': flops,
+            'bound': 'tensor', 'h2d': sum(t.numel() * 2 for t in (q_h, k_h, v_h)), 'd2h': o_h.numel() * 2,
+            'launches': 1,
+            'config': {'workload': f'dense causal FP8 attention (tau 1, no lists): q {N_Q} @ {Q_START} vs {KV} keys, '
+                                   f'H {h}/Hk {hk}/D {D}, per-head e4m3 scales amax/448',
+                       'e2e_path': 'pinned host bf16 q/k/v -> attention_sm120_fp8 (per-tensor scales, 3 host syncs) '
+                                   '-> pinned host output'}}
+
+
+def _selection(args, h, hk, dev, rank):
+    """Config 2: K-chunk block means into the cache, Q pooling, selection to CSR lists."""
+    import torch
+    import sm120_attn.sparse_prefill as ksp
+    from sm120_attn import ops
+    from sm120_attn._native import SA_SELECT_PER_HEAD
+    ksp.BLOCK = BLOCK
+    q, k, _ = make_rank_inputs(hk, 3000 + rank, args.strength, dev)
+    sp = ksp.SparsePrefill(h, hk, D, dev, tau=TAU, min_kv=0, min_q=0, kernel='sm120')
+    layer = 'bench-sel'
+    ksp._KMEAN_CACHE.clear()
+    ksp._cached_block_means(layer, 0, k[:Q_START], 0, Q_START)
+    MB, NB = N_Q // BLOCK, KV // BLOCK
+    counts = torch.empty(h * MB, dtype=torch.int32, device=dev)
+    lists = torch.empty(h * MB, NB, dtype=torch.int32, device=dev)
+    kc = k[Q_START:]
+
+    def rewind():
+        e = ksp._KMEAN_CACHE[(layer, 0)]
+        e['last_kv'] = Q_START
+        e['nb'] = Q_START // BLOCK
+
+    def step(qq=q, kk=kc):
+        km = ksp._cached_block_means(layer, 0, kk, Q_START, KV)
+        qm = sp._pool_q(qq, Q_START, Q_START, MB)
+        ops.select(qm, km, h, hk, NB, Q_START // BLOCK, sp.scale, TAU, SA_SELECT_PER_HEAD, counts=counts, lists=lists)
+    for _ in range(args.warmup):
+        rewind()
+        step()
+    ms = _timed(step, args.steps, dev, int(os.environ.get('WORLD_SIZE', '1')), before=rewind)
+    nnz = int(counts.sum().item())
+    nbytes = 2 * N_Q * h * D + 2 * N_Q * hk * D + 4 * hk * NB * D + 4 * hk * MB * D + 4 * h * MB + 4 * nnz
+    qm = sp._pool_q(q, Q_START, Q_START, MB)
+    km = ksp._KMEAN_CACHE[(layer, 0)]['km'][:, :NB]
+    sel_ms = _kernel_ms(lambda: ops.select(qm, km, h, hk, NB, Q_START // BLOCK, sp.scale, TAU, SA_SELECT_PER_HEAD,
+                                           counts=counts, lists=lists), dev)
+    sel_bytes = 4 * h * MB * D + 4 * hk * NB * D + 4 * h * MB + 4 * nnz
+    q_h, k_h = q.cpu().pin_memory(), kc.cpu().pin_memory()
+    c_h = torch.empty(counts.shape, dtype=counts.dtype).pin_memory()
+    l_h = torch.empty(lists.shape, dtype=lists.dtype).pin_memory()
+    qd, kd = torch.empty_like(q), torch.empty_like(kc)
+
+    def e2e():
+        qd.copy_(q_h, non_blocking=True)
+        kd.copy_(k_h, non_blocking=True)
+        step(qd, kd)
+        c_h.copy_(counts, non_blocking=True)
+        l_h.copy_(lists, non_blocking=True)
+    rewind()
+    e2e()
+    e2e_ms = _timed(e2e, args.steps, dev, int(os.environ.get('WORLD_SIZE', '1')), before=rewind)
+    ops.check_status(dev)
+    return {'ms': ms, 'e2e_ms': e2e_ms, 'work': nbytes, 'unit': 'GB/s', 'scale': 1e9,
+            'kernel': 'select_kernel', 'kernel_ms': sel_ms, 'kernel_work': sel_bytes, 'bound': 'hbm',
+            'h2d': q_h.numel() * 2 + k_h.numel() * 2, 'd2h': c_h.numel() * 4 + l_h.numel() * 4, 'launches': 3,
+            'config': {'workload': f'selection path (configs[1] shape): K-chunk means into the cache, Q pooling, '
+                                   f'per-head selection to CSR; q {N_Q} @ {Q_START} vs {KV} keys, H {h}/Hk {hk}/D {D}, '
+                                   f'block {BLOCK}, tau {TAU}, {args.strength} injection',
+                       'bytes_per_step': nbytes, 'nnz': nnz,
+                       'note': 'value = algorithmic bytes (q + k chunk read, km read/append, CSR write) / time; '
+                               'roofline on select_kernel alone (qm, km, CSR bytes)'}}
+
+
+def _chunked(args, h, hk, dev, rank):
+    """Config 4: 262144-token prefill in 32 chunks of 8192, caches carried across chunks."""
+    import torch
+    import sm120_attn.sparse_prefill as ksp
+    import synth
+    from sm120_attn import ops
+    ksp.BLOCK = BLOCK
+    total, chunk = 262144, 8192
+    q, k, v, _ = synth.make_qkv(total, total, h, hk, D, block=BLOCK, q_start=0, seed=4000 + rank,
+                                strength='strong', hot=16, local=4, device=dev)
+    sp = ksp.SparsePrefill(h, hk, D, dev, tau=TAU, min_kv=8192, min_q=0, kernel='sm120fp8')
+    out = torch.empty(chunk, h, D, dtype=torch.bfloat16, device=dev)
+    layer = 'bench-chunked'
+    stream = torch.cuda.current_stream(dev)
+    per_chunk = []
+
+    def prefill(record=False):
+        ksp._KMEAN_CACHE.clear()
+        ksp._SCALE_CACHE.clear()
+        flops = 0.0
+        for c in range(total // chunk):
+            q0 = c * chunk
+            qc, kc, vc = q[q0:q0 + chunk], k[:q0 + chunk], v[:q0 + chunk]
+            if record:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+            km = ksp._cached_block_means(layer, 0, kc[q0:], q0, q0 + chunk)
+            scales = ksp._cached_scales(layer, 0, qc, kc, vc, q0)
+            sp.forward_sm120fp8(qc, kc, vc, q0, out=out, km=km, scales=scales)
+            if record:
+                b.record(stream)
+                per_chunk.append((a, b, sp.last_counts.sum()))
+    for _ in range(max(1, args.warmup // 3)):
+        prefill()
+    steps = max(1, min(args.steps, 3))
+    ms = _timed(prefill, steps, dev, int(os.environ.get('WORLD_SIZE', '1')))
+    prefill(record=True)
+    torch.cuda.synchronize(dev)
+    chunk_ms = [a.elapsed_time(b) for a, b, _ in per_chunk]
+    kept = [int(n.item()) for _, _, n in per_chunk]
+    exec_flops = sum(n * 4.0 * D * 128 * 128 for n in kept)
+    dense_flops = sum(causal_flops(h, D, chunk, (c + 1) * chunk) for c in range(total // chunk))
+    ops.check_status(dev)
+    return {'ms': ms, 'steps': steps, 'e2e_ms': None, 'work': exec_flops, 'unit': 'TFLOPS', 'scale': 1e12,
+            'kernel': 'attn_fwd_kernel<fp8>', 'kernel_ms': None, 'kernel_work': None, 'bound': 'tensor',
+            'h2d': 0, 'd2h': 0, 'launches': 6 * (total // chunk),
+            'config': {'workload': f'chunked prefill of {total} tokens in {total // chunk} chunks of {chunk} through '
+                                   f'SparsePrefill.forward_sm120fp8, block-mean and scale caches carried; H {h}/Hk {hk}/'
+                                   f'D {D}, block {BLOCK}, tau {TAU}; strong injection: sink + local window (4 blocks) '
+                                   f'+ 16 hot blocks per KV head',
+                       'ms_per_chunk': [round(x, 3) for x in chunk_ms],
+                       'kept_fraction_overall': round(exec_flops / dense_flops, 4),
+                       'value_definition': 'executed-tile FLOPs (4 D 128 128 per kept 128x128 tile) / prefill time'}}
+
+
+def run_other(args):
+    from sm120_attn.shard import kv_head_range, reduce_over_ranks
+    import torch.distributed as dist
+    world, rank, local, dev = _rank_env()
+    if args.scaling == 'strong':
+        try:
+            lo, hi = kv_head_range(rank, world, HK_FULL)
+        except ValueError as e:
+            raise SystemExit(f'strong scaling: {e}')
+        hk = hi - lo
+    else:
+        hk = HK_FULL
+    h = hk * (H_FULL // HK_FULL)
+    clocks = Clocks(local)
+    clocks.start()
+    res = {'dense': _dense, 'selection': _selection, 'chunked': _chunked}[args.workload](args, h, hk, dev, rank)
+    clk = clocks.stop()
+    steps = res.get('steps', args.steps)
+    e2e_ms = res['e2e_ms'] if res['e2e_ms'] is not None else res['ms']
+    kms = res['kernel_ms'] if res['kernel_ms'] is not None else 0.0
+    (ms, e2e_ms, kms), (work,) = reduce_over_ranks([res['ms'], e2e_ms, kms], [res['work']], device=dev)
+    hbm, bf16, how = peaks()
+    value = work * steps / (ms * 1e-3) / res['scale']
+    line = {
+        'metric': METRIC, 'value': round(value, 2), 'unit': res['unit'], 'n_gpus': world, 'steps': steps,
+        'warmup': args.warmup, 'ms_per_step': round(ms / steps, 4), 'higher_is_better': True,
+        'scaling': args.scaling, 'vs_baseline': None,
+        'dtype': 'fp8-e4m3 (fp32 accumulate, bf16 in/out)' if res['unit'] == 'TFLOPS' else 'bf16 in, fp32 scores, int32 CSR',
+        'data': 'synthetic (seeded, BASELINE shapes and injection)', 'config': dict(res['config']),
+    }
+    line['config']['parallelism'] = f'kv-head shards x{world} ({args.scaling}), no collective on the data path'
+    line['config']['l2'] = 'inputs larger than L2; no flush'
+    if res['kernel_work'] is not None and kms > 0:
+        ach = res['kernel_work'] / (kms * 1e-3) / res['scale']
+        peak = 2.0 * bf16 if res['bound'] == 'tensor' else hbm
+        line['roofline'] = {'bound': res['bound'], 'kernel': res['kernel'], 'achieved': round(ach, 1),
+                            'peak': round(peak, 1), 'unit': 'TFLOP/s' if res['bound'] == 'tensor' else 'GB/s',
+                            'frac': round(ach / peak, 4), 'traffic': None,
+                            'peak_source': f'{how} (MEASURED_PEAKS.json)' + (' x2 for e4m3' if res['bound'] == 'tensor' else '')}
+    if res['e2e_ms'] is not None:
+        line['e2e'] = {'value': round(work * steps / (e2e_ms * 1e-3) / res['scale'], 2), 'unit': res['unit'],
+                       'h2d_bytes_per_step': res['h2d'], 'd2h_bytes_per_step': res['d2h'],
+                       'ms_per_step': round(e2e_ms / steps, 4)}
+    line['gpu_launches'] = res['launches'] * steps
+    line['clocks'] = clk
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def cpu_sample(strength, seconds_budget=20.0):
     """Reference algorithm on the host (oracle/, numpy): selection + masked fp32 attention of the
     last `rows` query rows of one KV-head group of the workload; returns (TFLOPS, description, threads)."""
@@ -356,14 +627,17 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--profile-range', action='store_true',
                     help='bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)')
+    ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked'])
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'b200':
         print('note: warmup raised to 3', file=sys.stderr)
         args.warmup = 3
     if args.impl == 'reference':
         run_reference(args)
-    else:
+    elif args.workload == 'chunk':
         run_b200(args)
+    else:
+        run_other(args)
 
 
 if __name__ == '__main__':

@@ -93,11 +93,18 @@ SA_API int sa_block_means_bf16(const void* x, int64_t x_row_stride, int64_t x_he
  * Outputs (any may be NULL): counts[row]; lists[row*list_stride + i] = selected block ids in
  * ascending order for i < counts[row] (entries past counts[row] are not written);
  * masks[row*nb_total + j] = 0/1.
+ * workspace: device scratch of at least sa_select_workspace_bytes(num_heads, MB, nb_total) bytes,
+ * 16-byte aligned (the fp32 logits of every row); its contents on entry do not matter.  head_dim
+ * must be a multiple of 32; qm and km 16-byte aligned with strides that are multiples of 4.
  */
 SA_API int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_head_stride, const float* km,
               int64_t km_head_stride, int64_t km_block_stride, int nb_km, int num_heads, int num_kv_heads,
               int head_dim, int MB, int nb_total, int qblk0, float scale, float tau, int mode, int32_t* counts,
-              int32_t* lists, int64_t list_stride, uint8_t* masks, void* stream);
+              int32_t* lists, int64_t list_stride, uint8_t* masks, void* workspace, size_t workspace_bytes,
+              void* stream);
+
+/* Bytes of workspace sa_select needs for these sizes (0 for invalid sizes). */
+SA_API size_t sa_select_workspace_bytes(int num_heads, int MB, int nb_total);
 
 /* scale modes of sa_quantize_e4m3 */
 #define SA_QUANT_MUL 0           /* e4m3(x * s)            fp32 multiply by s = 1/scale        */

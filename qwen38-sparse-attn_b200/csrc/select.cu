@@ -1,18 +1,23 @@
-// Kernel (b): fused dynamic block selection.
+// Kernel (b): dynamic block selection, two launches over a caller-provided workspace.
 //
-// One CTA per (kv head, q block) - or per (kv head, pair of q blocks) in pair-union mode - scores
-// every causal key block against the pooled queries of all g query heads of that kv head, so each
-// cached key-block mean is read once per CTA.  Then one warp per query head:
-//   softmax over the causal blocks (fp32, like the reference's torch.softmax);
-//   tau selection without a sort: the kept set of the reference - the shortest prefix of the
-//   probabilities sorted in descending order whose float64-accumulated sum, rounded to fp32,
-//   reaches fp32(tau) (sparse_prefill.py:75-77) - is the set of blocks with p > v* plus the
-//   first k ties of value v*, where v* is the largest probability whose "mass of all p >= v*"
-//   reaches tau.  v* is found by bisection on the fp32 bit pattern (probabilities are >= 0, so
-//   integer order is value order) with float64 warp sums; ties are taken in ascending block order.
-// The diagonal and the sink block are forced and future blocks cleared per q block before any
-// union (sparse_prefill.py:78-84, :223), then the row is emitted as counts / ascending lists /
-// optional 0/1 mask.
+// (b1) score_kernel - logits[h*MB + m][j] = (qm[m, h] . km[h / g, j]) * scale for every causal key
+//      block j <= qblk0 + m (sparse_prefill.py:68-74; fp32 like the reference's einsum).  A CTA
+//      computes 64 rows (q block, query head pairs of one kv head) x 128 key blocks; each thread an
+//      8 x 4 register tile; head_dim is staged through shared memory in 32-wide chunks with
+//      cp.async, double buffered, rows padded to 36 floats so that no load conflicts.  Key blocks
+//      at or beyond nb_km are scored as zero vectors (the driver's zero padding,
+//      sparse_prefill.py:219-221).
+// (b2) select_kernel - one warp per output row (per query head or per kv head x q block, or per
+//      query head x pair of q blocks), the logits row in registers (lane l holds blocks l, l+32,..):
+//      softmax over the causal blocks (fp32, like torch.softmax); tau selection without a sort:
+//      the reference keeps the shortest prefix of the probabilities sorted in descending order
+//      whose float64-accumulated sum, rounded to fp32, reaches fp32(tau) (sparse_prefill.py:75-77).
+//      That prefix is {p > v*} plus the first ties of value v* in ascending block order, where v*
+//      is the largest probability whose "mass of all p >= v*" reaches tau; v* is found by
+//      bisection on the fp32 bit pattern (probabilities are >= 0, so integer order is value order)
+//      with float64 sums.  The diagonal and the sink block are forced per q block before any union
+//      (sparse_prefill.py:78-84, :223), then the row is emitted as count / ascending list / 0-1
+//      mask.  Rows longer than 2048 blocks take a shared-memory path with the same arithmetic.
 #include <algorithm>
 
 #include "sa_common.cuh"
@@ -20,8 +25,126 @@
 namespace sa {
 namespace {
 
+// ------------------------------------------------------------------------------------------------
+// (b1) scores
+// ------------------------------------------------------------------------------------------------
+constexpr int SC_ROWS = 64, SC_COLS = 128, SC_DC = 32, SC_PAD = 36, SC_THREADS = 256;
+constexpr int SC_SMEM = 2 * (SC_ROWS + SC_COLS) * SC_PAD * 4;
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(dst), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+__global__ void __launch_bounds__(SC_THREADS, 2) score_kernel(
+    const float* __restrict__ qm, int64_t qbs, int64_t qhs, const float* __restrict__ km, int64_t khs, int64_t kbs,
+    int nb_km, int H, int Hk, int D, int MB, int nb_total, int qblk0, float scale, float* __restrict__ logits,
+    int64_t lrs) {
+    extern __shared__ __align__(16) float sc_smem[];
+    const int g = H / Hk;
+    const int hk = blockIdx.z;
+    const int R = MB * g;                                         // rows of this kv head: r = m*g + i
+    const int r0 = blockIdx.y * SC_ROWS, j0 = blockIdx.x * SC_COLS;
+    const int m_last = min(R - 1, r0 + SC_ROWS - 1) / g;
+    if (j0 > qblk0 + m_last || j0 >= nb_total) return;           // every block of the tile is in the future
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float* sQ = sc_smem;                                          // [2][SC_ROWS][SC_PAD]
+    float* sK = sc_smem + 2 * SC_ROWS * SC_PAD;                   // [2][SC_COLS][SC_PAD]
+
+    // this thread's copies: 2 float4 of the Q tile, 4 of the K tile per chunk
+    const float* qsrc[2];
+    bool qok[2];
+    uint32_t qdst[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int idx = tid + u * SC_THREADS, row = idx >> 3, c4 = idx & 7;
+        const int r = r0 + row;
+        qok[u] = r < R;
+        const int m = qok[u] ? r / g : 0, i = qok[u] ? r - m * g : 0;
+        qsrc[u] = qm + static_cast<int64_t>(m) * qbs + static_cast<int64_t>(hk * g + i) * qhs + c4 * 4;
+        qdst[u] = smem_u32(sQ + row * SC_PAD + c4 * 4);
+    }
+    const float* ksrc[4];
+    bool kok[4];
+    uint32_t kdst[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int idx = tid + u * SC_THREADS, col = idx >> 3, c4 = idx & 7;
+        const int j = j0 + col;
+        kok[u] = j < nb_km && j < nb_total;
+        ksrc[u] = km + static_cast<int64_t>(hk) * khs + static_cast<int64_t>(kok[u] ? j : 0) * kbs + c4 * 4;
+        kdst[u] = smem_u32(sK + col * SC_PAD + c4 * 4);
+    }
+    auto load_chunk = [&](int buf, int d0) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+            cp_async16(qdst[u] + buf * SC_ROWS * SC_PAD * 4, qok[u] ? qsrc[u] + d0 : qm, qok[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            cp_async16(kdst[u] + buf * SC_COLS * SC_PAD * 4, kok[u] ? ksrc[u] + d0 : km, kok[u]);
+        cp_async_commit();
+    };
+
+    float acc[8][4];
+#pragma unroll
+    for (int a = 0; a < 8; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+    const int nch = D / SC_DC;
+    load_chunk(0, 0);
+    for (int ch = 0; ch < nch; ++ch) {
+        if (ch + 1 < nch) {
+            load_chunk((ch + 1) & 1, (ch + 1) * SC_DC);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float* q = sQ + (ch & 1) * SC_ROWS * SC_PAD + warp * 8 * SC_PAD;     // rows 8w.. (broadcast)
+        const float* k = sK + (ch & 1) * SC_COLS * SC_PAD + lane * SC_PAD;          // cols lane + 32c
+#pragma unroll
+        for (int dd = 0; dd < SC_DC; dd += 4) {
+            float4 qa[8], kb[4];
+#pragma unroll
+            for (int a = 0; a < 8; ++a) qa[a] = *reinterpret_cast<const float4*>(q + a * SC_PAD + dd);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) kb[c] = *reinterpret_cast<const float4*>(k + c * 32 * SC_PAD + dd);
+#pragma unroll
+            for (int a = 0; a < 8; ++a)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    acc[a][c] = fmaf(qa[a].x, kb[c].x, acc[a][c]);
+                    acc[a][c] = fmaf(qa[a].y, kb[c].y, acc[a][c]);
+                    acc[a][c] = fmaf(qa[a].z, kb[c].z, acc[a][c]);
+                    acc[a][c] = fmaf(qa[a].w, kb[c].w, acc[a][c]);
+                }
+        }
+        __syncthreads();                                          // buffer ch&1 is refilled at ch+2
+    }
+#pragma unroll
+    for (int a = 0; a < 8; ++a) {
+        const int r = r0 + warp * 8 + a;
+        if (r >= R) break;
+        const int m = r / g, i = r - m * g;
+        float* out = logits + static_cast<int64_t>((hk * g + i) * MB + m) * lrs;
+        const int lim = min(nb_total - 1, qblk0 + m);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int j = j0 + lane + 32 * c;
+            if (j <= lim) out[j] = acc[a][c] * scale;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// (b2) selection
+// ------------------------------------------------------------------------------------------------
 constexpr int SEL_WARPS = 8;
 constexpr int SEL_THREADS = SEL_WARPS * 32;
+constexpr int SEL_MAX_NPL = 64;                                   // register rows up to 2048 blocks
 
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -44,9 +167,106 @@ __device__ __forceinline__ int warp_sum_i(int v) {
     return v;
 }
 
-// Selects blocks of one (head, q block) row in place: L[0..nbc) holds logits on entry and the
-// probabilities afterwards; the selection is OR-ed into bits[].
-__device__ void select_row(float* L, int nbc, float tau_f, uint32_t* bits, int lane) {
+// Number of ties (in ascending block order) that must be kept: ties of value vstar are added to
+// `above` one at a time until the fp32-rounded float64 mass reaches tau.
+__device__ __forceinline__ int ties_needed(double above, float vstar, int ties, float tau_f) {
+    int kt = ties;
+    double acc = above;
+    for (int k = 1; k <= ties; ++k) {
+        acc += static_cast<double>(vstar);
+        if (static_cast<float>(acc) >= tau_f) { kt = k; break; }
+    }
+    return kt;
+}
+
+// Register path: selects within one row of nbc <= 32*NPL blocks; returns the kept flags of this
+// lane's blocks (bit c <-> block lane + 32c).
+template <int NPL>
+__device__ uint64_t select_row_regs(const float* __restrict__ L, int nbc, float tau_f, int lane) {
+    constexpr bool PRE = NPL <= 16;                               // keep float64 copies in registers
+    float p[NPL];
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const int j = lane + 32 * c;
+        p[c] = j < nbc ? __ldg(L + j) : -INFINITY;
+    }
+    float mx = p[0];
+#pragma unroll
+    for (int c = 1; c < NPL; ++c) mx = fmaxf(mx, p[c]);
+    mx = warp_max_f(mx);
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        p[c] = (lane + 32 * c < nbc) ? expf(p[c] - mx) : 0.f;
+        s += p[c];
+    }
+    s = warp_sum_f(s);
+    double pd[PRE ? NPL : 1];
+    double t0 = 0.0, t1 = 0.0;
+    float pmax = 0.f;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const bool valid = lane + 32 * c < nbc;
+        p[c] = valid ? __fdiv_rn(p[c], s) : -1.f;                 // -1: not a block of this row
+        const double d = valid ? static_cast<double>(p[c]) : 0.0;
+        if constexpr (PRE) pd[c] = d;
+        if (c & 1) t1 += d; else t0 += d;
+        pmax = fmaxf(pmax, p[c]);
+    }
+    const double tot = warp_sum_d(t0 + t1);
+    uint64_t keep = 0;
+    if (!(static_cast<float>(tot) >= tau_f)) {                   // tau never reached: every causal block
+#pragma unroll
+        for (int c = 0; c < NPL; ++c)
+            if (lane + 32 * c < nbc) keep |= 1ull << c;
+        return keep;
+    }
+    // largest v (bit pattern) with fp32(sum_{p >= v} p) >= tau: pred(lo) true, pred(hi) false;
+    // v* <= max p, so the search starts below max p's successor
+    uint32_t lo = 0u, hi = __float_as_uint(warp_max_f(pmax)) + 1u;
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + ((hi - lo) >> 1);
+        const float v = __uint_as_float(mid);
+        double m0 = 0.0, m1 = 0.0, m2 = 0.0, m3 = 0.0;
+#pragma unroll
+        for (int c = 0; c < NPL; ++c) {
+            double d;
+            if constexpr (PRE) d = (p[c] >= v) ? pd[c] : 0.0;
+            else d = (p[c] >= v) ? static_cast<double>(p[c]) : 0.0;
+            if ((c & 3) == 0) m0 += d;
+            else if ((c & 3) == 1) m1 += d;
+            else if ((c & 3) == 2) m2 += d;
+            else m3 += d;
+        }
+        const double m = warp_sum_d((m0 + m1) + (m2 + m3));
+        if (static_cast<float>(m) >= tau_f) lo = mid; else hi = mid;
+    }
+    const float vstar = __uint_as_float(lo);
+    double above = 0.0;
+    int ties = 0;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        above += p[c] > vstar ? static_cast<double>(p[c]) : 0.0;
+        ties += (p[c] == vstar);
+    }
+    above = warp_sum_d(above);
+    ties = warp_sum_i(ties);
+    const int kt = ties_needed(above, vstar, ties, tau_f);
+    int seen = 0;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const bool tie = p[c] == vstar;
+        const uint32_t tb = __ballot_sync(0xffffffffu, tie);
+        const int rank = seen + __popc(tb & ((1u << lane) - 1u));
+        if (p[c] > vstar || (tie && rank < kt)) keep |= 1ull << c;
+        seen += __popc(tb);
+    }
+    return keep;
+}
+
+// Shared-memory path for rows longer than 32*SEL_MAX_NPL blocks: L (the workspace row) is
+// overwritten with the probabilities; the selection is OR-ed into bits[] (shared memory).
+__device__ void select_row_smem(float* L, int nbc, float tau_f, uint32_t* bits, int lane) {
     float mx = -INFINITY;
     for (int j = lane; j < nbc; j += 32) mx = fmaxf(mx, L[j]);
     mx = warp_max_f(mx);
@@ -58,19 +278,20 @@ __device__ void select_row(float* L, int nbc, float tau_f, uint32_t* bits, int l
     }
     s = warp_sum_f(s);
     double tot = 0.0;
+    float pmax = 0.f;
     for (int j = lane; j < nbc; j += 32) {
         const float p = __fdiv_rn(L[j], s);
         L[j] = p;
         tot += static_cast<double>(p);
+        pmax = fmaxf(pmax, p);
     }
     tot = warp_sum_d(tot);
     __syncwarp();
-    if (!(static_cast<float>(tot) >= tau_f)) {          // tau never reached: keep every causal block
+    if (!(static_cast<float>(tot) >= tau_f)) {
         for (int j = lane; j < nbc; j += 32) atomicOr(&bits[j >> 5], 1u << (j & 31));
         return;
     }
-    // largest v (bit pattern) with fp32(sum_{p >= v} p) >= tau: pred(lo) true, pred(hi) false
-    uint32_t lo = 0u, hi = 0x3F800001u;
+    uint32_t lo = 0u, hi = __float_as_uint(warp_max_f(pmax)) + 1u;
     while (hi - lo > 1u) {
         const uint32_t mid = lo + ((hi - lo) >> 1);
         const float v = __uint_as_float(mid);
@@ -92,12 +313,7 @@ __device__ void select_row(float* L, int nbc, float tau_f, uint32_t* bits, int l
     }
     above = warp_sum_d(above);
     ties = warp_sum_i(ties);
-    int kt = ties;                                        // ties needed to cross tau (ascending block order)
-    double acc = above;
-    for (int k = 1; k <= ties; ++k) {
-        acc += static_cast<double>(vstar);
-        if (static_cast<float>(acc) >= tau_f) { kt = k; break; }
-    }
+    const int kt = ties_needed(above, vstar, ties, tau_f);
     int seen = 0;
     for (int base = 0; base < nbc; base += 32) {
         const int j = base + lane;
@@ -112,204 +328,177 @@ __device__ void select_row(float* L, int nbc, float tau_f, uint32_t* bits, int l
     }
 }
 
-// Register-resident variant of select_row for rows of at most 32*NPL blocks: lane l holds blocks
-// l, l+32, ...; identical arithmetic (fp32 softmax, float64 sums, bisection, tie order).
-template <int NPL>
-__device__ void select_row_regs(const float* L, int nbc, float tau_f, uint32_t* bits, int lane) {
-    float p[NPL];
-#pragma unroll
-    for (int c = 0; c < NPL; ++c) {
-        const int j = lane + 32 * c;
-        p[c] = j < nbc ? L[j] : -INFINITY;
-    }
-    float mx = p[0];
-#pragma unroll
-    for (int c = 1; c < NPL; ++c) mx = fmaxf(mx, p[c]);
-    mx = warp_max_f(mx);
-    float s = 0.f;
-#pragma unroll
-    for (int c = 0; c < NPL; ++c) {
-        p[c] = (lane + 32 * c < nbc) ? expf(p[c] - mx) : 0.f;
-        s += p[c];
-    }
-    s = warp_sum_f(s);
-    double tot = 0.0;
-#pragma unroll
-    for (int c = 0; c < NPL; ++c) {
-        p[c] = (lane + 32 * c < nbc) ? __fdiv_rn(p[c], s) : -1.f;   // -1: not a block of this row
-        tot += p[c] > 0.f ? static_cast<double>(p[c]) : 0.0;
-    }
-    tot = warp_sum_d(tot);
-    if (!(static_cast<float>(tot) >= tau_f)) {
-#pragma unroll
-        for (int c = 0; c < NPL; ++c) {
-            const uint32_t b = __ballot_sync(0xffffffffu, lane + 32 * c < nbc);
-            if (lane == 0 && b) atomicOr(&bits[c], b);
-        }
-        return;
-    }
-    uint32_t lo = 0u, hi = 0x3F800001u;
-    while (hi - lo > 1u) {
-        const uint32_t mid = lo + ((hi - lo) >> 1);
-        const float v = __uint_as_float(mid);
-        double m = 0.0;
-#pragma unroll
-        for (int c = 0; c < NPL; ++c) m += p[c] >= v ? static_cast<double>(p[c]) : 0.0;
-        m = warp_sum_d(m);
-        if (static_cast<float>(m) >= tau_f) lo = mid; else hi = mid;
-    }
-    const float vstar = __uint_as_float(lo);
-    double above = 0.0;
-    int ties = 0;
-#pragma unroll
-    for (int c = 0; c < NPL; ++c) {
-        above += p[c] > vstar ? static_cast<double>(p[c]) : 0.0;
-        ties += (p[c] == vstar);
-    }
-    above = warp_sum_d(above);
-    ties = warp_sum_i(ties);
-    int kt = ties;
-    double acc = above;
-    for (int k = 1; k <= ties; ++k) {
-        acc += static_cast<double>(vstar);
-        if (static_cast<float>(acc) >= tau_f) { kt = k; break; }
-    }
-    int seen = 0;
-#pragma unroll
-    for (int c = 0; c < NPL; ++c) {
-        const bool tie = p[c] == vstar;
-        const uint32_t tb = __ballot_sync(0xffffffffu, tie);
-        const int rank = seen + __popc(tb & ((1u << lane) - 1u));
-        const bool keep = p[c] > vstar || (tie && rank < kt);
-        const uint32_t kb = __ballot_sync(0xffffffffu, keep);
-        if (lane == 0 && kb) atomicOr(&bits[c], kb);
-        seen += __popc(tb);
+struct SelArgs {
+    float* logits;
+    int64_t lrs;
+    int H, Hk, MB, nb_total, qblk0, mode;
+    float tau_f;
+    int32_t* counts;
+    int32_t* lists;
+    int64_t list_stride;
+    uint8_t* masks;
+};
+
+// Output unit -> its first logits row (h0, m0) and the number of rows OR-ed into it: PER_HEAD one
+// row; PAIR_UNION rows (h0, m0), (h0, m0 + 1); KV_UNION rows (h0 + i, m0) for the g heads.
+__device__ __forceinline__ void unit_rows(const SelArgs& a, int unit, int& h0, int& m0, int& nrows) {
+    const int g = a.H / a.Hk;
+    if (a.mode == SA_SELECT_PER_HEAD) {
+        h0 = unit / a.MB; m0 = unit - h0 * a.MB; nrows = 1;
+    } else if (a.mode == SA_SELECT_PAIR_UNION) {
+        const int half = a.MB / 2;
+        h0 = unit / half; m0 = 2 * (unit - h0 * half); nrows = 2;
+    } else {
+        const int hk = unit / a.MB;
+        m0 = unit - hk * a.MB; h0 = hk * g; nrows = g;
     }
 }
 
-__global__ void __launch_bounds__(SEL_THREADS) select_kernel(
-    const float* __restrict__ qm, int64_t qbs, int64_t qhs, const float* __restrict__ km, int64_t khs, int64_t kbs,
-    int nb_km, int H, int Hk, int D, int MB, int nb_total, int qblk0, float scale, float tau_f, int mode,
-    int32_t* __restrict__ counts, int32_t* __restrict__ lists, int64_t list_stride, uint8_t* __restrict__ masks,
-    int nbw) {
-    extern __shared__ __align__(16) float sm[];
-    const int g = H / Hk;
-    const int hk = blockIdx.y, unit = blockIdx.x;
+template <int NPL>
+__global__ void __launch_bounds__(SEL_THREADS) select_kernel(const SelArgs a, int units) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nbp = nbw * 32;
-    float* qv = sm;                                       // [g][D]
-    float* logit = qv + g * D;                            // [g][nbp]
-    uint32_t* bits = reinterpret_cast<uint32_t*>(logit + static_cast<size_t>(g) * nbp);   // [g][nbw]
-    for (int i = threadIdx.x; i < g * nbw; i += SEL_THREADS) bits[i] = 0u;
-    const int nsub = (mode == SA_SELECT_PAIR_UNION) ? 2 : 1;
-    for (int sub = 0; sub < nsub; ++sub) {
-        const int m = (mode == SA_SELECT_PAIR_UNION) ? 2 * unit + sub : unit;
-        const int gi = qblk0 + m;
-        const int nbc = min(gi + 1, nb_total);
-        __syncthreads();
-        for (int i = threadIdx.x; i < g * D; i += SEL_THREADS) {
-            const int hh = i / D, d = i - hh * D;
-            qv[i] = qm[static_cast<int64_t>(m) * qbs + static_cast<int64_t>(hk * g + hh) * qhs + d];
-        }
-        __syncthreads();
-        // scores: one thread per key block, all g heads at once (km row read with 16-byte loads)
-        for (int j = threadIdx.x; j < nbc; j += SEL_THREADS) {
-            float acc[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-            if (j < nb_km) {
-                const float* kr = km + static_cast<int64_t>(hk) * khs + static_cast<int64_t>(j) * kbs;
-                for (int d = 0; d < D; d += 4) {
-                    const float4 kv = *reinterpret_cast<const float4*>(kr + d);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        if (i < g) {
-                            const float* q = qv + i * D + d;
-                            acc[i] = fmaf(q[0], kv.x, acc[i]);
-                            acc[i] = fmaf(q[1], kv.y, acc[i]);
-                            acc[i] = fmaf(q[2], kv.z, acc[i]);
-                            acc[i] = fmaf(q[3], kv.w, acc[i]);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-                if (i < g) logit[i * nbp + j] = acc[i] * scale;
-        }
-        __syncthreads();
-        for (int i = warp; i < g; i += SEL_WARPS) {
-            float* L = logit + static_cast<size_t>(i) * nbp;
-            if (nbc <= 128) select_row_regs<4>(L, nbc, tau_f, bits + i * nbw, lane);
-            else if (nbc <= 512) select_row_regs<16>(L, nbc, tau_f, bits + i * nbw, lane);
-            else select_row(L, nbc, tau_f, bits + i * nbw, lane);
-            __syncwarp();
-            if (lane == 0) {
-                if (gi < nb_total) atomicOr(&bits[i * nbw + (gi >> 5)], 1u << (gi & 31));   // diagonal
-                atomicOr(&bits[i * nbw], 1u);                                                 // sink
-            }
-        }
+    const int unit = blockIdx.x * SEL_WARPS + warp;
+    if (unit >= units) return;
+    int h0, m0, nrows;
+    unit_rows(a, unit, h0, m0, nrows);
+    uint64_t keep = 0;
+    for (int k = 0; k < nrows; ++k) {
+        const int h = a.mode == SA_SELECT_KV_UNION ? h0 + k : h0;
+        const int m = a.mode == SA_SELECT_PAIR_UNION ? m0 + k : m0;
+        const int gi = a.qblk0 + m;
+        const int nbc = min(gi + 1, a.nb_total);
+        uint64_t kr = select_row_regs<NPL>(a.logits + static_cast<int64_t>(h * a.MB + m) * a.lrs, nbc, a.tau_f, lane);
+        if (gi < a.nb_total && (gi & 31) == lane) kr |= 1ull << (gi >> 5);     // diagonal
+        if (lane == 0) kr |= 1ull;                                             // sink
+        keep |= kr;
     }
-    __syncthreads();
-    // emit rows
-    const int nrows_here = (mode == SA_SELECT_KV_UNION) ? 1 : g;
-    for (int i = warp; i < nrows_here; i += SEL_WARPS) {
-        int64_t row;
-        if (mode == SA_SELECT_PER_HEAD) row = static_cast<int64_t>(hk * g + i) * MB + unit;
-        else if (mode == SA_SELECT_PAIR_UNION) row = static_cast<int64_t>(hk * g + i) * (MB / 2) + unit;
-        else row = static_cast<int64_t>(hk) * MB + unit;
-        int total = 0;
-        for (int w = 0; w < nbw; ++w) {
-            uint32_t word;
-            if (mode == SA_SELECT_KV_UNION) {
-                word = 0u;
-                for (int hh = 0; hh < g; ++hh) word |= bits[hh * nbw + w];
-            } else {
-                word = bits[i * nbw + w];
-            }
-            const int j = w * 32 + lane;
-            const bool on = (word >> lane) & 1u;
-            if (lists && on) lists[row * list_stride + total + __popc(word & ((1u << lane) - 1u))] = j;
-            if (masks && j < nb_total) masks[row * nb_total + j] = on ? 1 : 0;
-            total += __popc(word);
-        }
-        if (counts && lane == 0) counts[row] = total;
+    int total = 0;
+    const int nbw = (a.nb_total + 31) >> 5;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        if (c >= nbw) break;
+        const bool on = (keep >> c) & 1ull;
+        const uint32_t word = __ballot_sync(0xffffffffu, on);
+        const int j = 32 * c + lane;
+        if (a.lists && on)
+            a.lists[static_cast<int64_t>(unit) * a.list_stride + total + __popc(word & ((1u << lane) - 1u))] = j;
+        if (a.masks && j < a.nb_total) a.masks[static_cast<int64_t>(unit) * a.nb_total + j] = on ? 1 : 0;
+        total += __popc(word);
     }
+    if (a.counts && lane == 0) a.counts[unit] = total;
 }
+
+// Long rows: per-warp bit rows in shared memory ([SEL_WARPS][nbw] words).
+__global__ void __launch_bounds__(SEL_THREADS) select_kernel_long(const SelArgs a, int units, int nbw) {
+    extern __shared__ uint32_t sel_bits[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int unit = blockIdx.x * SEL_WARPS + warp;
+    if (unit >= units) return;
+    uint32_t* bits = sel_bits + warp * nbw;
+    for (int w = lane; w < nbw; w += 32) bits[w] = 0u;
+    __syncwarp();
+    int h0, m0, nrows;
+    unit_rows(a, unit, h0, m0, nrows);
+    for (int k = 0; k < nrows; ++k) {
+        const int h = a.mode == SA_SELECT_KV_UNION ? h0 + k : h0;
+        const int m = a.mode == SA_SELECT_PAIR_UNION ? m0 + k : m0;
+        const int gi = a.qblk0 + m;
+        const int nbc = min(gi + 1, a.nb_total);
+        select_row_smem(a.logits + static_cast<int64_t>(h * a.MB + m) * a.lrs, nbc, a.tau_f, bits, lane);
+        __syncwarp();
+        if (lane == 0) {
+            if (gi < a.nb_total) atomicOr(&bits[gi >> 5], 1u << (gi & 31));
+            atomicOr(&bits[0], 1u);
+        }
+        __syncwarp();
+    }
+    int total = 0;
+    for (int w = 0; w < nbw; ++w) {
+        const uint32_t word = bits[w];
+        const int j = w * 32 + lane;
+        const bool on = (word >> lane) & 1u;
+        if (a.lists && on)
+            a.lists[static_cast<int64_t>(unit) * a.list_stride + total + __popc(word & ((1u << lane) - 1u))] = j;
+        if (a.masks && j < a.nb_total) a.masks[static_cast<int64_t>(unit) * a.nb_total + j] = on ? 1 : 0;
+        total += __popc(word);
+    }
+    if (a.counts && lane == 0) a.counts[unit] = total;
+}
+
+int64_t logits_row_stride(int nb_total) { return (static_cast<int64_t>(nb_total) + 31) / 32 * 32; }
 
 }  // namespace
 }  // namespace sa
 
 using namespace sa;
 
+extern "C" size_t sa_select_workspace_bytes(int num_heads, int MB, int nb_total) {
+    if (num_heads <= 0 || MB <= 0 || nb_total <= 0) return 0;
+    return static_cast<size_t>(num_heads) * MB * logits_row_stride(nb_total) * sizeof(float);
+}
+
 extern "C" int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_head_stride, const float* km,
                          int64_t km_head_stride, int64_t km_block_stride, int nb_km, int num_heads, int num_kv_heads,
                          int head_dim, int MB, int nb_total, int qblk0, float scale, float tau, int mode,
-                         int32_t* counts, int32_t* lists, int64_t list_stride, uint8_t* masks, void* stream) {
+                         int32_t* counts, int32_t* lists, int64_t list_stride, uint8_t* masks, void* workspace,
+                         size_t workspace_bytes, void* stream) {
     if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || MB <= 0 || nb_total <= 0 || qblk0 < 0 ||
         nb_km < 0)
         return fail(SA_ERR_ARG, "sa_select: bad sizes");
     const int g = num_heads / num_kv_heads;
-    if (g > 16) return fail(SA_ERR_UNSUPPORTED, "sa_select: more than 16 query heads per kv head");
-    if (head_dim % 4 || head_dim <= 0) return fail(SA_ERR_UNSUPPORTED, "sa_select: head_dim %% 4");
+    if (head_dim <= 0 || head_dim % SC_DC) return fail(SA_ERR_UNSUPPORTED, "sa_select: head_dim %% %d", SC_DC);
     if (!qm || (!km && nb_km > 0)) return fail(SA_ERR_ARG, "sa_select: null pointer");
-    if ((reinterpret_cast<uintptr_t>(km) & 15) || km_block_stride % 4 || km_head_stride % 4)
-        return fail(SA_ERR_ALIGN, "sa_select: km must be 16-byte aligned with strides %% 4 == 0");
-    if (mode == SA_SELECT_PAIR_UNION && (MB % 2)) return fail(SA_ERR_ARG, "sa_select: pair union needs even MB");
+    if ((reinterpret_cast<uintptr_t>(km) & 15) || km_block_stride % 4 || km_head_stride % 4 ||
+        (reinterpret_cast<uintptr_t>(qm) & 15) || qm_block_stride % 4 || qm_head_stride % 4)
+        return fail(SA_ERR_ALIGN, "sa_select: qm and km must be 16-byte aligned with strides %% 4 == 0");
     if (mode < 0 || mode > 2) return fail(SA_ERR_ARG, "sa_select: bad mode");
+    if (mode == SA_SELECT_PAIR_UNION && (MB % 2)) return fail(SA_ERR_ARG, "sa_select: pair union needs even MB");
     if (lists && list_stride < nb_total) return fail(SA_ERR_ARG, "sa_select: list_stride < nb_total");
-    const int nbw = (nb_total + 31) / 32;
-    const size_t smem = (static_cast<size_t>(g) * head_dim + static_cast<size_t>(g) * nbw * 32) * sizeof(float) +
-                        static_cast<size_t>(g) * nbw * sizeof(uint32_t);
-    if (smem > 227 * 1024) return fail(SA_ERR_UNSUPPORTED, "sa_select: %d key blocks need %zu B of shared memory", nb_total, smem);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return fail(SA_ERR_CUDA, "sa_select: %s", cudaGetErrorString(e));
+    const size_t need = sa_select_workspace_bytes(num_heads, MB, nb_total);
+    if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
+        return fail(SA_ERR_ARG, "sa_select: workspace of %zu bytes (16-byte aligned) needed", need);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* L = static_cast<float*>(workspace);
+    const int64_t lrs = logits_row_stride(nb_total);
+
+    cudaError_t e = cudaSuccess;
+    {
+        static bool smem_set[64] = {};                            // once per device (idempotent)
+        int dev = 0;
+        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return fail(SA_ERR_CUDA, "sa_select: %s", cudaGetErrorString(e));
+        if (dev >= 64 || !smem_set[dev]) {
+            e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM);
+            if (e != cudaSuccess) return fail(SA_ERR_CUDA, "sa_select: %s", cudaGetErrorString(e));
+            if (dev < 64) smem_set[dev] = true;
+        }
     }
-    const int units = (mode == SA_SELECT_PAIR_UNION) ? MB / 2 : MB;
-    dim3 grid(units, num_kv_heads);
-    select_kernel<<<grid, SEL_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
-        qm, qm_block_stride, qm_head_stride, km, km_head_stride, km_block_stride, nb_km, num_heads, num_kv_heads,
-        head_dim, MB, nb_total, qblk0, scale, static_cast<float>(tau), mode, counts, lists, list_stride, masks, nbw);
+    dim3 sgrid((nb_total + SC_COLS - 1) / SC_COLS, (MB * g + SC_ROWS - 1) / SC_ROWS, num_kv_heads);
+    score_kernel<<<sgrid, SC_THREADS, SC_SMEM, s>>>(qm, qm_block_stride, qm_head_stride, km, km_head_stride,
+                                                   km_block_stride, nb_km, num_heads, num_kv_heads, head_dim, MB,
+                                                   nb_total, qblk0, scale, L, lrs);
+    int rc = check_launch("score_kernel");
+    if (rc) return rc;
+
+    const SelArgs a{L, lrs, num_heads, num_kv_heads, MB, nb_total, qblk0, mode, static_cast<float>(tau),
+                    counts, lists, list_stride, masks};
+    const int units = (mode == SA_SELECT_PER_HEAD) ? num_heads * MB
+                    : (mode == SA_SELECT_PAIR_UNION) ? num_heads * (MB / 2) : num_kv_heads * MB;
+    const int blocks = (units + SEL_WARPS - 1) / SEL_WARPS;
+    const int npl = (nb_total + 31) / 32;
+    if (npl <= 4) select_kernel<4><<<blocks, SEL_THREADS, 0, s>>>(a, units);
+    else if (npl <= 8) select_kernel<8><<<blocks, SEL_THREADS, 0, s>>>(a, units);
+    else if (npl <= 16) select_kernel<16><<<blocks, SEL_THREADS, 0, s>>>(a, units);
+    else if (npl <= 32) select_kernel<32><<<blocks, SEL_THREADS, 0, s>>>(a, units);
+    else if (npl <= SEL_MAX_NPL) select_kernel<SEL_MAX_NPL><<<blocks, SEL_THREADS, 0, s>>>(a, units);
+    else {
+        const size_t smem = static_cast<size_t>(SEL_WARPS) * npl * sizeof(uint32_t);
+        if (smem > 227 * 1024) return fail(SA_ERR_UNSUPPORTED, "sa_select: %d key blocks", nb_total);
+        if (smem > 48 * 1024) {
+            e = cudaFuncSetAttribute(select_kernel_long, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e != cudaSuccess) return fail(SA_ERR_CUDA, "sa_select: %s", cudaGetErrorString(e));
+        }
+        select_kernel_long<<<blocks, SEL_THREADS, smem, s>>>(a, units, npl);
+    }
     return check_launch("select_kernel");
 }

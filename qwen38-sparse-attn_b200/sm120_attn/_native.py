@@ -18,16 +18,17 @@ SA_DEV_WAIT_Q, SA_DEV_WAIT_KV, SA_DEV_WAIT_S, SA_DEV_WAIT_P, SA_DEV_WAIT_O, SA_D
 SA_SELECT_PER_HEAD, SA_SELECT_KV_UNION, SA_SELECT_PAIR_UNION = 0, 1, 2
 SA_QUANT_MUL, SA_QUANT_MUL_BF16, SA_QUANT_DIV = 0, 1, 2
 
-_i32, _i64, _f32, _p = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+_i32, _i64, _f32, _p, _sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 
-# name -> argument types (return type is int for all but sa_last_error)
+# name -> argument types (return type is int for all but sa_last_error and the size queries)
 SIGNATURES = {
     'sa_version': [],
     'sa_read_status': [_p, _p, _p],
     'sa_block_means_bf16': [_p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _p, _i64, _i64, _i32, _p, _i64, _i64, _p,
                             _i32, _i32, _p],
     'sa_select': [_p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _f32, _i32, _p, _p,
-                  _i64, _p, _p],
+                  _i64, _p, _p, _sz, _p],
+    'sa_select_workspace_bytes': [_i32, _i32, _i32],
     'sa_quantize_e4m3': [_p, _i64, _i64, _i32, _i32, _i32, _p, _i32, _i32, _p, _i64, _i64, _i32, _i32, _p],
     'sa_absmax_bf16': [_p, _i64, _i64, _i32, _i32, _i32, _i32, _p, _p],
     'sa_attn_fwd_fp8': [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32,
@@ -35,6 +36,10 @@ SIGNATURES = {
     'sa_attn_fwd_bf16': [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32,
                          _i32, _i32, _p, _p, _i64, _i32, _i32, _f32, _p, _p],
 }
+
+
+# entry points that return a size instead of a status code
+SIZE_QUERIES = {'sa_select_workspace_bytes': _sz}
 
 
 class NativeLibraryError(RuntimeError):
@@ -63,7 +68,7 @@ def lib():
         for name, args in SIGNATURES.items():
             f = getattr(L, name)
             f.argtypes = args
-            f.restype = ctypes.c_int
+            f.restype = SIZE_QUERIES.get(name, ctypes.c_int)
         L.sa_last_error.argtypes = []
         L.sa_last_error.restype = ctypes.c_char_p
         _LIB = L

@@ -68,15 +68,27 @@ def block_means(x, pos0: int, block: int, out, out_block0: int, q8=None, inv_sca
            q8.stride(1) if q8 is not None else 0, _p(inv_scale), iss, int(fixed_divisor), _stream(x.device))
 
 
+def select_workspace_bytes(num_heads: int, MB: int, nb_total: int) -> int:
+    return int(N.lib().sa_select_workspace_bytes(num_heads, MB, nb_total))
+
+
 def select(qm, km, num_heads: int, num_kv_heads: int, nb_total: int, qblk0: int, scale: float, tau: float,
-           mode: int, counts=None, lists=None, masks=None):
-    """Block selection (see sa_select).  qm [MB, H, D] fp32, km [Hk, NBk, D] fp32."""
+           mode: int, counts=None, lists=None, masks=None, workspace=None):
+    """Block selection (see sa_select).  qm [MB, H, D] fp32, km [Hk, NBk, D] fp32.
+
+    workspace: optional uint8 device tensor of at least select_workspace_bytes(...) bytes; by
+    default one is taken from torch's caching allocator for the call."""
     _need_cuda('select', qm, km, counts, lists, masks)
     assert qm.dtype == torch.float32 and km.dtype == torch.float32 and qm.stride(2) == 1 and km.stride(2) == 1
     MB, H, D = qm.shape
+    need = select_workspace_bytes(num_heads, MB, nb_total)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=qm.device)
+    _need_cuda('select', workspace)
     N.call('sa_select', _p(qm), qm.stride(0), qm.stride(1), _p(km), km.stride(0), km.stride(1), km.shape[1],
            num_heads, num_kv_heads, D, MB, nb_total, qblk0, float(scale), float(tau), mode, _p(counts), _p(lists),
-           lists.stride(0) if lists is not None else 0, _p(masks), _stream(qm.device))
+           lists.stride(0) if lists is not None else 0, _p(masks), _p(workspace), workspace.numel(),
+           _stream(qm.device))
 
 
 def quantize(x, scale, mode: int, out, transpose: bool = False, rows_pad: int = 0):

@@ -14,7 +14,7 @@ ROOT = Path(__file__).resolve().parent.parent
 def declared_symbols():
     names = set()
     for h in (ROOT / 'include').glob('*.h'):
-        names |= set(re.findall(r'^SA_API\s+(?:const\s+char\s*\*|int)\s+(sa_\w+)\s*\(', h.read_text(), flags=re.M))
+        names |= set(re.findall(r'^SA_API\s+(?:const\s+char\s*\*|int|size_t)\s+(sa_\w+)\s*\(', h.read_text(), flags=re.M))
     return names
 
 
@@ -30,7 +30,8 @@ def test_library_exports_every_declared_symbol():
 
 
 @pytest.mark.parametrize('call,code', [
-    (lambda L: L.sa_select(None, 0, 0, None, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0.0, 0.0, 0, None, None, 0, None, None), -1),
+    (lambda L: L.sa_select(None, 0, 0, None, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0.0, 0.0, 0, None, None, 0, None, None, 0,
+                           None), -1),
     (lambda L: L.sa_block_means_bf16(None, 0, 0, 10, 2, 100, 0, 64, None, 0, 0, 0, None, 0, 0, None, 0, 0, None), -3),
     (lambda L: L.sa_attn_fwd_fp8(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, 10, 8, 2, 64, 100, 0, 0, None, None,
                                  0, 128, 64, None, 0, None, 0, None, 0, 1.0, None, None), -3),
@@ -49,7 +50,21 @@ def test_native_error_message():
     from sm120_attn import _native as N
     with pytest.raises(N.NativeError, match='bad sizes'):
         N.call('sa_select', None, 0, 0, None, 0, 0, 0, 0, 0, 0, 0, 0, 0, ctypes.c_float(0), ctypes.c_float(0), 0,
-               None, None, 0, None, None)
+               None, None, 0, None, None, 0, None)
+
+
+def test_select_workspace_size_and_refusal():
+    from sm120_attn import _native as N
+    L = N.lib()
+    need = L.sa_select_workspace_bytes(64, 64, 512)
+    assert need == 64 * 64 * 512 * 4
+    assert L.sa_select_workspace_bytes(64, 64, 500) == 64 * 64 * 512 * 4      # rows padded to 32 blocks
+    assert L.sa_select_workspace_bytes(0, 64, 512) == 0
+    # valid sizes but no workspace: refused before any launch (no GPU needed)
+    buf = (ctypes.c_float * 4)()
+    rc = L.sa_select(ctypes.addressof(buf), 0, 0, ctypes.addressof(buf), 0, 0, 0, 8, 2, 128, 4, 16, 0, 0.1, 0.95, 0,
+                     None, None, 0, None, None, 0, None)
+    assert rc == -1 and b'workspace' in L.sa_last_error()
 
 
 def test_ops_refuse_cpu_tensors():
