@@ -106,6 +106,29 @@ SA_API int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_head_s
 /* Bytes of workspace sa_select needs for these sizes (0 for invalid sizes). */
 SA_API size_t sa_select_workspace_bytes(int num_heads, int MB, int nb_total);
 
+/*
+ * sa_select without a workspace argument: the same selection, with its scratch taken from a
+ * 40 MiB (41943040-byte) buffer that is compiled into the library, one per device.  It has no
+ * counterpart in the reference, whose selection allocates through PyTorch.  It is meant for
+ * callers that cannot allocate device memory at the point where they select blocks - a C or C++
+ * host runtime driving this library through plain pointers with no device allocator of its own,
+ * or a serving loop that must not allocate (and possibly synchronise the device) per request.
+ *   - Sizes whose sa_select_workspace_bytes() exceeds 41943040 are refused with
+ *     SA_ERR_UNSUPPORTED and a message naming the sizes; use sa_select then.  (64 heads x 64
+ *     q blocks fit up to 2560 key blocks.)
+ *   - The first call made with a given device current looks up the buffer's address on that
+ *     device; later calls on that device only reuse it.  Make that first call before capturing
+ *     any stream.
+ *   - Nothing in the buffer needs to start at zero: each call writes every entry it reads.
+ *   - All calls on one device share the buffer: calls whose work overlaps on the GPU (different
+ *     streams, or host threads without ordering) race.  Order them on one stream.
+ *   - No device memory is allocated or freed by this call.
+ */
+SA_API int sa_select_static(const float* qm, int64_t qm_block_stride, int64_t qm_head_stride, const float* km,
+              int64_t km_head_stride, int64_t km_block_stride, int nb_km, int num_heads, int num_kv_heads,
+              int head_dim, int MB, int nb_total, int qblk0, float scale, float tau, int mode, int32_t* counts,
+              int32_t* lists, int64_t list_stride, uint8_t* masks, void* stream);
+
 /* scale modes of sa_quantize_e4m3 */
 #define SA_QUANT_MUL 0           /* e4m3(x * s)            fp32 multiply by s = 1/scale        */
 #define SA_QUANT_MUL_BF16 1      /* e4m3(bf16(x * s))      the glue, sparse_prefill.py:230-233 */

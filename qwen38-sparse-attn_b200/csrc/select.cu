@@ -19,6 +19,7 @@
 //      (sparse_prefill.py:78-84, :223), then the row is emitted as count / ascending list / 0-1
 //      mask.  Rows longer than 2048 blocks take a shared-memory path with the same arithmetic.
 #include <algorithm>
+#include <mutex>
 
 #include "sa_common.cuh"
 
@@ -427,6 +428,12 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel_long(const SelArgs 
 
 int64_t logits_row_stride(int nb_total) { return (static_cast<int64_t>(nb_total) + 31) / 32 * 32; }
 
+// Scratch of sa_select_static: one buffer per device, part of the module image, so that entry
+// point needs no allocation.  Every call uses all of it that it needs, hence calls overlapping on a
+// device race.
+constexpr size_t STATIC_SCRATCH_BYTES = size_t(40) << 20;
+static __device__ __align__(256) unsigned char g_select_scratch[STATIC_SCRATCH_BYTES];
+
 }  // namespace
 }  // namespace sa
 
@@ -501,4 +508,42 @@ extern "C" int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_he
         select_kernel_long<<<blocks, SEL_THREADS, smem, s>>>(a, units, npl);
     }
     return check_launch("select_kernel");
+}
+
+// Same selection as sa_select, on the static scratch buffer above instead of a caller workspace.
+// The buffer's device address is looked up once per device (cudaGetSymbolAddress, with the caller's
+// current device) on the first call made with that device current.
+extern "C" int sa_select_static(const float* qm, int64_t qm_block_stride, int64_t qm_head_stride, const float* km,
+                                int64_t km_head_stride, int64_t km_block_stride, int nb_km, int num_heads,
+                                int num_kv_heads, int head_dim, int MB, int nb_total, int qblk0, float scale, float tau,
+                                int mode, int32_t* counts, int32_t* lists, int64_t list_stride, uint8_t* masks,
+                                void* stream) {
+    static std::mutex mu;
+    static void* scratch[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(SA_ERR_CUDA, "sa_select_static: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return fail(SA_ERR_UNSUPPORTED, "sa_select_static: device %d", dev);
+    void* ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!scratch[dev]) {
+            e = cudaGetSymbolAddress(&scratch[dev], g_select_scratch);
+            if (e != cudaSuccess) {
+                scratch[dev] = nullptr;
+                return fail(SA_ERR_CUDA, "sa_select_static: scratch address on device %d: %s", dev,
+                            cudaGetErrorString(e));
+            }
+        }
+        ws = scratch[dev];
+    }
+    const size_t need = sa_select_workspace_bytes(num_heads, MB, nb_total);
+    if (need > STATIC_SCRATCH_BYTES)
+        return fail(SA_ERR_UNSUPPORTED,
+                    "sa_select_static: %d heads x %d q blocks x %d key blocks need %zu bytes of scratch, more than "
+                    "the %zu-byte static buffer; call sa_select with a workspace instead",
+                    num_heads, MB, nb_total, need, STATIC_SCRATCH_BYTES);
+    return sa_select(qm, qm_block_stride, qm_head_stride, km, km_head_stride, km_block_stride, nb_km, num_heads,
+                     num_kv_heads, head_dim, MB, nb_total, qblk0, scale, tau, mode, counts, lists, list_stride, masks,
+                     ws, STATIC_SCRATCH_BYTES, stream);
 }
