@@ -3,8 +3,8 @@
 
 One step = one prefill chunk through the drop-in API `SparsePrefill.forward_sm120fp8` with the
 incremental block-mean cache (`_cached_block_means`): pool the chunk's keys into the cache
-(kernel a), pool + quantise the queries (kernel a), select blocks (kernel b), quantise K and V^T,
-block-sparse FP8 attention (kernel c).  Shape of BASELINE configs[1]: Q 8192 rows at offset 57344
+(kernel a), pool + quantise the queries (kernel a), score and select blocks (kernel b, two
+launches), quantise K and V, block-sparse FP8 attention (kernel c).  Shape of BASELINE configs[1]: Q 8192 rows at offset 57344
 against 65536 keys, 64 query / 8 KV heads, head_dim 128, block 128, tau 0.95, seeded synthetic
 inputs with the benchmark's hot-block injection.  Inputs (q 134 MB, k/v 134 MB each) exceed the
 126 MB L2, so no flush is needed between steps.
@@ -49,12 +49,12 @@ METRIC = 'sparse prefill attention TFLOPS (exec blocks) + prefill TTFT @64K/128K
 H_FULL, HK_FULL, D = 64, 8, 128
 N_Q, KV, BLOCK, TAU = 8192, 65536, 128, 0.95
 Q_START = KV - N_Q
-# Kernels of this package launched per step: K-chunk block means, Q block means + e4m3, selection,
-# K e4m3, V^T e4m3, attention.
-LAUNCHES_PER_STEP = 6
+# Kernels of this package launched per step: K-chunk block means, Q block means + e4m3, scores,
+# selection, K e4m3, V e4m3, attention.
+LAUNCHES_PER_STEP = 7
 # DRAM bytes (read + write) of one attention launch of this workload, from the ncu capture summarised
-# in profiles/attn_fwd_fp8_sparse_prefill.md (213.8 MB read + 106.4 MB written).
-ATTN_DRAM_BYTES = 320225280
+# in profiles/attn_fwd_fp8_sparse_prefill.md (220.3 MB read + 108.4 MB written).
+ATTN_DRAM_BYTES = 328640000
 
 
 def peaks():
@@ -295,8 +295,12 @@ def _rank_env():
     return world, rank, local, dev
 
 
+PROFILE_RANGE = False        # set from --profile-range: bracket the first timed region for ncu
+
+
 def _timed(fn, steps, dev, world, before=None):
     """Device time (ms) of `steps` calls of fn on the current stream, barrier + synchronize on both sides."""
+    global PROFILE_RANGE
     import torch
     import torch.distributed as dist
 
@@ -307,6 +311,10 @@ def _timed(fn, steps, dev, world, before=None):
     barrier()
     stream = torch.cuda.current_stream(dev)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    prof = PROFILE_RANGE
+    PROFILE_RANGE = False
+    if prof:
+        torch.cuda.profiler.start()
     t0.record(stream)
     for _ in range(steps):
         if before is not None:
@@ -314,6 +322,8 @@ def _timed(fn, steps, dev, world, before=None):
         fn()
     t1.record(stream)
     barrier()
+    if prof:
+        torch.cuda.profiler.stop()
     return t0.elapsed_time(t1)
 
 
@@ -492,9 +502,11 @@ def _chunked(args, h, hk, dev, rank):
 
 
 def run_other(args):
+    global PROFILE_RANGE
     from sm120_attn.shard import kv_head_range, reduce_over_ranks
     import torch.distributed as dist
     world, rank, local, dev = _rank_env()
+    PROFILE_RANGE = args.profile_range
     if args.scaling == 'strong':
         try:
             lo, hi = kv_head_range(rank, world, HK_FULL)
