@@ -395,11 +395,14 @@ def attention_ref(q, k, v, q_pos0: int, masks=None, q_block: int = 64, kv_block:
 
 def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None, lists=None,
                                q_block: int = 128, kv_block: int = 64, q_front: int = 0, tile: int = 128,
-                               key_tile: int = 64):
+                               key_tile: int = 64, group: int = 1):
     """Numerical model of the block-sparse FP8 forward (kai_fa_fp8.py:248-292, kai_fa_fp8_tma.py:256-272).
 
     Walks each (head, 128-row tile)'s block list from the last entry to the first in `key_tile`-key
-    steps (a 128-key block is split, upper half first), with the online softmax in the exp2 domain,
+    steps (a 128-key block is split, upper half first); every `group` consecutive steps form one key
+    tile of the online softmax (the CUDA FP8 kernel takes one 64-key step per tile; a kernel taking
+    two steps per tile, not necessarily adjacent keys, is modelled by group=2).  Online softmax in
+    the exp2 domain,
     P scaled by 448 and rounded to e4m3 before the PV product, the row sum over unrounded P, and
     `O * (sv / 448) / rowsum` (0 for an empty row).  The order and granularity of the walk set where
     P is rounded, so they follow the CUDA kernel.  Inputs are e4m3 bit patterns q8 [n, H, D],
@@ -438,8 +441,8 @@ def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None,
             m = np.full(tile, -np.inf)
             l = np.zeros(tile)
             o = np.zeros((tile, D))
-            for k0 in starts:
-                keys = np.arange(k0, k0 + key_tile)
+            for gi in range(0, len(starts), group):
+                keys = np.concatenate([np.arange(k0, k0 + key_tile) for k0 in starts[gi:gi + group]])
                 kk = np.zeros((len(keys), D))
                 vk = np.zeros((len(keys), D))
                 inr = keys < N

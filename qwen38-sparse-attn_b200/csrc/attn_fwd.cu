@@ -22,15 +22,11 @@
 #include <climits>
 #include <mutex>
 
+#include "attn_common.cuh"
 #include "sa_common.cuh"
 
 namespace sa {
 namespace {
-
-constexpr int KEY_NONE = 1 << 30;   // key base of an absent tile: every key masked, TMA zero-fills
-constexpr int KEY_END = -1;         // stage descriptor after the last tile of a walk
-constexpr float LOG2E = 1.4426950408889634f;
-constexpr float LOG2_448 = 8.807354922057604f;
 
 template <bool FP8>
 struct Cfg {
@@ -67,123 +63,6 @@ struct Cfg {
     static constexpr float RESCALE_SLACK = FP8 ? 0.f : 8.f;
 };
 
-struct Params {
-    const int32_t* counts;
-    const int32_t* lists;
-    int64_t list_stride;
-    void* out;
-    int64_t o_row_stride, o_head_stride;
-    int n_q, H, Hk, kv_len, q_front, q_offset, n_tiles, kv_block, q_block, list_rows_per_head;
-    const float* q_scale;
-    const float* k_scale;
-    const float* v_scale;
-    int qss, kss, vss;
-    float softmax_scale;
-    int32_t* status;
-};
-
-// Sequence of 64-key tiles one (head, 128-row query tile) walks, from the last block-list entry
-// to the first like the reference (kai_fa_fp8_tma.py:149-162).  Modes: dense causal walk; one
-// list of 64- or 128-key blocks for the whole tile; two lists of 64-key blocks, one per 64-row
-// half of the tile (the BF16 path's 64-row query blocks), walked as their merged union with a
-// per-tile mask of the halves that selected the block.  The producer and every softmax thread
-// run the same walk; list heads are loaded one step ahead, so a step never waits on its load.
-struct Walker {
-    const int32_t* a;
-    const int32_t* b;
-    int ia, ib;          // list index of the cached head (counting down)
-    int va, vb;          // cached list heads (-1 when exhausted)
-    int dense_next;      // dense: next 64-key tile base, counting down
-    int kvb;
-    int blk_lim;         // block ids at or above this are invalid (their key base would overflow)
-    int half;            // 128-key blocks: which half of the current block comes next (1 = upper)
-    int mode;            // 0 dense, 1 one list, 2 two lists
-    bool bad;
-
-    __device__ __forceinline__ int load(const int32_t* p, int i) const { return i >= 0 ? __ldg(p + i) : -1; }
-
-    __device__ __forceinline__ bool next(int& kbase, uint32_t& rowmask) {
-        rowmask = 3u;
-        if (mode == 0) {
-            if (dense_next < 0) return false;
-            kbase = dense_next;
-            dense_next -= 64;
-            return true;
-        }
-        if (mode == 1) {
-            if (ia < 0) return false;
-            const int blk = va;
-            if (blk < 0 || blk >= blk_lim) {
-                bad = true;
-                kbase = KEY_NONE;
-            } else {
-                kbase = blk * kvb + (kvb == 128 ? half * 64 : 0);
-            }
-            if (kvb == 128 && half == 1) {
-                half = 0;
-            } else {
-                half = 1;
-                --ia;
-                va = load(a, ia);
-            }
-            return true;
-        }
-        if (va < 0 && vb < 0) return false;
-        const int blk = max(va, vb);
-        rowmask = (va == blk ? 1u : 0u) | (vb == blk ? 2u : 0u);
-        if (va == blk) { --ia; va = load(a, ia); }
-        if (vb == blk) { --ib; vb = load(b, ib); }
-        if (blk >= KEY_NONE / 64) {
-            bad = true;
-            kbase = KEY_NONE;
-        } else {
-            kbase = blk * 64;
-        }
-        return true;
-    }
-};
-
-__device__ __forceinline__ Walker make_walker(const Params& p, int h, int m) {
-    Walker w;
-    w.bad = false;
-    w.kvb = p.kv_block;
-    w.blk_lim = KEY_NONE / p.kv_block;
-    w.half = 1;
-    w.a = w.b = nullptr;
-    w.ia = w.ib = -1;
-    w.va = w.vb = -1;
-    w.dense_next = -1;
-    if (!p.counts) {
-        w.mode = 0;
-        const int last = p.q_offset + (m + 1) * 128;              // one past the tile's last position
-        const int keys = min(last, p.kv_len);
-        w.dense_next = keys > 0 ? ((keys + 63) / 64 - 1) * 64 : -1;
-    } else if (p.q_block == 128) {
-        w.mode = 1;
-        const int64_t row = static_cast<int64_t>(h) * p.list_rows_per_head + m;
-        w.a = p.lists + row * p.list_stride;
-        w.ia = max(__ldg(p.counts + row), 0) - 1;
-        w.va = w.load(w.a, w.ia);
-    } else {
-        w.mode = 2;
-        const int r0 = 2 * m, r1 = 2 * m + 1;
-        const int64_t row0 = static_cast<int64_t>(h) * p.list_rows_per_head + r0;
-        w.a = p.lists + row0 * p.list_stride;
-        w.ia = max(__ldg(p.counts + row0), 0) - 1;
-        if (r1 < p.list_rows_per_head) {
-            w.b = p.lists + (row0 + 1) * p.list_stride;
-            w.ib = max(__ldg(p.counts + row0 + 1), 0) - 1;
-        }
-        w.va = w.load(w.a, w.ia);
-        w.vb = w.b ? w.load(w.b, w.ib) : -1;
-        if (w.va < -1 || w.vb < -1) {   // negative entries: treat the list as exhausted
-            w.bad = true;
-            w.va = max(w.va, -1);
-            w.vb = max(w.vb, -1);
-        }
-    }
-    return w;
-}
 
 template <bool FP8>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -553,37 +432,6 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
 // ------------------------------------------------------------------------------------------------
 // Host side: tensor maps and launch
 // ------------------------------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    });
-    return fn;
-}
-
-int encode3d(CUtensorMap* map, bool fp8, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
-             uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle sw, const char* what) {
-    auto fn = encode_fn();
-    if (!fn) return fail(SA_ERR_TMA, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[3] = {d0, d1, d2};
-    cuuint64_t strides[2] = {s1_bytes, s2_bytes};
-    cuuint32_t box[3] = {b0, b1, b2};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
-                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return fail(SA_ERR_TMA, "tensor map for %s: error %d (dims %llu %llu %llu strides %llu %llu)", what, (int)r,
-                    (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2,
-                    (unsigned long long)s1_bytes, (unsigned long long)s2_bytes);
-    return SA_OK;
-}
-
 template <bool FP8>
 int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t krs, int64_t khs, const void* v,
                 int64_t vrs, int64_t vhs, void* out, int64_t ors, int64_t ohs, int n_q, int H, int Hk, int D, int kv_len,

@@ -43,7 +43,7 @@ __device__ __forceinline__ uint2 quant8(const float (&f)[8], float s, int mode) 
 // One CTA per (block b, group of heads).  threadIdx.x -> (head in group, 16-byte column chunk),
 // threadIdx.y -> row group: rows lo+ty, lo+ty+RG, ... are summed in order by each thread and the
 // RG partial sums are added in row-group order (RG = 1 gives a strictly sequential row sum).
-__global__ void block_means_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64_t xhs, int n, int heads,
+__global__ void __launch_bounds__(512, 2) block_means_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64_t xhs, int n, int heads,
                                    int D, int pos0, int block, int b0, int heads_per_cta, float* __restrict__ out,
                                    int64_t ohs, int64_t obs, int out_block0, uint8_t* __restrict__ q8,
                                    int64_t q8rs, int64_t q8hs, const float* __restrict__ inv_scale, int iss,
@@ -64,14 +64,26 @@ __global__ void block_means_kernel(const uint16_t* __restrict__ x, int64_t xrs, 
         const uint16_t* src = x + static_cast<int64_t>(h) * xhs + c * 8;
         const float inv = q8 ? inv_scale[h * iss] : 0.f;
         uint8_t* dst = q8 ? q8 + static_cast<int64_t>(h) * q8hs + c * 8 : nullptr;
-#pragma unroll 8
-        for (int r = lo + ty; r < hi; r += RG) {
-            const uint4 v = ld_stream(src + static_cast<int64_t>(r) * xrs);
-            float f[8];
-            unpack8(v, f);
+        // 8 rows per batch: all 8 loads are issued before the first is used (8 x 16 B in flight per
+        // thread); the rows are still added in order
+        constexpr int BATCH = 8;
+        for (int base = lo + ty; base < hi; base += BATCH * RG) {
+            uint4 v[BATCH];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] += f[i];
-            if (dst) *reinterpret_cast<uint2*>(dst + static_cast<int64_t>(r) * q8rs) = quant8(f, inv, SA_QUANT_MUL_BF16);
+            for (int k = 0; k < BATCH; ++k) {
+                const int r = base + k * RG;
+                v[k] = r < hi ? ld_stream(src + static_cast<int64_t>(r) * xrs) : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int k = 0; k < BATCH; ++k) {
+                const int r = base + k * RG;
+                if (r >= hi) break;
+                float f[8];
+                unpack8(v[k], f);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] += f[i];
+                if (dst) *reinterpret_cast<uint2*>(dst + static_cast<int64_t>(r) * q8rs) = quant8(f, inv, SA_QUANT_MUL_BF16);
+            }
         }
     }
     if (RG > 1) {
@@ -99,21 +111,38 @@ __global__ void block_means_kernel(const uint16_t* __restrict__ x, int64_t xrs, 
     }
 }
 
-// Elementwise e4m3 quantisation, row-major output.  One thread per 16-byte input chunk.
-__global__ void quant_rows_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64_t xhs, int rows, int heads,
-                                  int D, const float* __restrict__ scale, int iss, int mode,
-                                  uint8_t* __restrict__ out, int64_t ors, int64_t ohs) {
+// Elementwise e4m3 quantisation, row-major output.  threadIdx.x (with blockIdx.y) picks a 16-byte
+// column chunk hc = (head, 8 elements) of the row, fixed for the thread; rows are walked in
+// batches of 8 blockDim.y apart, all 8 loads issued before the first is used.
+__global__ void __launch_bounds__(256) quant_rows_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64_t xhs,
+                                                         int rows, int heads, int D, const float* __restrict__ scale,
+                                                         int iss, int mode, uint8_t* __restrict__ out, int64_t ors,
+                                                         int64_t ohs) {
+    constexpr int BATCH = 8;
     const int cols = D >> 3;
-    const int64_t total = static_cast<int64_t>(rows) * heads * cols;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int c = static_cast<int>(i % cols);
-        const int64_t rh = i / cols;
-        const int h = static_cast<int>(rh % heads);
-        const int64_t r = rh / heads;
-        float f[8];
-        unpack8(ld_stream(x + r * xrs + h * xhs + c * 8), f);
-        *reinterpret_cast<uint2*>(out + r * ors + h * ohs + c * 8) = quant8(f, scale[h * iss], mode);
+    const int HC = heads * cols;
+    const int rstep = blockDim.y * BATCH;
+    for (int hc = blockIdx.y * blockDim.x + threadIdx.x; hc < HC; hc += gridDim.y * blockDim.x) {
+        const int h = hc / cols, c = hc - h * cols;
+        const uint16_t* src = x + static_cast<int64_t>(h) * xhs + c * 8;
+        uint8_t* dst = out + static_cast<int64_t>(h) * ohs + c * 8;
+        const float sc = scale[h * iss];
+        for (int r0 = blockIdx.x * rstep + threadIdx.y; r0 < rows; r0 += gridDim.x * rstep) {
+            uint4 v[BATCH];
+#pragma unroll
+            for (int k = 0; k < BATCH; ++k) {
+                const int r = r0 + k * static_cast<int>(blockDim.y);
+                v[k] = r < rows ? ld_stream(src + static_cast<int64_t>(r) * xrs) : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int k = 0; k < BATCH; ++k) {
+                const int r = r0 + k * static_cast<int>(blockDim.y);
+                if (r >= rows) break;
+                float f[8];
+                unpack8(v[k], f);
+                *reinterpret_cast<uint2*>(dst + static_cast<int64_t>(r) * ors) = quant8(f, sc, mode);
+            }
+        }
     }
 }
 
@@ -229,7 +258,7 @@ extern "C" int sa_block_means_bf16(const void* x, int64_t x_row_stride, int64_t 
     const long long ctas = static_cast<long long>(nblk) * nhg;
     const long long target = 2048ll * num_sms();
     int rg = 1;
-    while (rg < 16 && (ctas * tx * rg < target || tx * rg < 128) && tx * rg * 2 <= 1024 && rg * 2 <= block / 4) rg *= 2;
+    while (rg < 16 && (ctas * tx * rg < target || tx * rg < 128) && tx * rg * 2 <= 512 && rg * 2 <= block / 4) rg *= 2;
     dim3 grid(b1 - b0, nhg), blk(tx, rg);
     const size_t smem = rg > 1 ? static_cast<size_t>(rg - 1) * tx * 8 * sizeof(float) : 0;
     if (smem > 48 * 1024) cudaFuncSetAttribute(block_means_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -254,9 +283,13 @@ extern "C" int sa_quantize_e4m3(const void* x, int64_t x_row_stride, int64_t x_h
         if ((reinterpret_cast<uintptr_t>(out) & 7) || out_row_stride % 8 || out_head_stride % 8)
             return fail(SA_ERR_ALIGN, "sa_quantize_e4m3: out must be 8-byte aligned with strides % 8 == 0");
         if (rows == 0) return SA_OK;
-        const int64_t total = static_cast<int64_t>(rows) * heads * (head_dim / 8);
-        const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 16ll * num_sms()));
-        quant_rows_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint16_t*>(x), x_row_stride, x_head_stride, rows,
+        const int HC = heads * (head_dim / 8);
+        const int bx = std::min(HC, 128);
+        const dim3 blk(bx, 256 / bx);
+        const int gy = (HC + bx - 1) / bx;
+        const int per_cta = static_cast<int>(blk.y) * 8;
+        const int gx = std::max(1, std::min((rows + per_cta - 1) / per_cta, (8 * num_sms() + gy - 1) / gy));
+        quant_rows_kernel<<<dim3(gx, gy), blk, 0, s>>>(static_cast<const uint16_t*>(x), x_row_stride, x_head_stride, rows,
                                                  heads, head_dim, scale, scale_stride, mode, out,
                                                  out_row_stride, out_head_stride);
         return check_launch("quant_rows_kernel");

@@ -141,7 +141,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 #define SA_WAIT_SUSPEND_NS 1000000u   // try_wait suspend-time hint: a waiting warp sleeps (up to 1 ms)
 #endif                                // until the phase completes instead of re-issuing polls
 
-// Poll without a suspend hint: the cheapest test of a phase that has usually completed already.
+// Non-blocking test of a phase (mbarrier.test_wait): returns at once whether the phase with this
+// parity has completed.  (try_wait, below, may suspend the thread until the phase completes or a
+// time limit passes, so it must not be used to poll several barriers in turn.)
+__device__ __forceinline__ bool mbar_poll(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// try_wait without a suspend hint: the cheapest wait for a phase that has usually completed already.
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
