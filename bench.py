@@ -465,6 +465,7 @@ def _chunked(args, h, hk, dev, rank):
     def prefill(record=False):
         ksp._KMEAN_CACHE.clear()
         ksp._SCALE_CACHE.clear()
+        ksp._KV8_CACHE.clear()
         flops = 0.0
         for c in range(total // chunk):
             q0 = c * chunk
@@ -474,7 +475,8 @@ def _chunked(args, h, hk, dev, rank):
                 a.record(stream)
             km = ksp._cached_block_means(layer, 0, kc[q0:], q0, q0 + chunk)
             scales = ksp._cached_scales(layer, 0, qc, kc, vc, q0)
-            sp.forward_sm120fp8(qc, kc, vc, q0, out=out, km=km, scales=scales)
+            kv8 = ksp._cached_kv8(layer, 0, k, v, q0, q0 + chunk, scales) if args.fp8_kv_cache else None
+            sp.forward_sm120fp8(qc, kc, vc, q0, out=out, km=km, scales=scales, kv8=kv8)
             if record:
                 b.record(stream)
                 per_chunk.append((a, b, sp.last_counts.sum()))
@@ -495,7 +497,9 @@ def _chunked(args, h, hk, dev, rank):
             'config': {'workload': f'chunked prefill of {total} tokens in {total // chunk} chunks of {chunk} through '
                                    f'SparsePrefill.forward_sm120fp8, block-mean and scale caches carried; H {h}/Hk {hk}/'
                                    f'D {D}, block {BLOCK}, tau {TAU}; strong injection: sink + local window (4 blocks) '
-                                   f'+ 16 hot blocks per KV head',
+                                   f'+ 16 hot blocks per KV head; '
+                                   + ('FP8 KV cache (each K/V row quantised once)' if args.fp8_kv_cache else
+                                      'K/V history re-quantised every chunk (reference behaviour)'),
                        'ms_per_chunk': [round(x, 3) for x in chunk_ms],
                        'kept_fraction_overall': round(exec_flops / dense_flops, 4),
                        'value_definition': 'executed-tile FLOPs (4 D 128 128 per kept 128x128 tile) / prefill time'}}
@@ -640,6 +644,8 @@ def main():
     ap.add_argument('--profile-range', action='store_true',
                     help='bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)')
     ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked'])
+    ap.add_argument('--fp8-kv-cache', action='store_true',
+                    help='chunked workload: keep e4m3 K/V across chunks (SM120_SPARSE_FP8_KV_CACHE)')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'b200':
         print('note: warmup raised to 3', file=sys.stderr)

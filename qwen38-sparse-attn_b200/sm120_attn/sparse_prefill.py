@@ -184,11 +184,13 @@ class SparsePrefill:
         return out
 
     @torch.no_grad()
-    def forward_sm120fp8(self, q, k, v, q_start, out=None, km=None, scales=None):
+    def forward_sm120fp8(self, q, k, v, q_start, out=None, km=None, scales=None, kv8=None):
         """FP8 (e4m3) path, 128-row query blocks; k, v NHD [T, Hk, D] bf16, quantised here.
 
         scales: (sq, sk, sv) python floats (per-request, per-layer, cached by the caller); without
-        them per-call amax scales are used (three device syncs).
+        them per-call amax scales are used (three device syncs).  kv8: optional (k8, v8) uint8
+        [kv_len, Hk, D] already quantised with these scales (`_cached_kv8`); then k and v are not
+        read here.
         """
         BM = 128
         B = BLOCK
@@ -218,10 +220,15 @@ class SparsePrefill:
         lists = torch.empty(rows, nb_need, dtype=torch.int32, device=dev)
         ops.select(qm, km, self.H, self.Hk, nb_need, qs // B, self.scale, self.tau,
                    SA_SELECT_PAIR_UNION if B == 64 else SA_SELECT_PER_HEAD, counts=counts, lists=lists)
-        k8 = torch.empty(kv_len, self.Hk, self.D, dtype=torch.uint8, device=dev)
-        ops.quantize(k[:kv_len], inv[1:2], SA_QUANT_MUL_BF16, k8)
-        v8 = torch.empty(kv_len, self.Hk, self.D, dtype=torch.uint8, device=dev)
-        ops.quantize(v[:kv_len], inv[2:3], SA_QUANT_MUL_BF16, v8)
+        if kv8 is not None:
+            k8, v8 = kv8
+            if k8.shape[0] < kv_len or v8.shape[0] < kv_len:
+                raise ValueError('kv8 holds fewer rows than q_start + n')
+        else:
+            k8 = torch.empty(kv_len, self.Hk, self.D, dtype=torch.uint8, device=dev)
+            ops.quantize(k[:kv_len], inv[1:2], SA_QUANT_MUL_BF16, k8)
+            v8 = torch.empty(kv_len, self.Hk, self.D, dtype=torch.uint8, device=dev)
+            ops.quantize(v[:kv_len], inv[2:3], SA_QUANT_MUL_BF16, v8)
         t1 = self._tick()
         o, copy_back = self._out(out, n, dev)
         sc = torch.tensor([sq, sk, sv], dtype=torch.float32).to(dev, non_blocking=True)
@@ -340,6 +347,9 @@ def config():
             'min_q': pick('SM120_SPARSE_MIN_Q', 'min_q', 1024, int),
             'kernel': pick('SM120_SPARSE_KERNEL', 'kernel', 'sm120fp8', str),
             'fp8_pipeline': pick('SM120_SPARSE_FP8_PIPELINE', 'fp8_pipeline', 'tma', str),
+            # new: keep e4m3 K/V per (layer, request) and quantise each chunk's rows once
+            'fp8_kv_cache': pick('SM120_SPARSE_FP8_KV_CACHE', 'fp8_kv_cache', 0,
+                                 lambda v: str(v) not in ('0', 'false', 'False', '')),
         }
         print('[sm120-sparse] config %r' % (_CONFIG,), flush=True)
     return _CONFIG
@@ -402,6 +412,45 @@ def _cached_block_means(layer_key, first_page, key_chunk, q_start, kv_len, key_a
     entry['nb'] = b1
     entry['last_kv'] = kv_len
     return entry['km'][:, :b1]
+
+
+_KV8_CACHE: dict = {}
+
+
+def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales):
+    """Per-(layer, request) e4m3 K and V [kv_len, Hk, D] (uint8 views), each row quantised once.
+
+    The FP8 path quantises the whole key/value history with the request's scales on every chunk
+    (sparse_prefill.py:230-233); the scales are cached per request, so rows quantised for an earlier
+    chunk never change.  An entry contiguous with this chunk (its last row is q_start) and made with
+    the same scales only quantises rows q_start..kv_len; otherwise it is rebuilt from k, v (NHD, at
+    least kv_len rows).  The bytes are the same as re-quantising the history.
+    """
+    sk, sv = float(scales[1]), float(scales[2])
+    key = (layer_key, first_page)
+    entry = _KV8_CACHE.get(key)
+    Hk, D = k.shape[1], k.shape[2]
+    dev = k.device
+    if entry is None or q_start == 0 or entry['rows'] != q_start or entry['scales'] != (sk, sv):
+        if len(_KV8_CACHE) >= _KMEAN_MAX_ENTRIES:
+            _KV8_CACHE.pop(next(iter(_KV8_CACHE)))
+        cap = max(kv_len, 8192)
+        entry = {'k8': torch.empty(cap, Hk, D, dtype=torch.uint8, device=dev),
+                 'v8': torch.empty(cap, Hk, D, dtype=torch.uint8, device=dev), 'rows': 0, 'scales': (sk, sv),
+                 'inv': torch.tensor([1.0 / sk, 1.0 / sv], dtype=torch.float32).to(dev, non_blocking=True)}
+        _KV8_CACHE[key] = entry
+    lo = entry['rows']
+    if entry['k8'].shape[0] < kv_len:
+        cap = max(kv_len, 2 * entry['k8'].shape[0])
+        for name in ('k8', 'v8'):
+            grown = torch.empty(cap, Hk, D, dtype=torch.uint8, device=dev)
+            grown[:lo] = entry[name][:lo]
+            entry[name] = grown
+    if kv_len > lo:
+        ops.quantize(k[lo:kv_len], entry['inv'][0:1], SA_QUANT_MUL_BF16, entry['k8'][lo:kv_len])
+        ops.quantize(v[lo:kv_len], entry['inv'][1:2], SA_QUANT_MUL_BF16, entry['v8'][lo:kv_len])
+    entry['rows'] = kv_len
+    return entry['k8'][:kv_len], entry['v8'][:kv_len]
 
 
 _SCALE_CACHE: dict = {}
@@ -476,7 +525,9 @@ def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_me
         km = _cached_block_means(id(impl), first_pages[r], key[qsl[r]:qsl[r + 1]], kv_len - n, kv_len, key_all=k)
         if sp.kernel == 'sm120fp8':
             scales = _cached_scales(id(impl), first_pages[r], q_r, k[:kv_len], v[:kv_len], kv_len - n)
-            sp.forward_sm120fp8(q_r, k, v, kv_len - n, out=o_r, km=km, scales=scales)
+            kv8 = (_cached_kv8(id(impl), first_pages[r], k, v, kv_len - n, kv_len, scales)
+                   if config()['fp8_kv_cache'] else None)
+            sp.forward_sm120fp8(q_r, k, v, kv_len - n, out=o_r, km=km, scales=scales, kv8=kv8)
         else:
             sp.forward_sm120(q_r, k, v, kv_len - n, out=o_r, km=km)
     return True

@@ -35,10 +35,12 @@ def ksp():
     old = m.BLOCK
     m._KMEAN_CACHE.clear()
     m._SCALE_CACHE.clear()
+    m._KV8_CACHE.clear()
     yield m
     m.BLOCK = old
     m._KMEAN_CACHE.clear()
     m._SCALE_CACHE.clear()
+    m._KV8_CACHE.clear()
 
 
 def _heads_subset(H, g):
@@ -176,6 +178,29 @@ def test_cached_vs_direct_means_three_chunks(ksp):
         assert (o_cached.float() - o_direct.float()).abs().max().item() < 2e-2
 
 
+def test_fp8_kv_cache_chunks_bit_identical(ksp):
+    """The FP8 KV cache (each K/V row quantised once) gives the same output, bit for bit, as
+    re-quantising the history on every chunk, over three chunks of one request."""
+    ksp.BLOCK = 128
+    ksp._KV8_CACHE.clear()
+    H, Hk, D, n = 16, 2, 128, 1024
+    kv_total = 3 * n + 512
+    q, k, v, _ = synth.make_qkv(kv_total, kv_total, H, Hk, D, block=128, q_start=0, seed=17, strength='strong')
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    sp = ksp.SparsePrefill(H, Hk, D, DEV, tau=0.95, min_kv=0, min_q=0, kernel='sm120fp8')
+    for q_start in (0, n, 2 * n + 512):
+        kv_len = q_start + n
+        qc = qd[q_start:kv_len]
+        km = ksp._cached_block_means('kv8', 5, kd[q_start:kv_len], q_start, kv_len, key_all=kd)
+        scales = ksp._cached_scales('kv8', 5, qc, kd[:kv_len], vd[:kv_len], q_start)
+        o_plain = sp.forward_sm120fp8(qc, kd[:kv_len], vd[:kv_len], q_start, km=km, scales=scales)
+        kv8 = ksp._cached_kv8('kv8', 5, kd, vd, q_start, kv_len, scales)
+        o_cache = sp.forward_sm120fp8(qc, kd[:kv_len], vd[:kv_len], q_start, km=km, scales=scales, kv8=kv8)
+        torch.cuda.synchronize()
+        assert torch.equal(o_plain, o_cache), q_start
+    ksp._KV8_CACHE.clear()
+
+
 def test_stale_first_page(ksp):
     """tests/test_sparse_prefill.py:65-92: a recycled first page never supplies stale means or scales."""
     ksp.BLOCK = 64
@@ -259,12 +284,14 @@ def test_dropin_kernels_match_reference_semantics():
     assert rel_l2(f32(o8d), O.attention_ref(*deq, kv - n)) < 3e-2
 
 
-def test_try_sparse_forward_paged(ksp, monkeypatch):
+@pytest.mark.parametrize('kv_cache', [False, True])
+def test_try_sparse_forward_paged(ksp, monkeypatch, kv_cache):
     """The vLLM hook with a paged KV cache and fake metadata: eligible requests go through the sparse path
-    and match a direct forward_sm120fp8 call; the ineligible one is handed to _dense_request."""
+    and match a direct forward_sm120fp8 call (with and without the FP8 KV cache); the ineligible one is
+    handed to _dense_request."""
     ksp.BLOCK = 64
     monkeypatch.setattr(ksp, '_CONFIG', {'enabled': True, 'tau': 0.95, 'min_kv': 2048, 'min_q': 512,
-                                         'kernel': 'sm120fp8', 'fp8_pipeline': 'tma'})
+                                         'kernel': 'sm120fp8', 'fp8_pipeline': 'tma', 'fp8_kv_cache': kv_cache})
     ksp._STATE.clear()
     dense_calls = []
     monkeypatch.setattr(ksp, '_dense_request', lambda *a: dense_calls.append(a[-2:]))
@@ -312,3 +339,4 @@ def test_try_sparse_forward_paged(ksp, monkeypatch):
         o = sp2.forward_sm120fp8(q_r, kfull, vfull, kv - ql, km=km.contiguous(), scales=scales)
         assert rel_l2(f32(output[qsl[r]:qsl[r + 1]]), f32(o)) < 1e-6
     assert torch.all(output[qsl[1]:qsl[2]] == 0)
+    assert len(ksp._KV8_CACHE) == (2 if kv_cache else 0)

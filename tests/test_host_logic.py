@@ -40,11 +40,13 @@ def ksp(monkeypatch):
     monkeypatch.setattr(ops, 'absmax', fake_absmax)
     m._KMEAN_CACHE.clear()
     m._SCALE_CACHE.clear()
+    m._KV8_CACHE.clear()
     old_block = m.BLOCK
     yield m
     m.BLOCK = old_block
     m._KMEAN_CACHE.clear()
     m._SCALE_CACHE.clear()
+    m._KV8_CACHE.clear()
 
 
 def test_config_env_and_json(monkeypatch, tmp_path, capsys):
@@ -58,7 +60,8 @@ def test_config_env_and_json(monkeypatch, tmp_path, capsys):
         monkeypatch.delenv(k, raising=False)
     monkeypatch.setattr(m, '_CONFIG', None)
     c = m.config()
-    assert c == {'enabled': False, 'tau': 0.85, 'min_kv': 4096, 'min_q': 1024, 'kernel': 'sm120', 'fp8_pipeline': 'tma'}
+    assert c == {'enabled': False, 'tau': 0.85, 'min_kv': 4096, 'min_q': 1024, 'kernel': 'sm120', 'fp8_pipeline': 'tma',
+                 'fp8_kv_cache': False}
     assert 'config' in capsys.readouterr().out
     assert m.config() is c                                           # cached
     monkeypatch.setattr(m, '_CONFIG', None)
@@ -100,7 +103,7 @@ def _meta(qlens, kvlens, page=16, causal=True):
 def test_try_sparse_forward_gates(monkeypatch, case):
     import sm120_attn.sparse_prefill as m
     monkeypatch.setattr(m, '_CONFIG', {'enabled': case != 'disabled', 'tau': 0.95, 'min_kv': 8192, 'min_q': 1024,
-                                       'kernel': 'sm120fp8', 'fp8_pipeline': 'tma'})
+                                       'kernel': 'sm120fp8', 'fp8_pipeline': 'tma', 'fp8_kv_cache': False})
     monkeypatch.setattr(torch.cuda, 'is_current_stream_capturing', lambda: False)
     impl = types.SimpleNamespace(sliding_window=(-1, -1) if case != 'window' else (128, 0), scale=0.1)
     if case == 'short_q':
@@ -160,6 +163,44 @@ def test_cached_scales_bookkeeping(ksp):
     np.testing.assert_allclose(np.array([s0, s1, s2]), np.array([r0, r1, r2]), rtol=1e-12)
     assert s0 == s1 and s2 != s1
     assert ksp._SCALE_CACHE[('L', 3)]['last_kv'] == 1000 + 512
+
+
+def test_cached_kv8_quantises_each_row_once(ksp, monkeypatch):
+    """The FP8 KV cache quantises only a contiguous chunk's own rows; scale changes, gaps and q_start 0
+    rebuild it from the full history."""
+    from sm120_attn import ops
+    calls = []
+
+    def fake_quantize(x, scale, mode, out, transpose=False, rows_pad=0):
+        calls.append((x.shape[0], round(float(scale.reshape(-1)[0]), 3)))
+        out.copy_((x.float() * scale.reshape(1, 1, 1)).round().clamp(-100, 100).to(torch.int8).view(torch.uint8))
+
+    monkeypatch.setattr(ops, 'quantize', fake_quantize)
+    ksp._KV8_CACHE.clear()
+    Hk, D = 2, 8
+    k = torch.randn(10000, Hk, D).to(torch.bfloat16)
+    v = torch.randn(10000, Hk, D).to(torch.bfloat16)
+    sc = (0.1, 0.02, 0.03)
+    k8, v8 = ksp._cached_kv8('L', 3, k, v, 0, 1000, sc)
+    assert k8.shape == (1000, Hk, D) and calls == [(1000, 50.0), (1000, 33.333)]
+    calls.clear()
+    k8b, v8b = ksp._cached_kv8('L', 3, k, v, 1000, 2500, sc)            # contiguous: only the new rows
+    assert calls == [(1500, 50.0), (1500, 33.333)] and k8b.shape[0] == 2500
+    assert torch.equal(k8b[:1000], k8)                                   # earlier rows unchanged
+    calls.clear()
+    ksp._cached_kv8('L', 3, k, v, 3000, 4000, sc)                        # gap: rebuilt from row 0
+    assert calls == [(4000, 50.0), (4000, 33.333)]
+    calls.clear()
+    ksp._cached_kv8('L', 3, k, v, 4000, 4500, (0.1, 0.04, 0.03))         # other scales: rebuilt
+    assert calls == [(4500, 25.0), (4500, 33.333)]
+    calls.clear()
+    k8c, _ = ksp._cached_kv8('L', 3, k, v, 4500, 5000, (0.1, 0.04, 0.03))   # contiguous again
+    assert calls == [(500, 25.0), (500, 33.333)] and k8c.shape[0] == 5000
+    calls.clear()
+    k8d, _ = ksp._cached_kv8('L', 3, k, v, 5000, 10000, (0.1, 0.04, 0.03))  # past the 8192-row capacity
+    assert calls == [(5000, 25.0), (5000, 33.333)] and k8d.shape[0] == 10000
+    assert torch.equal(k8d[:5000], k8c)                                  # rows kept across the regrowth
+    ksp._KV8_CACHE.clear()
 
 
 def test_block_masks_rejects_unpadded_input(ksp):
