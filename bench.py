@@ -505,6 +505,103 @@ def _chunked(args, h, hk, dev, rank):
                        'value_definition': 'executed-tile FLOPs (4 D 128 128 per kept 128x128 tile) / prefill time'}}
 
 
+def run_ttft(args):
+    """Config 5: prefill TTFT of the random-init 64-layer GQA decoder (hidden 5120, 64/8 heads, SwiGLU
+    25600, vocab 151936) over 65536 / 131072 / 262144 random token ids in 8192-token chunks, sparse
+    FP8 attention at tau 0.95, tensor-parallel by KV head over the ranks (NCCL all-reduce after the
+    row-parallel projections).  value = TTFT of the 131072-token prompt."""
+    import torch
+    import torch.distributed as dist
+    import sm120_attn.sparse_prefill as ksp
+    from sm120_attn.decoder import DecoderConfig, TPDecoder
+    from sm120_attn.shard import reduce_over_ranks
+    world, rank, local, dev = _rank_env()
+    contexts = sorted(int(c) for c in args.contexts.split(','))
+    headline = 131072 if 131072 in contexts else contexts[-1]
+    cfg = DecoderConfig()
+    t_init = time.perf_counter()
+    model = TPDecoder(cfg, dev, rank=rank, world=world, group=None, seed=0, tau=TAU, kernel='sm120fp8',
+                      fp8_kv_cache=args.fp8_kv_cache, max_tokens=contexts[-1], chunk=8192, min_kv=8192)
+    torch.cuda.synchronize(dev)
+    t_init = time.perf_counter() - t_init
+    g = torch.Generator()
+    g.manual_seed(0)
+    ids_host = torch.randint(0, cfg.vocab, (contexts[-1],), generator=g).pin_memory()
+    ids_dev = ids_host.to(dev)
+    for _ in range(args.warmup):                              # warm-up prefills of the shortest prompt
+        model.prefill(ids_dev[:contexts[0]])
+    steps = 1                                                 # one prefill per prompt length
+    ttft, kept, first_tok, attn_ms, attn_flops = {}, {}, {}, 0.0, 0.0
+    clocks = Clocks(local)
+    clocks.start()
+    for T in contexts:
+        events = [] if T == headline else None
+        model.sp.kernel_events = events
+        model.sp._kept_acc = None
+        model.sp.stats['blocks_total'] = 0
+        toks = []
+        ms = _timed(lambda: toks.append(model.prefill(ids_dev[:T])), steps, dev, world)
+        model.sp.kernel_events = None
+        kept_units = float(model.sp._kept_acc.item()) / steps
+        kept[T] = round(float(model.sp.kept_fraction()), 4)
+        if events is not None:
+            attn_ms = sum(a.elapsed_time(b) for a, b in events) / steps
+            attn_flops = kept_units * 4.0 * cfg.head_dim * ksp.BLOCK * ksp.BLOCK
+        first_tok[T] = int(toks[-1].item())
+        ttft[T] = ms / steps
+    # end to end: ids from pinned host memory, first token read back, inside the timed region
+    tok_host = torch.empty(1, dtype=torch.int64).pin_memory()
+
+    def e2e():
+        ids = ids_host[:headline].to(dev, non_blocking=True)
+        tok_host.copy_(model.prefill(ids).reshape(1), non_blocking=True)
+    e2e_ms = _timed(e2e, 1, dev, world)
+    clk = clocks.stop()
+    keys = list(contexts)
+    vals, (flops_sum,) = reduce_over_ranks([ttft[T] for T in keys] + [e2e_ms, attn_ms], [attn_flops], device=dev)
+    ttft = dict(zip(keys, vals[:len(keys)]))
+    e2e_ms, attn_ms = vals[len(keys)], vals[len(keys) + 1]
+    hbm, bf16, how = peaks()
+    gemm_flops = cfg.prefill_flops(headline)
+    chunks = -(-headline // 8192)
+    launches = cfg.layers * (11 * chunks + 3) + 1
+    line = {
+        'metric': METRIC, 'value': round(ttft[headline] / 1000.0, 4), 'unit': 's', 'n_gpus': world, 'steps': steps,
+        'warmup': args.warmup, 'ms_per_step': round(ttft[headline], 2), 'higher_is_better': False,
+        'scaling': 'strong', 'vs_baseline': None,
+        'dtype': 'bf16 GEMMs (cuBLAS), fp8-e4m3 attention (fp32 accumulate), bf16 activations',
+        'data': 'synthetic: random N(0, 0.02) bf16 weights, seeded random token ids',
+        'config': {'workload': f'C5 prefill TTFT: random-init dense GQA decoder, {cfg.layers} layers, hidden '
+                               f'{cfg.hidden}, {cfg.heads}/{cfg.kv_heads} heads, head_dim {cfg.head_dim}, SwiGLU '
+                               f'{cfg.inter}, vocab {cfg.vocab}; 8192-token chunks, sparse FP8 attention tau {TAU} '
+                               f'(block {ksp.BLOCK}); value = TTFT of the {headline}-token prompt',
+                   'ttft_s': {str(T): round(ttft[T] / 1000.0, 4) for T in keys},
+                   'kept_fraction': {str(T): kept[T] for T in keys},
+                   'first_token': {str(T): first_tok[T] for T in keys}, 'fp8_kv_cache': bool(args.fp8_kv_cache),
+                   'parallelism': f'tensor parallel by KV head x{world} (NCCL all-reduce after o_proj and '
+                                  f'down_proj, all-gather of the last-token logits)',
+                   'gemm_tflops_per_gpu': round(gemm_flops / world / (ttft[headline] * 1e-3) / 1e12, 1),
+                   'attention_ms_of_ttft': round(attn_ms, 1), 'model_init_s': round(t_init, 1),
+                   'params': cfg.params(), 'l2': 'inputs larger than L2; no flush'},
+    }
+    if attn_ms > 0:
+        ach = flops_sum / world / (attn_ms * 1e-3) / 1e12
+        line['roofline'] = {'bound': 'tensor', 'kernel': 'attn_fwd_kernel<fp8> (all launches of the prefill)',
+                            'achieved': round(ach, 1), 'peak': round(2 * bf16, 1), 'unit': 'TFLOP/s',
+                            'frac': round(ach / (2 * bf16), 4), 'traffic': None,
+                            'peak_source': f'{how} (MEASURED_PEAKS.json) x2 for e4m3'}
+    line['e2e'] = {'value': round(e2e_ms / 1000.0, 4), 'unit': 's', 'h2d_bytes_per_step': headline * 8,
+                   'd2h_bytes_per_step': 8}
+    line['gpu_launches'] = launches * steps
+    line['clocks'] = clk
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.release_caches()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_other(args):
     global PROFILE_RANGE
     from sm120_attn.shard import kv_head_range, reduce_over_ranks
@@ -643,15 +740,23 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--profile-range', action='store_true',
                     help='bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)')
-    ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked'])
+    ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked', 'ttft'])
+    ap.add_argument('--contexts', default='65536,131072,262144',
+                    help='ttft workload: prompt lengths (the 131072 one is the reported value)')
     ap.add_argument('--fp8-kv-cache', action='store_true',
                     help='chunked workload: keep e4m3 K/V across chunks (SM120_SPARSE_FP8_KV_CACHE)')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'b200':
         print('note: warmup raised to 3', file=sys.stderr)
         args.warmup = 3
-    if args.impl == 'reference':
+    if args.impl == 'reference' and args.workload == 'ttft':
+        if int(os.environ.get('RANK', '0')) == 0:
+            print(json.dumps({'impl': 'reference', 'unavailable': 'config 5 (TTFT) has no CPU path in the reference: '
+                              'it is measured through a vLLM server on the GPU'}), flush=True)
+    elif args.impl == 'reference':
         run_reference(args)
+    elif args.workload == 'ttft':
+        run_ttft(args)
     elif args.workload == 'chunk':
         run_b200(args)
     else:

@@ -186,6 +186,32 @@ SA_API int sa_attn_fwd_bf16(const void* q, int64_t q_row_stride, int64_t q_head_
                      const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block, int kv_block,
                      float softmax_scale, int32_t* status, void* stream);
 
+/*
+ * Elementwise kernels of the end-to-end prefill harness (a random-init dense
+ * GQA decoder whose TTFT the reference measures through vLLM, scripts/bench_ttft.py:1-12).  The
+ * reference has no entry points of its own here: these compute what vLLM 0.22's model layers do
+ * (model_executor/layers/layernorm.py fused-add RMSNorm, rotary_embedding/base.py neox rotary
+ * embedding, activation.py SiluAndMul).  bf16 tensors, element strides, fp32 arithmetic.
+ */
+
+/* h <- bf16(h + delta) (delta may be NULL: no add), x <- bf16(s * rsqrt(mean(s^2) + eps) * weight)
+ * with s the fp32 sum; rows x hidden, hidden % 8 == 0 and <= 8192. */
+SA_API int sa_add_rmsnorm_bf16(const void* delta, int64_t delta_row_stride, void* h, int64_t h_row_stride,
+                               const void* weight, void* x, int64_t x_row_stride, int rows, int hidden, float eps,
+                               void* stream);
+
+/* qkv rows [q heads | k heads | v heads] x head_dim at positions pos0 + row: neox rotary embedding
+ * (element i < head_dim/2 pairs with i + head_dim/2) of the q and k heads with the fp32 table
+ * cos_sin [max_pos, head_dim] (cos of the head_dim/2 angles, then their sin); q goes to
+ * q_out [rows, num_heads, head_dim], k and v to k_out / v_out rows (heads contiguous). */
+SA_API int sa_rope_qkv_bf16(const void* qkv, int64_t qkv_row_stride, int rows, int num_heads, int num_kv_heads,
+                            int head_dim, const float* cos_sin, int pos0, int max_pos, void* q_out, void* k_out,
+                            int64_t k_row_stride, void* v_out, int64_t v_row_stride, void* stream);
+
+/* out[r, j] = silu(gate_up[r, j]) * gate_up[r, inter + j], j < inter (inter % 8 == 0). */
+SA_API int sa_silu_mul_bf16(const void* gate_up, int64_t gate_up_row_stride, int rows, int inter, void* out,
+                            int64_t out_row_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,9 @@ SIGNATURES = {
                         _i32, _i32, _p, _p, _i64, _i32, _i32, _p, _i32, _p, _i32, _p, _i32, _f32, _p, _p],
     'sa_attn_fwd_bf16': [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32,
                          _i32, _i32, _p, _p, _i64, _i32, _i32, _f32, _p, _p],
+    'sa_add_rmsnorm_bf16': [_p, _i64, _p, _i64, _p, _p, _i64, _i32, _i32, _f32, _p],
+    'sa_rope_qkv_bf16': [_p, _i64, _i32, _i32, _i32, _i32, _p, _i32, _i32, _p, _p, _i64, _p, _i64, _p],
+    'sa_silu_mul_bf16': [_p, _i64, _i32, _i32, _p, _i64, _p],
 }
 
 

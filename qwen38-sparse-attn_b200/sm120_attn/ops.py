@@ -144,3 +144,54 @@ def attn_bf16(q, k, v, out, kv_len: int, q_front: int, q_offset: int, counts, li
            v.stride(0), v.stride(1), _p(out), out.stride(0), out.stride(1), n, H, Hk, D, kv_len, q_front,
            q_offset, _p(counts), _p(lists), lists.stride(0) if lists is not None else 0, q_block, kv_block,
            float(softmax_scale), _p(st), _stream(q.device))
+
+
+# ---------------------------------------------------------------- end-to-end prefill harness kernels
+
+def _rows2d(name, t):
+    if t.dim() != 2 or t.stride(1) != 1 or t.dtype != torch.bfloat16:
+        raise ValueError(f'{name}: expected a bf16 [rows, cols] tensor with unit column stride')
+
+
+def add_rmsnorm(h, weight, x_out, eps: float, delta=None):
+    """h <- h + delta (when given); x_out <- rmsnorm(h) * weight (fp32 arithmetic); see sa_add_rmsnorm_bf16."""
+    _need_cuda('add_rmsnorm', h, weight, x_out, delta)
+    for name, t in (('h', h), ('x_out', x_out)) + ((('delta', delta),) if delta is not None else ()):
+        _rows2d(f'add_rmsnorm {name}', t)
+    rows, hidden = h.shape
+    if x_out.shape != h.shape or (delta is not None and delta.shape != h.shape) or weight.shape != (hidden,):
+        raise ValueError('add_rmsnorm: shape mismatch')
+    N.call('sa_add_rmsnorm_bf16', _p(delta), delta.stride(0) if delta is not None else 0, _p(h), h.stride(0),
+           _p(weight), _p(x_out), x_out.stride(0), rows, hidden, ctypes.c_float(eps), _stream(h.device))
+
+
+def rope_qkv(qkv, num_heads: int, num_kv_heads: int, head_dim: int, cos_sin, pos0: int, q_out, k_out, v_out):
+    """Rotary embedding of the q and k heads of qkv [rows, (H + 2 Hk) D] at positions pos0..; q to
+    q_out [rows, H, D], k and v to k_out / v_out [rows, Hk, D] (e.g. cache rows); see sa_rope_qkv_bf16."""
+    _need_cuda('rope_qkv', qkv, cos_sin, q_out, k_out, v_out)
+    _rows2d('rope_qkv qkv', qkv)
+    rows = qkv.shape[0]
+    if qkv.shape[1] != (num_heads + 2 * num_kv_heads) * head_dim:
+        raise ValueError('rope_qkv: qkv width does not match the head counts')
+    for t, hh in ((q_out, num_heads), (k_out, num_kv_heads), (v_out, num_kv_heads)):
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or t.shape[0] < rows or t.shape[1:] != (hh, head_dim) or \
+                t.stride(2) != 1 or t.stride(1) != head_dim:
+            raise ValueError('rope_qkv: outputs must be bf16 [rows, heads, head_dim] with contiguous heads')
+    if q_out.stride(0) != num_heads * head_dim:
+        raise ValueError('rope_qkv: q_out must be contiguous')
+    if cos_sin.dtype != torch.float32 or cos_sin.dim() != 2 or cos_sin.shape[1] != head_dim or not cos_sin.is_contiguous():
+        raise ValueError('rope_qkv: cos_sin must be a contiguous fp32 [max_pos, head_dim] table')
+    N.call('sa_rope_qkv_bf16', _p(qkv), qkv.stride(0), rows, num_heads, num_kv_heads, head_dim, _p(cos_sin), pos0,
+           cos_sin.shape[0], _p(q_out), _p(k_out), k_out.stride(0), _p(v_out), v_out.stride(0), _stream(qkv.device))
+
+
+def silu_mul(gate_up, out):
+    """out = silu(gate_up[:, :I]) * gate_up[:, I:] with I = out.shape[1]; see sa_silu_mul_bf16."""
+    _need_cuda('silu_mul', gate_up, out)
+    _rows2d('silu_mul gate_up', gate_up)
+    _rows2d('silu_mul out', out)
+    rows, inter = out.shape
+    if gate_up.shape != (rows, 2 * inter):
+        raise ValueError('silu_mul: gate_up must be [rows, 2 * inter]')
+    N.call('sa_silu_mul_bf16', _p(gate_up), gate_up.stride(0), rows, inter, _p(out), out.stride(0),
+           _stream(out.device))

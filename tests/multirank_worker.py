@@ -70,3 +70,47 @@ def run(rank, world, port, result_dir):
         Path(result_dir, f'ok{rank}').write_text('ok')
     finally:
         dist.destroy_process_group()
+
+
+TP_CFG = dict(layers=2, hidden=64, heads=8, kv_heads=2, head_dim=16, inter=96, vocab=48, init_std=0.1)
+
+
+def tp_logits(rank, world, all_reduce):
+    """Last-token logits of the tiny decoder from this rank's weight slices (fp32 torch on the CPU)."""
+    import math
+    import torch
+    from sm120_attn import decoder as dd
+    cfg = dd.DecoderConfig(**TP_CFG)
+    sh = dd.shard(cfg, rank, world)
+    weights = [dd.layer_weights(cfg, L, sh, 5, 'cpu') for L in range(cfg.layers)]
+    embed = dd.full_weight((cfg.vocab, cfg.hidden), dd._seed(5, -1, 'embed'), cfg.init_std, 'cpu')
+    v0, v1 = sh.vocab
+    lm = dd.full_weight((cfg.vocab, cfg.hidden), dd._seed(5, -1, 'lm_head'), cfg.init_std, 'cpu')[v0:v1]
+    ids = torch.randint(0, cfg.vocab, (40,), generator=torch.Generator().manual_seed(3))
+    attn = lambda L, q, k, v: dd.causal_attention(q, k, v, 1 / math.sqrt(cfg.head_dim))
+    return dd.reference_prefill(cfg, weights, embed, lm, ids, attn, all_reduce)
+
+
+def run_tp_decoder(rank, world, port, result_dir):
+    """Tensor-parallel decoder decomposition: each rank's head / intermediate / vocabulary slices
+    with all-reduces after the row-parallel projections give the unsharded model's logits."""
+    import torch
+    import torch.distributed as dist
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        def all_reduce(t):
+            t = t.contiguous()
+            dist.all_reduce(t)
+            return t
+        local = tp_logits(rank, world, all_reduce)
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local.contiguous())
+        got = torch.cat(parts, dim=1)
+        ref = tp_logits(0, 1, lambda t: t)
+        err = (got - ref).abs().max().item() / ref.abs().max().item()
+        assert err < 1e-5, err
+        Path(result_dir, f'ok{rank}').write_text(f'{err}')
+    finally:
+        dist.destroy_process_group()

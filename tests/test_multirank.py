@@ -36,3 +36,27 @@ def test_two_rank_kv_head_shards_match_unsharded(tmp_path):
     mp.start_processes(multirank_worker.run, args=(world, _free_port(), str(tmp_path)), nprocs=world,
                        start_method='spawn', join=True)
     assert sorted(p.name for p in tmp_path.iterdir()) == [f'ok{r}' for r in range(world)]
+
+
+def test_two_rank_tp_decoder_matches_unsharded(tmp_path):
+    """The C5 decoder's tensor-parallel split (KV-head / intermediate / vocabulary slices, all-reduce
+    after the row-parallel projections) reproduces the unsharded model on two gloo ranks."""
+    import torch.multiprocessing as mp
+    import multirank_worker
+    world = 2
+    mp.start_processes(multirank_worker.run_tp_decoder, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method='spawn', join=True)
+    assert sorted(p.name for p in tmp_path.iterdir()) == [f'ok{r}' for r in range(world)]
+
+
+def test_decoder_shards_partition():
+    from sm120_attn.decoder import DecoderConfig, shard
+    cfg = DecoderConfig()
+    for world in (1, 2, 4, 8):
+        got = [shard(cfg, r, world) for r in range(world)]
+        for field, total in (('q_heads', 64), ('kv_heads', 8), ('inter', 25600), ('vocab', 151936)):
+            spans = [getattr(s, field) for s in got]
+            assert spans[0][0] == 0 and spans[-1][1] == total
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    with pytest.raises(ValueError):
+        shard(cfg, 0, 3)
