@@ -505,6 +505,73 @@ def _chunked(args, h, hk, dev, rank):
                        'value_definition': 'executed-tile FLOPs (4 D 128 128 per kept 128x128 tile) / prefill time'}}
 
 
+def _hook(args, h, hk, dev, rank):
+    """Config 4 through the vLLM hook: the 262144-token prefill in 32 chunks of 8192, each chunk a
+    `try_sparse_forward` call over a paged K/V cache (page 16, pages in shuffled order, fake vLLM
+    metadata).  The reference's hook gathers the whole K/V history from the pages every chunk;
+    with --fp8-kv-cache the warm chunks read only their own pages."""
+    import types
+    import torch
+    import sm120_attn.sparse_prefill as ksp
+    import synth
+    from sm120_attn import ops
+    ksp.BLOCK = BLOCK
+    total, chunk, page = 262144, 8192, 16
+    q, k, v, _ = synth.make_qkv(total, total, h, hk, D, block=BLOCK, q_start=0, seed=4000 + rank,
+                                strength='strong', hot=16, local=4, device=dev)
+    npages = total // page
+    perm = torch.randperm(npages + 64, generator=torch.Generator().manual_seed(7))[:npages].to(dev)
+    key_cache = torch.empty(npages + 64, page, hk, D, dtype=torch.bfloat16, device=dev)
+    value_cache = torch.empty_like(key_cache)
+    key_cache[perm.long()] = k.view(npages, page, hk, D)
+    value_cache[perm.long()] = v.view(npages, page, hk, D)
+    del v
+    bt = perm.to(torch.int32).view(1, -1)
+    ksp._CONFIG = {'enabled': True, 'tau': TAU, 'min_kv': 8192, 'min_q': 1024, 'kernel': 'sm120fp8',
+                   'fp8_pipeline': 'tma', 'fp8_kv_cache': bool(args.fp8_kv_cache)}
+    ksp._STATE.clear()
+    impl = types.SimpleNamespace(sliding_window=(-1, -1), scale=D ** -0.5)
+    metas = [types.SimpleNamespace(causal=True, max_query_len=chunk, max_seq_len=(c + 1) * chunk,
+                                   query_start_loc=torch.tensor([0, chunk], dtype=torch.int32, device=dev),
+                                   seq_lens=torch.tensor([(c + 1) * chunk], dtype=torch.int32, device=dev),
+                                   block_table=bt) for c in range(total // chunk)]
+    out = torch.empty(chunk, h, D, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    per_chunk = []
+
+    def prefill(record=False):
+        for c, meta in enumerate(metas):
+            c0 = c * chunk
+            if record:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+            ksp.try_sparse_forward(impl, q[c0:c0 + chunk], k[c0:c0 + chunk], key_cache, value_cache, out, meta)
+            if record:
+                b.record(stream)
+                per_chunk.append((a, b, ksp._STATE[next(iter(ksp._STATE))].last_counts.sum()))
+    for _ in range(max(1, args.warmup // 3)):
+        prefill()
+    steps = max(1, min(args.steps, 3))
+    ms = _timed(prefill, steps, dev, int(os.environ.get('WORLD_SIZE', '1')))
+    prefill(record=True)
+    torch.cuda.synchronize(dev)
+    chunk_ms = [a.elapsed_time(b) for a, b, _ in per_chunk]
+    exec_flops = sum(int(n.item()) * 4.0 * D * 128 * 128 for _, _, n in per_chunk)
+    ops.check_status(dev)
+    ksp._CONFIG = None
+    return {'ms': ms, 'steps': steps, 'e2e_ms': None, 'work': exec_flops, 'unit': 'TFLOPS', 'scale': 1e12,
+            'kernel': 'attn_fwd_kernel<fp8>', 'kernel_ms': None, 'kernel_work': None, 'bound': 'tensor',
+            'h2d': 0, 'd2h': 0, 'launches': 7 * (total // chunk),
+            'config': {'workload': f'chunked prefill of {total} tokens in {total // chunk} chunks of {chunk} through '
+                                   f'the vLLM hook (try_sparse_forward) over a paged K/V cache (page {page}, shuffled '
+                                   f'pages); H {h}/Hk {hk}/D {D}, block {BLOCK}, tau {TAU}; C4 injection; '
+                                   + ('FP8 KV cache: warm chunks read only their own pages'
+                                      if args.fp8_kv_cache else 'whole K/V history gathered and re-quantised every '
+                                                                'chunk (reference behaviour)'),
+                       'ms_per_chunk': [round(x, 3) for x in chunk_ms],
+                       'value_definition': 'executed-tile FLOPs / prefill time (host metadata reads included)'}}
+
+
 def run_ttft(args):
     """Config 5: prefill TTFT of the random-init 64-layer GQA decoder (hidden 5120, 64/8 heads, SwiGLU
     25600, vocab 151936) over 65536 / 131072 / 262144 random token ids in 8192-token chunks, sparse
@@ -619,7 +686,8 @@ def run_other(args):
     h = hk * (H_FULL // HK_FULL)
     clocks = Clocks(local)
     clocks.start()
-    res = {'dense': _dense, 'selection': _selection, 'chunked': _chunked}[args.workload](args, h, hk, dev, rank)
+    res = {'dense': _dense, 'selection': _selection, 'chunked': _chunked, 'hook': _hook}[args.workload](
+        args, h, hk, dev, rank)
     clk = clocks.stop()
     steps = res.get('steps', args.steps)
     e2e_ms = res['e2e_ms'] if res['e2e_ms'] is not None else res['ms']
@@ -740,11 +808,11 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--profile-range', action='store_true',
                     help='bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)')
-    ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked', 'ttft'])
+    ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked', 'hook', 'ttft'])
     ap.add_argument('--contexts', default='65536,131072,262144',
                     help='ttft workload: prompt lengths (the 131072 one is the reported value)')
     ap.add_argument('--fp8-kv-cache', action='store_true',
-                    help='chunked workload: keep e4m3 K/V across chunks (SM120_SPARSE_FP8_KV_CACHE)')
+                    help='chunked / hook workloads: keep e4m3 K/V across chunks (SM120_SPARSE_FP8_KV_CACHE)')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'b200':
         print('note: warmup raised to 3', file=sys.stderr)

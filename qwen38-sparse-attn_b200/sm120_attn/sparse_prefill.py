@@ -184,25 +184,32 @@ class SparsePrefill:
         return out
 
     @torch.no_grad()
-    def forward_sm120fp8(self, q, k, v, q_start, out=None, km=None, scales=None, kv8=None):
+    def forward_sm120fp8(self, q, k, v, q_start, out=None, km=None, scales=None, kv8=None, k_rows=None):
         """FP8 (e4m3) path, 128-row query blocks; k, v NHD [T, Hk, D] bf16, quantised here.
 
         scales: (sq, sk, sv) python floats (per-request, per-layer, cached by the caller); without
         them per-call amax scales are used (three device syncs).  kv8: optional (k8, v8) uint8
         [kv_len, Hk, D] already quantised with these scales (`_cached_kv8`); then k and v are not
-        read here.
+        read here and may be None (with km and scales given), k_rows then standing for k.shape[0]
+        (the selection covers ceil(k_rows / BLOCK) key blocks, as with the key tensor itself).
         """
         BM = 128
         B = BLOCK
         n = q.shape[0]
         kv_len = q_start + n
-        assert k.shape[0] >= kv_len
+        if k is None or v is None:
+            if km is None or scales is None or kv8 is None:
+                raise ValueError('forward_sm120fp8: k and v may be omitted only with km, scales and kv8')
+            k_rows = kv_len if k_rows is None else k_rows
+        else:
+            k_rows = k.shape[0] if k_rows is None else k_rows
+        assert k_rows >= kv_len
         front = q_start % BM
         M = _cdiv(front + n, BM) * BM
         MB = M // B
         qs = q_start - front
         dev = q.device
-        need = max(_cdiv(k.shape[0], B) * B, qs + M)
+        need = max(_cdiv(k_rows, B) * B, qs + M)
         nb_need = need // B
         t0 = self._tick()
         if km is None:
@@ -417,14 +424,15 @@ def _cached_block_means(layer_key, first_page, key_chunk, q_start, kv_len, key_a
 _KV8_CACHE: dict = {}
 
 
-def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales):
+def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
     """Per-(layer, request) e4m3 K and V [kv_len, Hk, D] (uint8 views), each row quantised once.
 
     The FP8 path quantises the whole key/value history with the request's scales on every chunk
     (sparse_prefill.py:230-233); the scales are cached per request, so rows quantised for an earlier
     chunk never change.  An entry contiguous with this chunk (its last row is q_start) and made with
-    the same scales only quantises rows q_start..kv_len; otherwise it is rebuilt from k, v (NHD, at
-    least kv_len rows).  The bytes are the same as re-quantising the history.
+    the same scales only quantises rows q_start..kv_len; otherwise it is rebuilt from k, v (NHD).
+    k and v hold sequence rows k_row0 .. k_row0 + len (k_row0 > 0 only for a contiguous entry: a
+    rebuild needs every row from 0).  The bytes are the same as re-quantising the history.
     """
     sk, sv = float(scales[1]), float(scales[2])
     key = (layer_key, first_page)
@@ -432,6 +440,8 @@ def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales):
     Hk, D = k.shape[1], k.shape[2]
     dev = k.device
     if entry is None or q_start == 0 or entry['rows'] != q_start or entry['scales'] != (sk, sv):
+        if k_row0:
+            raise RuntimeError('stale FP8 KV cache entry and no key/value rows before %d to rebuild it' % k_row0)
         if len(_KV8_CACHE) >= _KMEAN_MAX_ENTRIES:
             _KV8_CACHE.pop(next(iter(_KV8_CACHE)))
         cap = max(kv_len, 8192)
@@ -447,10 +457,22 @@ def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales):
             grown[:lo] = entry[name][:lo]
             entry[name] = grown
     if kv_len > lo:
-        ops.quantize(k[lo:kv_len], entry['inv'][0:1], SA_QUANT_MUL_BF16, entry['k8'][lo:kv_len])
-        ops.quantize(v[lo:kv_len], entry['inv'][1:2], SA_QUANT_MUL_BF16, entry['v8'][lo:kv_len])
+        if k.shape[0] < kv_len - k_row0 or v.shape[0] < kv_len - k_row0 or lo < k_row0:
+            raise ValueError('_cached_kv8: k/v do not hold rows %d..%d' % (lo, kv_len))
+        ops.quantize(k[lo - k_row0:kv_len - k_row0], entry['inv'][0:1], SA_QUANT_MUL_BF16, entry['k8'][lo:kv_len])
+        ops.quantize(v[lo - k_row0:kv_len - k_row0], entry['inv'][1:2], SA_QUANT_MUL_BF16, entry['v8'][lo:kv_len])
     entry['rows'] = kv_len
     return entry['k8'][:kv_len], entry['v8'][:kv_len]
+
+
+def _fp8_warm(layer_key, first_page, q_start) -> bool:
+    """True when the block-mean, scale and FP8 KV caches of this (layer, request) all continue at
+    q_start, so a chunk needs none of the key/value history (only its own rows)."""
+    key = (layer_key, first_page)
+    km, sc, kv = _KMEAN_CACHE.get(key), _SCALE_CACHE.get(key), _KV8_CACHE.get(key)
+    return (q_start > 0 and km is not None and km.get('last_kv') == q_start and km['nb'] >= q_start // BLOCK
+            and sc is not None and sc['last_kv'] == q_start and kv is not None and kv['rows'] == q_start
+            and kv['scales'] == (float(sc['scales'][1]), float(sc['scales'][2])))
 
 
 _SCALE_CACHE: dict = {}
@@ -519,6 +541,20 @@ def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_me
             _dense_request(impl, q_r, key_cache, value_cache, o_r, bt[r], n, kv_len)
             continue
         npages = -(-kv_len // page)
+        q_start = kv_len - n
+        if sp.kernel == 'sm120fp8' and cfg['fp8_kv_cache'] and _fp8_warm(id(impl), first_pages[r], q_start):
+            # Block means, scales and the e4m3 history are cached: only this chunk's pages are read
+            # (the reference gathers the whole history every chunk, sparse_prefill.py:521-522).
+            p0 = q_start // page
+            pages = bt[r, p0:npages].long()
+            kc = key_cache[pages].reshape(-1, Hk, D)
+            vc = value_cache[pages].reshape(-1, Hk, D)
+            km = _cached_block_means(id(impl), first_pages[r], key[qsl[r]:qsl[r + 1]], q_start, kv_len)
+            scales = _cached_scales(id(impl), first_pages[r], q_r, None, None, q_start)
+            kv8 = _cached_kv8(id(impl), first_pages[r], kc, vc, q_start, kv_len, scales, k_row0=p0 * page)
+            sp.forward_sm120fp8(q_r, None, None, q_start, out=o_r, km=km, scales=scales, kv8=kv8,
+                                k_rows=npages * page)
+            continue
         pages = bt[r, :npages].long()
         k = key_cache[pages].reshape(npages * page, Hk, D)    # one gather copy, NHD
         v = value_cache[pages].reshape(npages * page, Hk, D)
@@ -526,7 +562,7 @@ def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_me
         if sp.kernel == 'sm120fp8':
             scales = _cached_scales(id(impl), first_pages[r], q_r, k[:kv_len], v[:kv_len], kv_len - n)
             kv8 = (_cached_kv8(id(impl), first_pages[r], k, v, kv_len - n, kv_len, scales)
-                   if config()['fp8_kv_cache'] else None)
+                   if cfg['fp8_kv_cache'] else None)
             sp.forward_sm120fp8(q_r, k, v, kv_len - n, out=o_r, km=km, scales=scales, kv8=kv8)
         else:
             sp.forward_sm120(q_r, k, v, kv_len - n, out=o_r, km=km)

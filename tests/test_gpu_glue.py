@@ -13,6 +13,7 @@ import types
 import numpy as np
 import pytest
 import torch
+import torch.nn.functional as F
 
 import oracle as O
 import synth
@@ -340,3 +341,52 @@ def test_try_sparse_forward_paged(ksp, monkeypatch, kv_cache):
         assert rel_l2(f32(output[qsl[r]:qsl[r + 1]]), f32(o)) < 1e-6
     assert torch.all(output[qsl[1]:qsl[2]] == 0)
     assert len(ksp._KV8_CACHE) == (2 if kv_cache else 0)
+
+
+def test_hook_fp8_kv_cache_reads_only_chunk_pages(ksp, monkeypatch):
+    """Three chunks of one request through the vLLM hook (1000-row chunks: boundaries off the page
+    and block grid).  With the FP8 KV cache on, chunks after the first read only their own pages of
+    the paged cache (the block means, scales and e4m3 history are cached) and give the same output,
+    bit for bit, as the path that gathers and re-quantises the whole history every chunk."""
+    ksp.BLOCK = 64
+    H, Hk, D, page, n, chunks = 8, 2, 128, 16, 1000, 3
+    total = n * chunks
+    npages_all = -(-total // page)
+    q, k, v, _ = synth.make_qkv(total, total, H, Hk, D, block=64, q_start=0, seed=23, strength='strong')
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    perm = torch.randperm(npages_all + 5, generator=torch.Generator().manual_seed(4))[:npages_all].to(DEV)
+    key_cache = torch.zeros(npages_all + 5, page, Hk, D, dtype=torch.bfloat16, device=DEV)
+    value_cache = torch.zeros_like(key_cache)
+    key_cache[perm.long()] = F.pad(kd, (0, 0, 0, 0, 0, npages_all * page - total)).view(npages_all, page, Hk, D)
+    value_cache[perm.long()] = F.pad(vd, (0, 0, 0, 0, 0, npages_all * page - total)).view(npages_all, page, Hk, D)
+    bt = perm.to(torch.int32).view(1, -1)
+    calls = []
+    real = ksp._cached_kv8
+
+    def spy(*a, **kw):
+        calls.append((a[2].shape[0], kw.get('k_row0', 0)))
+        return real(*a, **kw)
+    monkeypatch.setattr(ksp, '_cached_kv8', spy)
+    outs = {}
+    for kv_cache in (False, True):
+        monkeypatch.setattr(ksp, '_CONFIG', {'enabled': True, 'tau': 0.95, 'min_kv': 512, 'min_q': 512,
+                                             'kernel': 'sm120fp8', 'fp8_pipeline': 'tma', 'fp8_kv_cache': kv_cache})
+        ksp._STATE.clear()
+        impl = types.SimpleNamespace(sliding_window=(-1, -1), scale=D ** -0.5)
+        outs[kv_cache] = []
+        for c in range(chunks):
+            c0, kv_len = c * n, (c + 1) * n
+            meta = types.SimpleNamespace(causal=True, max_query_len=n, max_seq_len=kv_len,
+                                         query_start_loc=torch.tensor([0, n], dtype=torch.int32, device=DEV),
+                                         seq_lens=torch.tensor([kv_len], dtype=torch.int32, device=DEV), block_table=bt)
+            out = torch.zeros(n, H, D, dtype=torch.bfloat16, device=DEV)
+            assert ksp.try_sparse_forward(impl, qd[c0:kv_len], kd[c0:kv_len], key_cache, value_cache, out, meta)
+            outs[kv_cache].append(out)
+    torch.cuda.synchronize()
+    for a, b in zip(outs[False], outs[True]):
+        assert torch.equal(a, b)
+    # cache on: chunk 0 builds the entry from the full gather, chunks 1 and 2 pass only their pages
+    assert calls[0] == (-(-n // page) * page, 0)
+    for c in (1, 2):
+        p0 = c * n // page
+        assert calls[c] == ((-(-(c + 1) * n // page) - p0) * page, p0 * page)

@@ -203,6 +203,38 @@ def test_cached_kv8_quantises_each_row_once(ksp, monkeypatch):
     ksp._KV8_CACHE.clear()
 
 
+def test_fp8_warm_and_chunk_rows(ksp, monkeypatch):
+    """_fp8_warm is true only when the block-mean, scale and FP8 KV caches all continue at q_start;
+    a warm FP8 KV entry accepts just the chunk's rows (k_row0 > 0) and a stale one refuses them."""
+    from sm120_attn import ops
+    calls = []
+
+    def fake_quantize(x, scale, mode, out, transpose=False, rows_pad=0):
+        calls.append(x.shape[0])
+        out.copy_((x.float() * scale.reshape(1, 1, 1)).round().clamp(-100, 100).to(torch.int8).view(torch.uint8))
+
+    monkeypatch.setattr(ops, 'quantize', fake_quantize)
+    ksp.BLOCK = 64
+    g = torch.Generator().manual_seed(0)
+    k = torch.randn(4000, 2, 8, generator=g).to(torch.bfloat16)
+    v = torch.randn(4000, 2, 8, generator=g).to(torch.bfloat16)
+    q = torch.randn(1000, 4, 8, generator=g).to(torch.bfloat16)
+    assert not ksp._fp8_warm('W', 1, 1000)
+    ksp._cached_block_means('W', 1, k[:1000], 0, 1000)
+    sc = ksp._cached_scales('W', 1, q, k[:1000], v[:1000], 0)
+    assert not ksp._fp8_warm('W', 1, 1000)                              # no FP8 KV entry yet
+    k8, _ = ksp._cached_kv8('W', 1, k, v, 0, 1000, sc)
+    assert ksp._fp8_warm('W', 1, 1000)
+    assert not ksp._fp8_warm('W', 1, 1200) and not ksp._fp8_warm('W', 1, 0) and not ksp._fp8_warm('W', 2, 1000)
+    calls.clear()
+    k8b, v8b = ksp._cached_kv8('W', 1, k[992:2000], v[992:2000], 1000, 2000, sc, k_row0=992)
+    assert calls == [1000, 1000] and k8b.shape[0] == 2000 and torch.equal(k8b[:1000], k8)
+    full, _ = ksp._cached_kv8('X', 1, k, v, 0, 2000, sc)                 # the same rows quantised in one go
+    assert torch.equal(full, k8b)
+    with pytest.raises(RuntimeError):                                    # gap: a rebuild needs rows from 0
+        ksp._cached_kv8('W', 1, k[2992:], v[2992:], 3000, 3500, sc, k_row0=2992)
+
+
 def test_block_masks_rejects_unpadded_input(ksp):
     sp = ksp.SparsePrefill(8, 2, 128, 'cpu')
     ksp.BLOCK = 64
