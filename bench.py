@@ -199,30 +199,65 @@ def run_b200(args):
     kept = kept_blocks / causal_blocks
     flops = causal_flops(h, D, N_Q, KV) * kept
     tile_flops = kept_blocks * 4.0 * D * 128 * 128
-    # ---------------- end-to-end through the public API with pinned host buffers
+    # ---------------- end-to-end through the public API with pinned host buffers.  Every step copies
+    # its chunk's q, k and v in from pinned host memory and its output back; two device buffer sets
+    # and two copy streams let step i+1's upload and step i-1's download run under step i's compute
+    # (a serving loop's double buffering).  The timed region spans the first upload to the last
+    # download.
     q_h = q.cpu().pin_memory()
     k_h = k[Q_START:].cpu().pin_memory()
     v_h = v[Q_START:].cpu().pin_memory()
-    o_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_d = torch.empty_like(q)
+    o_h = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+    bufs = [(torch.empty_like(q), k.clone(), v.clone(), torch.empty_like(out)) for _ in range(2)]
+    cs_in, cs_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        q_d.copy_(q_h, non_blocking=True)
-        k[Q_START:].copy_(k_h, non_blocking=True)
-        v[Q_START:].copy_(v_h, non_blocking=True)
+    def upload(i):
+        qd, kb, vb, _ = bufs[i % 2]
+        cs_in.wait_event(comp_done[i % 2])                       # step i-2 has finished with the set
+        with torch.cuda.stream(cs_in):
+            qd.copy_(q_h, non_blocking=True)
+            kb[Q_START:].copy_(k_h, non_blocking=True)
+            vb[Q_START:].copy_(v_h, non_blocking=True)
+            in_ready[i % 2].record(cs_in)
+
+    def compute(i):
+        qd, kb, vb, ob = bufs[i % 2]
+        stream.wait_event(in_ready[i % 2])
+        stream.wait_event(out_done[i % 2])                        # step i-2's output has left the set
         rewind()
-        step(q_d, k[Q_START:])
-        o_h.copy_(out, non_blocking=True)
+        km = ksp._cached_block_means(layer, 0, kb[Q_START:], Q_START, KV)
+        sp.forward_sm120fp8(qd, kb, vb, Q_START, out=ob, km=km, scales=scales)
+        comp_done[i % 2].record(stream)
 
-    for _ in range(max(1, args.warmup)):
-        e2e_step()
+    def download(i):
+        cs_out.wait_event(comp_done[i % 2])
+        with torch.cuda.stream(cs_out):
+            o_h[i % 2].copy_(bufs[i % 2][3], non_blocking=True)
+            out_done[i % 2].record(cs_out)
+
+    def e2e_run(n_steps, start_event=None):
+        if start_event is not None:
+            cs_in.wait_event(start_event)
+        upload(0)
+        for i in range(n_steps):
+            if i + 1 < n_steps:
+                upload(i + 1)
+            compute(i)
+            download(i)
+        for b in range(2):
+            stream.wait_event(out_done[b])
+
+    e2e_run(max(2, args.warmup))
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    e2e_run(args.steps, e0)
     e1.record(stream)
     barrier()
+    o_h = o_h[0]
     e2e_ms = e0.elapsed_time(e1)
     clk = clocks.stop()
     h2d = q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2
@@ -268,7 +303,8 @@ def run_b200(args):
         },
         'e2e': {'value': round(e2e_val, 2), 'unit': 'TFLOPS', 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
                 'ms_per_step': round(e2e_ms / args.steps, 4),
-                'path': 'pinned host q/k/v of the chunk -> SparsePrefill.forward_sm120fp8 -> pinned host output'},
+                'path': 'pinned host q/k/v of the chunk -> SparsePrefill.forward_sm120fp8 -> pinned host output; '
+                        'double-buffered: uploads and downloads on two copy streams overlap neighbouring steps\' compute'},
         'gpu_launches': LAUNCHES_PER_STEP * args.steps,
         'clocks': clk,
     }

@@ -219,7 +219,8 @@ class SparsePrefill:
                               for t in (q, k, v)]).clamp_min_(1e-6).tolist()
             scales = tuple(a / 448.0 for a in amax)
         sq, sk, sv = scales
-        inv = torch.tensor([1.0 / sq, 1.0 / sk, 1.0 / sv], dtype=torch.float32).to(dev, non_blocking=True)
+        st = _scale_tensor(dev, sq, sk, sv)
+        inv, sc = st[0:3], st[3:6]
         q8 = torch.empty(n, self.H, self.D, dtype=torch.uint8, device=dev)
         qm = self._pool_q(q, q_start, qs, MB, q8=q8, inv_scale=inv[0:1])
         rows = self.H * (M // BM)
@@ -238,7 +239,6 @@ class SparsePrefill:
             ops.quantize(v[:kv_len], inv[2:3], SA_QUANT_MUL_BF16, v8)
         t1 = self._tick()
         o, copy_back = self._out(out, n, dev)
-        sc = torch.tensor([sq, sk, sv], dtype=torch.float32).to(dev, non_blocking=True)
         ev0, ev1 = self._attn_events()
         if ev0 is not None:
             ev0.record()
@@ -421,6 +421,29 @@ def _cached_block_means(layer_key, first_page, key_chunk, q_start, kv_len, key_a
     return entry['km'][:, :b1]
 
 
+_SCALE_TENSORS: dict = {}
+
+
+def _scale_tensor(dev, sq, sk, sv):
+    """Device fp32 [1/sq, 1/sk, 1/sv, sq, sk, sv] for one scale triple, kept per (device, triple).
+
+    A host tensor copied from pageable memory makes the copy wait for the whole stream (a device
+    sync every chunk); the triple is fixed per request and layer, so it is staged once through
+    pinned memory and reused."""
+    dev = torch.device(dev)
+    if dev.type != 'cuda':                                      # host-side tests with fake ops
+        return torch.tensor([1.0 / sq, 1.0 / sk, 1.0 / sv, sq, sk, sv], dtype=torch.float32, device=dev)
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), float(sq), float(sk), float(sv))
+    hit = _SCALE_TENSORS.get(key)
+    if hit is None:
+        if len(_SCALE_TENSORS) >= 4 * _KMEAN_MAX_ENTRIES:
+            _SCALE_TENSORS.pop(next(iter(_SCALE_TENSORS)))
+        host = torch.tensor([1.0 / sq, 1.0 / sk, 1.0 / sv, sq, sk, sv], dtype=torch.float32).pin_memory()
+        hit = (host.to(dev, non_blocking=True), host)          # the pinned source lives as long as the entry
+        _SCALE_TENSORS[key] = hit
+    return hit[0]
+
+
 _KV8_CACHE: dict = {}
 
 
@@ -447,7 +470,7 @@ def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
         cap = max(kv_len, 8192)
         entry = {'k8': torch.empty(cap, Hk, D, dtype=torch.uint8, device=dev),
                  'v8': torch.empty(cap, Hk, D, dtype=torch.uint8, device=dev), 'rows': 0, 'scales': (sk, sv),
-                 'inv': torch.tensor([1.0 / sk, 1.0 / sv], dtype=torch.float32).to(dev, non_blocking=True)}
+                 'inv': _scale_tensor(dev, scales[0], sk, sv)[1:3]}
         _KV8_CACHE[key] = entry
     lo = entry['rows']
     if entry['k8'].shape[0] < kv_len:
@@ -518,8 +541,11 @@ def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_me
         return False
     if torch.cuda.is_current_stream_capturing():
         return False
-    qsl = attn_metadata.query_start_loc.tolist()
-    seq_lens = attn_metadata.seq_lens.tolist()
+    # host copies of the metadata when the backend keeps them (no device read), else the device tensors
+    qsl = getattr(attn_metadata, 'query_start_loc_cpu', None)
+    qsl = (qsl if qsl is not None else attn_metadata.query_start_loc).tolist()
+    seq_lens = getattr(attn_metadata, 'seq_lens_cpu', None)
+    seq_lens = (seq_lens if seq_lens is not None else attn_metadata.seq_lens).tolist()
     nreq = len(seq_lens)
     eligible = [r for r in range(nreq) if qsl[r + 1] - qsl[r] >= cfg['min_q'] and seq_lens[r] >= cfg['min_kv']]
     if not eligible:
