@@ -624,7 +624,8 @@ def run_ttft(args):
     cfg = DecoderConfig()
     t_init = time.perf_counter()
     model = TPDecoder(cfg, dev, rank=rank, world=world, group=None, seed=0, tau=TAU, kernel='sm120fp8',
-                      fp8_kv_cache=args.fp8_kv_cache, max_tokens=contexts[-1], chunk=8192, min_kv=8192)
+                      fp8_kv_cache=args.fp8_kv_cache, max_tokens=contexts[-1], chunk=8192, min_kv=8192,
+                      comm_blocks=args.comm_blocks)
     torch.cuda.synchronize(dev)
     t_init = time.perf_counter() - t_init
     g = torch.Generator()
@@ -682,7 +683,8 @@ def run_ttft(args):
                    'kept_fraction': {str(T): kept[T] for T in keys},
                    'first_token': {str(T): first_tok[T] for T in keys}, 'fp8_kv_cache': bool(args.fp8_kv_cache),
                    'parallelism': f'tensor parallel by KV head x{world} (NCCL all-reduce after o_proj and '
-                                  f'down_proj, all-gather of the last-token logits)',
+                                  f'down_proj in {model.comm_blocks} row block(s), each overlapping the next '
+                                  f'block\'s GEMMs; all-gather of the last-token logits)',
                    'gemm_tflops_per_gpu': round(gemm_flops / world / (ttft[headline] * 1e-3) / 1e12, 1),
                    'attention_ms_of_ttft': round(attn_ms, 1), 'model_init_s': round(t_init, 1),
                    'params': cfg.params(), 'l2': 'inputs larger than L2; no flush'},
@@ -845,6 +847,8 @@ def main():
     ap.add_argument('--profile-range', action='store_true',
                     help='bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)')
     ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked', 'hook', 'ttft'])
+    ap.add_argument('--comm-blocks', type=int, default=2,
+                    help='ttft workload: row blocks whose all-reduces overlap the next block\'s GEMMs (1: none)')
     ap.add_argument('--contexts', default='65536,131072,262144',
                     help='ttft workload: prompt lengths (the 131072 one is the reported value)')
     ap.add_argument('--fp8-kv-cache', action='store_true',

@@ -122,7 +122,7 @@ class TPDecoder:
 
     def __init__(self, cfg: DecoderConfig, device, rank: int = 0, world: int = 1, group=None, seed: int = 0,
                  tau: float = 0.95, kernel: str = 'sm120fp8', fp8_kv_cache: bool = False, max_tokens: int = 131072,
-                 chunk: int = 8192, min_kv: int = 8192):
+                 chunk: int = 8192, min_kv: int = 8192, comm_blocks: int = 2):
         self.cfg, self.device, self.rank, self.world, self.group = cfg, torch.device(device), rank, world, group
         self.sh = shard(cfg, rank, world)
         self.hq = self.sh.q_heads[1] - self.sh.q_heads[0]
@@ -149,6 +149,12 @@ class TPDecoder:
                     'o': torch.empty(c, E, dtype=bf, device=dev), 'gu': torch.empty(c, 2 * self.il, dtype=bf, device=dev),
                     'a': torch.empty(c, self.il, dtype=bf, device=dev), 'd': torch.empty(c, E, dtype=bf, device=dev)}
         self._key = ('tp-decoder', id(self))
+        # With several ranks the row-parallel projections run in `comm_blocks` row blocks whose
+        # all-reduces go to a side stream, each overlapping the next block's GEMMs (1: no overlap).
+        self.comm_blocks = max(1, int(comm_blocks)) if world > 1 else 1
+        if self.comm_blocks > 1:
+            self.comm_stream = torch.cuda.Stream(dev)
+            self._ev = [[torch.cuda.Event() for _ in range(self.comm_blocks)] for _ in range(4)]
 
     def _all_reduce(self, t):
         if self.world > 1:
@@ -186,6 +192,9 @@ class TPDecoder:
                 ops.rope_qkv(qkv, self.hq, self.hk, D, self.cos_sin, c0, q, self.k_cache[L][c0:c0 + n],
                              self.v_cache[L][c0:c0 + n])
                 self._attention(L, q, c0, n, attn)
+                if self.comm_blocks > 1:
+                    self._mlp_overlapped(W, attn.view(n, self.hq * D), h, x, o, gu, a, d, n)
+                    continue
                 torch.matmul(attn.view(n, self.hq * D), W['o'].t(), out=o)
                 self._all_reduce(o)
                 ops.add_rmsnorm(h, W['ln2'], x, cfg.eps, delta=o)
@@ -193,6 +202,8 @@ class TPDecoder:
                 ops.silu_mul(gu, a)
                 torch.matmul(a, W['down'].t(), out=d)
                 self._all_reduce(d)
+        if self.comm_blocks > 1:
+            torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
         last = slice(n - 1, n)
         x1 = b['x'][last]
         ops.add_rmsnorm(b['h'][last], self.final_norm, x1, cfg.eps, delta=b['d'][last])
@@ -202,6 +213,36 @@ class TPDecoder:
             torch.distributed.all_gather(parts, logits, group=self.group)
             logits = torch.cat(parts, dim=1)
         return logits[0] if return_logits else logits.argmax(dim=1)[0]
+
+    def _mlp_overlapped(self, W, attn2d, h, x, o, gu, a, d, n):
+        """o = attn W_o^T, all-reduce, h += o, x = rmsnorm(h), MLP, d = a W_down^T, all-reduce, in row
+        blocks: block j's all-reduce runs on the side stream while block j+1's GEMMs run; the last
+        block's all-reduce of d is the only one the compute stream waits for unoverlapped."""
+        cfg, cur, comm = self.cfg, torch.cuda.current_stream(self.device), self.comm_stream
+        nb = self.comm_blocks
+        step = -(-n // nb)
+        blocks = [(r, min(n, r + step)) for r in range(0, n, step)]
+        ev_o, done_o, ev_d, done_d = self._ev
+        comm.wait_stream(cur)                                    # buffers are free (previous layer's use done)
+        for j, (r0, r1) in enumerate(blocks):
+            torch.matmul(attn2d[r0:r1], W['o'].t(), out=o[r0:r1])
+            ev_o[j].record(cur)
+            comm.wait_event(ev_o[j])
+            with torch.cuda.stream(comm):
+                torch.distributed.all_reduce(o[r0:r1], group=self.group)
+                done_o[j].record(comm)
+        for j, (r0, r1) in enumerate(blocks):
+            cur.wait_event(done_o[j])
+            ops.add_rmsnorm(h[r0:r1], W['ln2'], x[r0:r1], cfg.eps, delta=o[r0:r1])
+            torch.matmul(x[r0:r1], W['gate_up'].t(), out=gu[r0:r1])
+            ops.silu_mul(gu[r0:r1], a[r0:r1])
+            torch.matmul(a[r0:r1], W['down'].t(), out=d[r0:r1])
+            ev_d[j].record(cur)
+            comm.wait_event(ev_d[j])
+            with torch.cuda.stream(comm):
+                torch.distributed.all_reduce(d[r0:r1], group=self.group)
+                done_d[j].record(comm)
+        cur.wait_stream(comm)
 
     def release_caches(self):
         """Drop this model's entries from the module-level block-mean, scale and FP8 KV caches."""
