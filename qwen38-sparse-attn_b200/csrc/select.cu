@@ -222,12 +222,10 @@ __device__ uint64_t select_row_regs(const float* __restrict__ L, int nbc, float 
             if (lane + 32 * c < nbc) keep |= 1ull << c;
         return keep;
     }
-    // largest v (bit pattern) with fp32(sum_{p >= v} p) >= tau: pred(lo) true, pred(hi) false;
-    // v* <= max p, so the search starts below max p's successor
-    uint32_t lo = 0u, hi = __float_as_uint(warp_max_f(pmax)) + 1u;
-    while (hi - lo > 1u) {
-        const uint32_t mid = lo + ((hi - lo) >> 1);
-        const float v = __uint_as_float(mid);
+    // largest v (bit pattern) with fp32(sum_{p >= v} p in float64) >= tau: pred(lo) true, pred(hi)
+    // false; v* <= max p, so the search starts below max p's successor.
+    auto pred64 = [&](uint32_t bits) -> bool {
+        const float v = __uint_as_float(bits);
         double m0 = 0.0, m1 = 0.0, m2 = 0.0, m3 = 0.0;
 #pragma unroll
         for (int c = 0; c < NPL; ++c) {
@@ -239,8 +237,35 @@ __device__ uint64_t select_row_regs(const float* __restrict__ L, int nbc, float 
             else if ((c & 3) == 2) m2 += d;
             else m3 += d;
         }
-        const double m = warp_sum_d((m0 + m1) + (m2 + m3));
-        if (static_cast<float>(m) >= tau_f) lo = mid; else hi = mid;
+        return static_cast<float>(warp_sum_d((m0 + m1) + (m2 + m3))) >= tau_f;
+    };
+    const uint32_t top = __float_as_uint(warp_max_f(pmax)) + 1u;
+    // The search itself sums in fp32 (shorter dependency chains, half the shuffles); its boundary
+    // is then checked with the float64 predicate, and searched again in float64 in the rare rows
+    // where the two disagree there (a mass within fp32 rounding of tau), so the result is the
+    // float64 one exactly.
+    uint32_t lo = 0u, hi = top;
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + ((hi - lo) >> 1);
+        const float v = __uint_as_float(mid);
+        float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll
+        for (int c = 0; c < NPL; ++c) {
+            const float d = (p[c] >= v) ? p[c] : 0.f;
+            if ((c & 3) == 0) m0 += d;
+            else if ((c & 3) == 1) m1 += d;
+            else if ((c & 3) == 2) m2 += d;
+            else m3 += d;
+        }
+        if (warp_sum_f((m0 + m1) + (m2 + m3)) >= tau_f) lo = mid; else hi = mid;
+    }
+    if (!(pred64(lo) && (hi == top || !pred64(hi)))) {
+        lo = 0u;
+        hi = top;
+        while (hi - lo > 1u) {
+            const uint32_t mid = lo + ((hi - lo) >> 1);
+            if (pred64(mid)) lo = mid; else hi = mid;
+        }
     }
     const float vstar = __uint_as_float(lo);
     double above = 0.0;
