@@ -326,3 +326,55 @@ def test_attn_fp8_list_with_future_padding_block():
     ref = O.attention_ref(_deq(q8, scales[0]), _deq(k8, scales[1]), _deq(v8, scales[2]), q_pos0, masks,
                           q_block=128, kv_block=64, q_front=front)
     assert rel_l2(out, ref) < 3e-2
+
+
+def _random_shapes(seed, count):
+    """Seeded attention shapes: ragged and single-row chunks, chunk offsets off the 128 grid, GQA
+    ratios 1-8, 64- and 128-key blocks, list densities from forced-blocks-only to near-dense."""
+    rng = np.random.default_rng(seed)
+    heads = [(1, 1), (2, 1), (8, 8), (16, 2), (8, 1), (4, 2)]
+    out = []
+    for i in range(count):
+        n = int(rng.choice([1, 3, 127, 128, 129, int(rng.integers(2, 1500))]))
+        kv = n + int(rng.integers(0, 4000))
+        H, Hk = heads[int(rng.integers(len(heads)))]
+        out.append((n, kv, H, Hk, int(rng.choice([64, 128])), float(rng.choice([0.0, 0.05, 0.3, 0.9])),
+                    int(rng.integers(0, 128)), 1000 + i))
+    return out
+
+
+@pytest.mark.parametrize('n,kv,H,Hk,kv_block,density,front,seed', _random_shapes(7, 10))
+def test_attn_fp8_random_shapes(n, kv, H, Hk, kv_block, density, front, seed):
+    """Sweep of the FP8 kernel over seeded shapes: the chunk's first row sits `front` rows into its
+    128-row tile (q_front); lists from random masks plus the sink and diagonal blocks."""
+    _, (q8, k8, v8), scales = _fp8_case(n, kv, H, Hk, seed=seed, per_head=bool(seed & 1))
+    q_pos0 = kv - n
+    front = min(front, q_pos0)                        # the tile cannot start before position 0
+    q_offset = q_pos0 - front
+    n_tiles = -(-(front + n) // 128)
+    NB = -(-kv // kv_block)
+    masks = _random_tile_masks(H, n_tiles, NB, q_offset, kv_block, density, seed=seed)
+    counts, lists = _lists_from_masks(masks)
+    out = _run_fp8(q8, k8, v8, scales, kv, front, q_offset, counts, lists, kv_block)
+    assert np.isfinite(out).all()
+    ref = O.attention_ref(_deq(q8, scales[0]), _deq(k8, scales[1]), _deq(v8, scales[2]), q_pos0, masks,
+                          q_block=128, kv_block=kv_block, q_front=front)
+    model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, q_pos0, counts.cpu().numpy(), lists.cpu().numpy(),
+                                         q_block=128, kv_block=kv_block, q_front=front)
+    assert rel_l2(out, model) < 1e-2, rel_l2(out, model)
+    assert rel_l2(out, ref) < 3e-2, rel_l2(out, ref)
+
+
+@pytest.mark.parametrize('n,kv,H,Hk,kv_block,density,front,seed', _random_shapes(11, 8))
+def test_attn_bf16_random_shapes(n, kv, H, Hk, kv_block, density, front, seed):
+    q, k, v, _ = synth.make_qkv(n, kv, H, Hk, 128, seed=seed)
+    q_pos0 = kv - n
+    front = min(front, q_pos0)
+    q_offset = q_pos0 - front
+    n_tiles = -(-(front + n) // 128)
+    NB = -(-kv // kv_block)
+    masks = _random_tile_masks(H, n_tiles, NB, q_offset, kv_block, density, seed=seed)
+    counts, lists = _lists_from_masks(masks)
+    out = _run_bf16(q, k, v, kv, front, q_offset, counts, lists, kv_block)
+    ref = O.attention_ref(f32(q), f32(k), f32(v), q_pos0, masks, q_block=128, kv_block=kv_block, q_front=front)
+    assert np.abs(out - ref).max() < 2e-2
