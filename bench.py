@@ -608,6 +608,55 @@ def _hook(args, h, hk, dev, rank):
                        'value_definition': 'executed-tile FLOPs / prefill time (host metadata reads included)'}}
 
 
+def _decoder_kernels(args, h, hk, dev, rank):
+    """The config-5 harness kernels at one 8192-token chunk of the full decoder (1 GPU widths):
+    fused residual add + RMSNorm over [8192, 5120], RoPE + K/V cache write of qkv [8192, 80 x 128],
+    SwiGLU of gate_up [8192, 2 x 25600].  Inputs are larger than L2 except rope's table rows."""
+    import torch
+    from sm120_attn import ops
+    from sm120_attn.decoder import DecoderConfig, rope_table
+    cfg = DecoderConfig()
+    n, E, D, I = 8192, cfg.hidden, cfg.head_dim, cfg.inter
+    Hq, Hkv = cfg.heads, cfg.kv_heads
+    g = torch.Generator(device=dev)
+    g.manual_seed(rank)
+    bf = torch.bfloat16
+    hbuf = torch.randn(n, E, generator=g, device=dev).to(bf)
+    delta = torch.randn(n, E, generator=g, device=dev).to(bf)
+    w = torch.ones(E, dtype=bf, device=dev)
+    x = torch.empty(n, E, dtype=bf, device=dev)
+    qkv = torch.randn(n, (Hq + 2 * Hkv) * D, generator=g, device=dev).to(bf)
+    q = torch.empty(n, Hq, D, dtype=bf, device=dev)
+    kc = torch.empty(3 * n, Hkv, D, dtype=bf, device=dev)
+    vc = torch.empty_like(kc)
+    table = rope_table(3 * n, D, cfg.rope_theta, dev)
+    gu = torch.randn(n, 2 * I, generator=g, device=dev).to(bf)
+    act = torch.empty(n, I, dtype=bf, device=dev)
+    kernels = [
+        ('add_rmsnorm_kernel', lambda: ops.add_rmsnorm(hbuf, w, x, cfg.eps, delta=delta), 8 * n * E),
+        ('rope_qkv_kernel', lambda: ops.rope_qkv(qkv, Hq, Hkv, D, table, 2 * n, q, kc[2 * n:], vc[2 * n:]),
+         4 * n * (Hq + 2 * Hkv) * D),
+        ('silu_mul_kernel', lambda: ops.silu_mul(gu, act), 6 * n * I),
+    ]
+    per = {}
+    for name, fn, nbytes in kernels:
+        for _ in range(3):
+            fn()
+        per[name] = (_kernel_ms(fn, dev, reps=20), nbytes)
+    steps = max(1, args.steps)
+    ms = _timed(lambda: [fn() for _, fn, _ in kernels], steps, dev, int(os.environ.get('WORLD_SIZE', '1')))
+    total = sum(b for _, (_, b) in per.items())
+    top = max(per, key=lambda k: per[k][1])
+    return {'ms': ms, 'steps': steps, 'e2e_ms': None, 'work': total, 'unit': 'GB/s', 'scale': 1e9,
+            'kernel': top, 'kernel_ms': per[top][0], 'kernel_work': per[top][1], 'bound': 'hbm',
+            'h2d': 0, 'd2h': 0, 'launches': len(kernels), 'dtype': 'bf16 in/out, fp32 arithmetic',
+            'config': {'workload': f'config-5 harness kernels at one {n}-token chunk: add_rmsnorm [{n}, {E}], '
+                                   f'rope_qkv [{n}, {Hq}+2x{Hkv} heads x {D}], silu_mul [{n}, 2x{I}]',
+                       'per_kernel': {k: {'us': round(t * 1000, 1), 'MB': round(b / 1e6, 1),
+                                          'GB/s': round(b / (t * 1e-3) / 1e9, 1)} for k, (t, b) in per.items()},
+                       'value_definition': 'algorithmic bytes of the three kernels / their time'}}
+
+
 def run_ttft(args):
     """Config 5: prefill TTFT of the random-init 64-layer GQA decoder (hidden 5120, 64/8 heads, SwiGLU
     25600, vocab 151936) over 65536 / 131072 / 262144 random token ids in 8192-token chunks, sparse
@@ -724,7 +773,8 @@ def run_other(args):
     h = hk * (H_FULL // HK_FULL)
     clocks = Clocks(local)
     clocks.start()
-    res = {'dense': _dense, 'selection': _selection, 'chunked': _chunked, 'hook': _hook}[args.workload](
+    res = {'dense': _dense, 'selection': _selection, 'chunked': _chunked, 'hook': _hook,
+           'decoder_kernels': _decoder_kernels}[args.workload](
         args, h, hk, dev, rank)
     clk = clocks.stop()
     steps = res.get('steps', args.steps)
@@ -737,7 +787,8 @@ def run_other(args):
         'metric': METRIC, 'value': round(value, 2), 'unit': res['unit'], 'n_gpus': world, 'steps': steps,
         'warmup': args.warmup, 'ms_per_step': round(ms / steps, 4), 'higher_is_better': True,
         'scaling': args.scaling, 'vs_baseline': None,
-        'dtype': 'fp8-e4m3 (fp32 accumulate, bf16 in/out)' if res['unit'] == 'TFLOPS' else 'bf16 in, fp32 scores, int32 CSR',
+        'dtype': res.get('dtype') or ('fp8-e4m3 (fp32 accumulate, bf16 in/out)' if res['unit'] == 'TFLOPS'
+                                      else 'bf16 in, fp32 scores, int32 CSR'),
         'data': 'synthetic (seeded, BASELINE shapes and injection)', 'config': dict(res['config']),
     }
     line['config']['parallelism'] = f'kv-head shards x{world} ({args.scaling}), no collective on the data path'
@@ -846,7 +897,7 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--profile-range', action='store_true',
                     help='bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)')
-    ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked', 'hook', 'ttft'])
+    ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked', 'hook', 'ttft', 'decoder_kernels'])
     ap.add_argument('--comm-blocks', type=int, default=2,
                     help='ttft workload: row blocks whose all-reduces overlap the next block\'s GEMMs (1: none)')
     ap.add_argument('--contexts', default='65536,131072,262144',

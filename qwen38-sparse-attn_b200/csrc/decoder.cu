@@ -187,7 +187,7 @@ extern "C" int sa_add_rmsnorm_bf16(const void* delta, int64_t delta_row_stride, 
         return fail(SA_ERR_ALIGN, "sa_add_rmsnorm_bf16: tensors must be 16-byte aligned with row strides %% 8 == 0");
     if (rows == 0) return SA_OK;
     const int nv = (hidden / 8 + 127) / 128;
-    const dim3 grid(std::min(rows, 8 * num_sms()));
+    const dim3 grid(std::min(rows, 32 * num_sms()));             // up to 16 resident per SM, rows grid-strided
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     auto* d = static_cast<const uint16_t*>(delta);
     auto* hp = static_cast<uint16_t*>(h);
