@@ -445,6 +445,23 @@ def _scale_tensor(dev, sq, sk, sv):
 
 
 _KV8_CACHE: dict = {}
+# Device memory the FP8 KV cache may hold over all (layer, request) entries; the oldest entries are
+# dropped past it (a dropped request is rebuilt from its K/V pages on its next chunk).
+KV8_CACHE_MAX_BYTES = int(float(os.environ.get('SM120_SPARSE_FP8_KV_CACHE_GB', '16')) * (1 << 30))
+
+
+def _kv8_bytes(entry) -> int:
+    return entry['k8'].numel() + entry['v8'].numel()
+
+
+def _kv8_evict(keep_key):
+    """Drop the oldest entries (never keep_key) until the cache is within KV8_CACHE_MAX_BYTES."""
+    total = sum(_kv8_bytes(e) for e in _KV8_CACHE.values())
+    for key in list(_KV8_CACHE):
+        if total <= KV8_CACHE_MAX_BYTES:
+            break
+        if key != keep_key:
+            total -= _kv8_bytes(_KV8_CACHE.pop(key))
 
 
 def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
@@ -479,6 +496,7 @@ def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
             grown = torch.empty(cap, Hk, D, dtype=torch.uint8, device=dev)
             grown[:lo] = entry[name][:lo]
             entry[name] = grown
+    _kv8_evict(key)
     if kv_len > lo:
         if k.shape[0] < kv_len - k_row0 or v.shape[0] < kv_len - k_row0 or lo < k_row0:
             raise ValueError('_cached_kv8: k/v do not hold rows %d..%d' % (lo, kv_len))

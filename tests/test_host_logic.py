@@ -235,6 +235,24 @@ def test_fp8_warm_and_chunk_rows(ksp, monkeypatch):
         ksp._cached_kv8('W', 1, k[2992:], v[2992:], 3000, 3500, sc, k_row0=2992)
 
 
+def test_kv8_cache_byte_cap(ksp, monkeypatch):
+    """The FP8 KV cache drops its oldest entries past KV8_CACHE_MAX_BYTES (never the one in use); a
+    dropped request is rebuilt from its rows on its next chunk."""
+    from sm120_attn import ops
+    monkeypatch.setattr(ops, 'quantize', lambda x, scale, mode, out, transpose=False, rows_pad=0: out.zero_())
+    k = torch.zeros(9000, 2, 8, dtype=torch.bfloat16)
+    sc = (0.1, 0.02, 0.03)
+    per_entry = 2 * 8192 * 2 * 8                                # k8 + v8 at the minimum capacity
+    monkeypatch.setattr(ksp, 'KV8_CACHE_MAX_BYTES', 2 * per_entry)
+    for layer in ('L0', 'L1', 'L2'):
+        ksp._cached_kv8(layer, 1, k, k, 0, 1000, sc)
+    assert list(k_[0] for k_ in ksp._KV8_CACHE) == ['L1', 'L2']  # the oldest went first
+    ksp._cached_kv8('L1', 1, k, k, 1000, 9000, sc)              # grows past the cap: others dropped
+    assert list(k_[0] for k_ in ksp._KV8_CACHE) == ['L1']
+    assert ksp._KV8_CACHE[('L1', 1)]['rows'] == 9000
+    ksp._KV8_CACHE.clear()
+
+
 def test_block_masks_rejects_unpadded_input(ksp):
     sp = ksp.SparsePrefill(8, 2, 128, 'cpu')
     ksp.BLOCK = 64
