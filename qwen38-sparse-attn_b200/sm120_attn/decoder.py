@@ -142,7 +142,10 @@ class TPDecoder:
         self.v_cache = [torch.empty(max_tokens, self.hk, D, dtype=torch.bfloat16, device=dev) for _ in self.layers]
         self.sp = ksp.SparsePrefill(self.hq, self.hk, D, dev, tau=tau, min_kv=min_kv, min_q=0, kernel=kernel)
         if fp8_kv_cache:                       # this model's e4m3 K/V (every layer at max_tokens) must fit
-            need = cfg.layers * 2 * max_tokens * self.hk * D
+            rows = 8192
+            while rows < max_tokens:           # entries grow by doubling from 8192 rows
+                rows *= 2
+            need = cfg.layers * 2 * rows * self.hk * D
             ksp.KV8_CACHE_MAX_BYTES = max(ksp.KV8_CACHE_MAX_BYTES, need + (1 << 30))
         c, bf = chunk, torch.bfloat16
         self.buf = {'h': torch.empty(c, E, dtype=bf, device=dev), 'x': torch.empty(c, E, dtype=bf, device=dev),
