@@ -717,7 +717,9 @@ def run_ttft(args):
     hbm, bf16, how = peaks()
     gemm_flops = cfg.prefill_flops(headline)
     chunks = -(-headline // 8192)
-    launches = cfg.layers * (11 * chunks + 3) + 1
+    # per layer and chunk: add_rmsnorm + rope + 7 on the attention path, then add_rmsnorm + silu per
+    # communication block; 3 absmax per layer on the first chunk; the final add_rmsnorm
+    launches = cfg.layers * ((9 + 2 * model.comm_blocks) * chunks + 3) + 1
     line = {
         'metric': METRIC, 'value': round(ttft[headline] / 1000.0, 4), 'unit': 's', 'n_gpus': world, 'steps': steps,
         'warmup': args.warmup, 'ms_per_step': round(ttft[headline], 2), 'higher_is_better': False,
