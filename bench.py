@@ -4,7 +4,7 @@
 One step = one prefill chunk through the drop-in API `SparsePrefill.forward_sm120fp8` with the
 incremental block-mean cache (`_cached_block_means`): pool the chunk's keys into the cache
 (kernel a), pool + quantise the queries (kernel a), score and select blocks (kernel b, two
-launches), quantise K and V, block-sparse FP8 attention (kernel c).  Shape of BASELINE configs[1]: Q 8192 rows at offset 57344
+launches), quantise K and V, block-sparse FP8 attention (kernel c).  Shape of benchmark configuration 2: Q 8192 rows at offset 57344
 against 65536 keys, 64 query / 8 KV heads, head_dim 128, block 128, tau 0.95, seeded synthetic
 inputs with the benchmark's hot-block injection.  Inputs (q 134 MB, k/v 134 MB each) exceed the
 126 MB L2, so no flush is needed between steps.
@@ -661,7 +661,7 @@ def run_ttft(args):
     """Config 5: prefill TTFT of the random-init 64-layer GQA decoder (hidden 5120, 64/8 heads, SwiGLU
     25600, vocab 151936) over 65536 / 131072 / 262144 random token ids in 8192-token chunks, sparse
     FP8 attention at tau 0.95, tensor-parallel by KV head over the ranks (NCCL all-reduce after the
-    row-parallel projections).  value = TTFT of the 131072-token prompt."""
+    row-parallel projections).  value = TTFT of the 131072-token prompt (benchmark configuration 5)."""
     import torch
     import torch.distributed as dist
     import sm120_attn.sparse_prefill as ksp
@@ -791,7 +791,7 @@ def run_other(args):
         'scaling': args.scaling, 'vs_baseline': None,
         'dtype': res.get('dtype') or ('fp8-e4m3 (fp32 accumulate, bf16 in/out)' if res['unit'] == 'TFLOPS'
                                       else 'bf16 in, fp32 scores, int32 CSR'),
-        'data': 'synthetic (seeded, BASELINE shapes and injection)', 'config': dict(res['config']),
+        'data': 'synthetic (seeded, benchmark shapes and injection)', 'config': dict(res['config']),
     }
     line['config']['parallelism'] = f'kv-head shards x{world} ({args.scaling}), no collective on the data path'
     line['config']['l2'] = 'inputs larger than L2; no flush'

@@ -187,7 +187,7 @@ SA_API int sa_attn_fwd_bf16(const void* q, int64_t q_row_stride, int64_t q_head_
                      float softmax_scale, int32_t* status, void* stream);
 
 /*
- * Elementwise kernels of the end-to-end prefill harness (a random-init dense
+ * Elementwise kernels of the end-to-end prefill harness (benchmark configuration 5: a random-init dense
  * GQA decoder whose TTFT the reference measures through vLLM, scripts/bench_ttft.py:1-12).  The
  * reference has no entry points of its own here: these compute what vLLM 0.22's model layers do
  * (model_executor/layers/layernorm.py fused-add RMSNorm, rotary_embedding/base.py neox rotary

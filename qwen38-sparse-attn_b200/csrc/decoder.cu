@@ -1,4 +1,4 @@
-// Elementwise kernels of the end-to-end prefill harness (random-init dense GQA decoder, BASELINE
+// Elementwise kernels of the end-to-end prefill harness (random-init dense GQA decoder, benchmark
 // config 5): fused residual add + RMSNorm, rotary position embedding of q/k with the K/V cache write,
 // and the SwiGLU activation.  The reference measures TTFT through vLLM's model code (its fused
 // add RMSNorm, neox-style rotary embedding and SiluAndMul, vllm 0.22:

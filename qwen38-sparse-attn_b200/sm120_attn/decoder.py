@@ -1,4 +1,4 @@
-"""Tensor-parallel random-init GQA decoder prefill: the end-to-end TTFT harness of BASELINE config 5.
+"""Tensor-parallel random-init GQA decoder prefill: the end-to-end TTFT harness of benchmark configuration 5.
 
 The reference reports prefill TTFT of a served model whose attention goes through the sparse prefill
 hook (README.md:29-31, measured by scripts/bench_ttft.py: a streamed completion request, chunked

@@ -1,4 +1,4 @@
-"""End-to-end prefill harness on the GPU: its elementwise kernels against plain
+"""End-to-end prefill harness (benchmark configuration 5) on the GPU: its elementwise kernels against plain
 fp32 PyTorch, and a small decoder's prefill through the sparse attention path against an fp32
 reference forward of the same weights."""
 import math

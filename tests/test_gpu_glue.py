@@ -1,7 +1,7 @@
 """The drop-in `sm120_attn` API end to end on the GPU against the oracle.
 
 Covers the reference's glue tests (tests/test_sparse_prefill.py:28-48, :65-92;
-tests/test_sparse_prefill_fp8.py:13-31) and BASELINE config 1 (H 64, Hk 8, D 128, 1024 queries at
+tests/test_sparse_prefill_fp8.py:13-31) and benchmark configuration 1 (H 64, Hk 8, D 128, 1024 queries at
 7168 against 8192 keys, block 128, tau 0.95, both injection strengths).  Masks: exact up to the
 tau-boundary exemption.  Outputs: rel-L2 3e-2 (FP8) / max-abs 2e-2 (BF16) against the fp32
 reference computed on the same masks and the same (quantised) operands.
