@@ -73,3 +73,21 @@ def test_ops_refuse_cpu_tensors():
     x = torch.zeros(4, 2, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match='CUDA'):
         ops.absmax(x, per_head=True)
+
+
+def test_plain_c_caller(tmp_path):
+    """The header is valid C99 and the library links and answers from a C program (no Python, no GPU)."""
+    import shutil
+    import subprocess
+    from sm120_attn import _native as N
+    gcc = shutil.which('gcc')
+    if gcc is None:
+        pytest.skip('gcc not available')
+    lib = Path(N.LIB_PATH)
+    exe = tmp_path / 'c_caller'
+    cmd = [gcc, '-std=c99', '-Wall', '-Wextra', '-Werror', '-I', str(ROOT / 'include'), str(ROOT / 'tests' / 'c_caller.c'),
+           '-o', str(exe), '-L', str(lib.parent), '-l:' + lib.name, '-Wl,-rpath,' + str(lib.parent)]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert '0 failures' in r.stdout
