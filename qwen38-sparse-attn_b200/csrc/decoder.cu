@@ -153,18 +153,6 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const uint16_t* __restric
     }
 }
 
-int num_sms() {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 148;
-    }
-    return sms;
-}
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 int grid_for(int64_t work, int threads) {
     const int64_t want = (work + threads - 1) / threads;

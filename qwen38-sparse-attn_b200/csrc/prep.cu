@@ -213,18 +213,6 @@ __global__ void absmax_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64
     if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned int*>(out + (per_head ? h : 0)), m);
 }
 
-int num_sms() {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 148;
-    }
-    return sms;
-}
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
 }  // namespace sa

@@ -25,6 +25,8 @@ namespace sa {
 void set_error(const char* fmt, ...);
 int fail(int code, const char* fmt, ...);
 int check_launch(const char* what);
+int num_sms();                          // SM count of the current device (cached after the first call)
+bool aligned16(const void* p);
 
 // ------------------------------------------------------------------------------------------
 // Small device utilities
