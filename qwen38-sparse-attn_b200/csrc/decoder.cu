@@ -153,7 +153,6 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const uint16_t* __restric
     }
 }
 
-
 int grid_for(int64_t work, int threads) {
     const int64_t want = (work + threads - 1) / threads;
     return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 16ll * num_sms())));

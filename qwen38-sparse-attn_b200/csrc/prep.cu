@@ -213,7 +213,6 @@ __global__ void absmax_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64
     if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<unsigned int*>(out + (per_head ? h : 0)), m);
 }
 
-
 }  // namespace
 }  // namespace sa
 
