@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(SC_THREADS, 2) score_kernel(
 // ------------------------------------------------------------------------------------------------
 constexpr int SEL_WARPS = 8;
 constexpr int SEL_THREADS = SEL_WARPS * 32;
-constexpr int SEL_MAX_NPL = 64;                                   // register rows up to 2048 blocks
+constexpr int SEL_MAX_NPL = 64;   // rows up to 2048 blocks in registers (one warp up to 1024, a warp pair above)
 
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -451,6 +451,178 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel_long(const SelArgs 
     if (a.counts && lane == 0) a.counts[unit] = total;
 }
 
+// Rows of 1025..2048 blocks: two warps per output unit, each holding half of every row in
+// registers (half s, lane l: blocks 1024 s + l + 32 c, c < 32).  Their partial sums, maxima and
+// counts are combined through double-buffered shared-memory slots with one 64-thread named barrier
+// per exchange, so both warps take the same decisions.  (One warp per 2048-block row needs 255
+// registers, one CTA per SM, and code too large for the instruction cache.)
+constexpr int SPLIT_NPL = 32;
+constexpr int SPLIT_BLOCKS = 32 * SPLIT_NPL;                      // blocks per half
+
+struct PairX {
+    double* slot;                                                  // [2 buffers][2 halves]
+    int bar;                                                       // named barrier id of the pair
+    int half;
+    int k;                                                         // exchange count
+    // v: this warp's value (the same in every lane); returns both halves combined by op
+    __device__ __forceinline__ double both(double v, bool take_max) {
+        double* sl = slot + (k & 1) * 2;
+        if ((threadIdx.x & 31) == 0) sl[half] = v;
+        asm volatile("bar.sync %0, 64;" :: "r"(bar) : "memory");
+        const double r = take_max ? fmax(sl[0], sl[1]) : sl[0] + sl[1];
+        ++k;
+        return r;
+    }
+    __device__ __forceinline__ double sum(double v) { return both(v, false); }
+    __device__ __forceinline__ float maxf(float v) { return static_cast<float>(both(static_cast<double>(v), true)); }
+};
+
+__device__ uint32_t select_row_split(const float* __restrict__ L, int nbc, float tau_f, int lane, PairX& x) {
+    constexpr int NPL = SPLIT_NPL;
+    const int base = x.half * SPLIT_BLOCKS;
+    float p[NPL];
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const int j = base + lane + 32 * c;
+        p[c] = j < nbc ? __ldg(L + j) : -INFINITY;
+    }
+    float mx = p[0];
+#pragma unroll
+    for (int c = 1; c < NPL; ++c) mx = fmaxf(mx, p[c]);
+    mx = x.maxf(warp_max_f(mx));
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        p[c] = (base + lane + 32 * c < nbc) ? expf(p[c] - mx) : 0.f;
+        s += p[c];
+    }
+    s = static_cast<float>(x.sum(static_cast<double>(warp_sum_f(s))));
+    double t0 = 0.0, t1 = 0.0;
+    float pmax = 0.f;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const bool valid = base + lane + 32 * c < nbc;
+        p[c] = valid ? __fdiv_rn(p[c], s) : -1.f;                 // -1: not a block of this row
+        const double d = valid ? static_cast<double>(p[c]) : 0.0;
+        if (c & 1) t1 += d; else t0 += d;
+        pmax = fmaxf(pmax, p[c]);
+    }
+    const double tot = x.sum(warp_sum_d(t0 + t1));
+    uint32_t keep = 0;
+    if (!(static_cast<float>(tot) >= tau_f)) {                   // tau never reached: every causal block
+#pragma unroll
+        for (int c = 0; c < NPL; ++c)
+            if (base + lane + 32 * c < nbc) keep |= 1u << c;
+        return keep;
+    }
+    auto pred64 = [&](uint32_t bits) -> bool {
+        const float v = __uint_as_float(bits);
+        double m0 = 0.0, m1 = 0.0, m2 = 0.0, m3 = 0.0;
+#pragma unroll
+        for (int c = 0; c < NPL; ++c) {
+            const double d = (p[c] >= v) ? static_cast<double>(p[c]) : 0.0;
+            if ((c & 3) == 0) m0 += d;
+            else if ((c & 3) == 1) m1 += d;
+            else if ((c & 3) == 2) m2 += d;
+            else m3 += d;
+        }
+        return static_cast<float>(x.sum(warp_sum_d((m0 + m1) + (m2 + m3)))) >= tau_f;
+    };
+    const uint32_t top = __float_as_uint(x.maxf(warp_max_f(pmax))) + 1u;
+    // fp32 search, float64 check of its boundary, float64 search again where they disagree (as in
+    // select_row_regs)
+    uint32_t lo = 0u, hi = top;
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + ((hi - lo) >> 1);
+        const float v = __uint_as_float(mid);
+        float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll
+        for (int c = 0; c < NPL; ++c) {
+            const float d = (p[c] >= v) ? p[c] : 0.f;
+            if ((c & 3) == 0) m0 += d;
+            else if ((c & 3) == 1) m1 += d;
+            else if ((c & 3) == 2) m2 += d;
+            else m3 += d;
+        }
+        if (static_cast<float>(x.sum(static_cast<double>(warp_sum_f((m0 + m1) + (m2 + m3))))) >= tau_f) lo = mid;
+        else hi = mid;
+    }
+    const bool lo_ok = pred64(lo);
+    const bool hi_ok = hi == top ? false : pred64(hi);
+    if (!(lo_ok && !hi_ok)) {
+        lo = 0u;
+        hi = top;
+        while (hi - lo > 1u) {
+            const uint32_t mid = lo + ((hi - lo) >> 1);
+            if (pred64(mid)) lo = mid; else hi = mid;
+        }
+    }
+    const float vstar = __uint_as_float(lo);
+    double above = 0.0;
+    int ties = 0;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        above += p[c] > vstar ? static_cast<double>(p[c]) : 0.0;
+        ties += (p[c] == vstar);
+    }
+    above = x.sum(warp_sum_d(above));
+    ties = warp_sum_i(ties);
+    const int ties_low = static_cast<int>(x.sum(x.half == 0 ? static_cast<double>(ties) : 0.0));
+    const int ties_all = static_cast<int>(x.sum(static_cast<double>(ties)));
+    const int kt = ties_needed(above, vstar, ties_all, tau_f);
+    int seen = x.half ? ties_low : 0;                              // ties are kept in ascending block order
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const bool tie = p[c] == vstar;
+        const uint32_t tb = __ballot_sync(0xffffffffu, tie);
+        const int rank = seen + __popc(tb & ((1u << lane) - 1u));
+        if (p[c] > vstar || (tie && rank < kt)) keep |= 1u << c;
+        seen += __popc(tb);
+    }
+    return keep;
+}
+
+__global__ void __launch_bounds__(SEL_THREADS) select_kernel_split(const SelArgs a, int units) {
+    __shared__ double xslot[SEL_WARPS / 2][4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pair = warp >> 1, half = warp & 1;
+    const int unit = blockIdx.x * (SEL_WARPS / 2) + pair;
+    if (unit >= units) return;                                     // both warps of the pair leave
+    PairX x{xslot[pair], 1 + pair, half, 0};
+    int h0, m0, nrows;
+    unit_rows(a, unit, h0, m0, nrows);
+    uint32_t keep = 0;
+    const int base = half * SPLIT_BLOCKS;
+    for (int k = 0; k < nrows; ++k) {
+        const int h = a.mode == SA_SELECT_KV_UNION ? h0 + k : h0;
+        const int m = a.mode == SA_SELECT_PAIR_UNION ? m0 + k : m0;
+        const int gi = a.qblk0 + m;
+        const int nbc = min(gi + 1, a.nb_total);
+        uint32_t kr = select_row_split(a.logits + static_cast<int64_t>(h * a.MB + m) * a.lrs, nbc, a.tau_f, lane, x);
+        if (gi < a.nb_total && gi >= base && gi < base + SPLIT_BLOCKS && (gi & 31) == lane)
+            kr |= 1u << ((gi - base) >> 5);                                  // diagonal
+        if (half == 0 && lane == 0) kr |= 1u;                                // sink
+        keep |= kr;
+    }
+    int cnt = 0;
+#pragma unroll
+    for (int c = 0; c < SPLIT_NPL; ++c) cnt += __popc(__ballot_sync(0xffffffffu, (keep >> c) & 1u));
+    const int before = static_cast<int>(x.sum(half == 0 ? static_cast<double>(cnt) : 0.0));
+    int total = half ? before : 0;
+#pragma unroll
+    for (int c = 0; c < SPLIT_NPL; ++c) {
+        const int j = base + 32 * c + lane;
+        if (base + 32 * c >= a.nb_total) break;
+        const bool on = (keep >> c) & 1u;
+        const uint32_t word = __ballot_sync(0xffffffffu, on);
+        if (a.lists && on)
+            a.lists[static_cast<int64_t>(unit) * a.list_stride + total + __popc(word & ((1u << lane) - 1u))] = j;
+        if (a.masks && j < a.nb_total) a.masks[static_cast<int64_t>(unit) * a.nb_total + j] = on ? 1 : 0;
+        total += __popc(word);
+    }
+    if (a.counts && half == 1 && lane == 0) a.counts[unit] = total;
+}
+
 int64_t logits_row_stride(int nb_total) { return (static_cast<int64_t>(nb_total) + 31) / 32 * 32; }
 
 // Scratch of sa_select_static: one buffer per device, part of the module image, so that entry
@@ -521,7 +693,7 @@ extern "C" int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_he
     else if (npl <= 8) select_kernel<8><<<blocks, SEL_THREADS, 0, s>>>(a, units);
     else if (npl <= 16) select_kernel<16><<<blocks, SEL_THREADS, 0, s>>>(a, units);
     else if (npl <= 32) select_kernel<32><<<blocks, SEL_THREADS, 0, s>>>(a, units);
-    else if (npl <= SEL_MAX_NPL) select_kernel<SEL_MAX_NPL><<<blocks, SEL_THREADS, 0, s>>>(a, units);
+    else if (npl <= 2 * SPLIT_NPL) select_kernel_split<<<(units + SEL_WARPS / 2 - 1) / (SEL_WARPS / 2), SEL_THREADS, 0, s>>>(a, units);
     else {
         const size_t smem = static_cast<size_t>(SEL_WARPS) * npl * sizeof(uint32_t);
         if (smem > 227 * 1024) return fail(SA_ERR_UNSUPPORTED, "sa_select: %d key blocks", nb_total);

@@ -100,6 +100,9 @@ SEL = [  # (block, kv, q_start, n, strength, H, Hk)
     (64, 4096, 3072, 1024, 'strong', 8, 2),
     (64, 4000, 3000, 1000, 'strong', 16, 2),
     (128, 20000, 12000, 8000, 'strong', 8, 1),
+    (64, 100032, 98016, 2016, 'strong', 8, 2),          # 1563 key blocks: rows split over a warp pair
+    (128, 250000, 245000, 5000, 'strong', 8, 1),        # 1954 key blocks
+    (64, 140032, 139008, 1024, 'unit', 4, 1),           # 2188 key blocks: the shared-memory row path
 ]
 
 
