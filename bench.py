@@ -870,14 +870,16 @@ def run_reference(args):
         return
     vals = []
     desc, threads = '', 0
+    for _ in range(max(0, args.warmup)):                       # short untimed samples (BLAS threads, caches)
+        cpu_sample(args.strength, seconds_budget=2.0)
     for _ in range(max(1, min(args.steps, 2))):
         v, desc, threads = cpu_sample(args.strength, seconds_budget=10.0)
         vals.append(v)
     value = sum(vals) / len(vals)
     line = {
         'metric': METRIC, 'value': round(value, 6), 'unit': 'TFLOPS', 'impl': 'reference', 'n_gpus': world,
-        'steps': len(vals), 'warmup': 0, 'higher_is_better': True, 'scaling': args.scaling, 'vs_baseline': None,
-        'dtype': 'fp32', 'data': 'synthetic (seeded, same workload as the b200 arm)',
+        'steps': len(vals), 'warmup': max(0, args.warmup), 'higher_is_better': True, 'scaling': args.scaling,
+        'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic (seeded, same workload as the b200 arm)',
         'config': {'workload': f'sparse prefill chunk (configs[1] shape): q {N_Q} @ {Q_START} vs {KV} keys, '
                                f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection',
                    'global_batch': 1, 'seq_len': KV, 'parallelism': 'host cores of rank 0'},
