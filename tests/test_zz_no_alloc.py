@@ -27,7 +27,7 @@ def _static(qm, km, H, Hk, nb_total, qblk0, scale, tau, mode, counts, lists, mas
 
 @pytest.mark.gpu
 @pytest.mark.parametrize('mode_name,MB,nb_total,qblk0', [('PER_HEAD', 64, 512, 448), ('PAIR_UNION', 32, 300, 270),
-                                                         ('KV_UNION', 16, 96, 80)])
+                                                         ('KV_UNION', 16, 96, 80), ('PER_HEAD', 64, 1500, 1440)])
 def test_static_scratch_select_matches_workspace_select(mode_name, MB, nb_total, qblk0):
     from sm120_attn import _native as N, ops
     mode = getattr(N, 'SA_SELECT_' + mode_name)
