@@ -253,6 +253,35 @@ def test_kv8_cache_byte_cap(ksp, monkeypatch):
     ksp._KV8_CACHE.clear()
 
 
+def test_cached_block_means_random_sequences(ksp):
+    """Property test: any sequence of chunks of one (layer, request) - contiguous appends, restarts at
+    0 and gaps that force a rebuild from the history, at block 64 and 128, chunk boundaries anywhere -
+    gives the same block-mean cache as the oracle's restatement of the reference."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=40, deadline=None, derandomize=True)
+    @given(block=st.sampled_from([64, 128]),
+           steps=st.lists(st.tuples(st.integers(1, 700), st.sampled_from(['next', 'restart', 'gap']),
+                                    st.integers(1, 300)), min_size=1, max_size=6),
+           seed=st.integers(0, 2 ** 16))
+    def check(block, steps, seed):
+        ksp.BLOCK = block
+        ksp._KMEAN_CACHE.clear()
+        oracle = O.KMeanCacheOracle(block)
+        keys = torch.randn(6 * 1000 + 8, 2, 8, generator=torch.Generator().manual_seed(seed)).to(torch.bfloat16)
+        kf = keys.float().numpy()
+        end = 0
+        for n, kind, gap in steps:
+            q_start = 0 if kind == 'restart' or end == 0 else end + (gap if kind == 'gap' else 0)
+            kv_len = q_start + n
+            got = ksp._cached_block_means('fuzz', 7, keys[q_start:kv_len], q_start, kv_len, key_all=keys)
+            ref = oracle.update('fuzz', 7, kf[q_start:kv_len], q_start, kv_len, key_all=kf)
+            np.testing.assert_array_equal(got.numpy(), ref)
+            assert ksp._KMEAN_CACHE[('fuzz', 7)]['last_kv'] == kv_len
+            end = kv_len
+    check()
+
+
 def test_block_masks_rejects_unpadded_input(ksp):
     sp = ksp.SparsePrefill(8, 2, 128, 'cpu')
     ksp.BLOCK = 64
