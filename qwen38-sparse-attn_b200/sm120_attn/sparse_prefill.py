@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import json
 import os
+import weakref
 
 import torch
 
@@ -536,6 +537,31 @@ def _cached_scales(layer_key, first_page, q, k, v, q_start):
     return entry['scales']
 
 
+_META_HOST: dict = {'ref': None, 'vals': None}
+
+
+def _host_metadata(attn_metadata):
+    """(query_start_loc, seq_lens, first page of each request) as host lists.  vLLM hands every
+    attention layer of a step the same metadata object, so the device reads (each a stream sync)
+    happen once per step, not once per layer: the lists are kept for the object last seen, held by a
+    weak reference so a later object can never be mistaken for it.  Host copies the backend keeps
+    (`query_start_loc_cpu`, `seq_lens_cpu`) are used when present."""
+    ref = _META_HOST['ref']
+    if ref is not None and ref() is attn_metadata:
+        return _META_HOST['vals']
+    qsl = getattr(attn_metadata, 'query_start_loc_cpu', None)
+    qsl = (qsl if qsl is not None else attn_metadata.query_start_loc).tolist()
+    seq_lens = getattr(attn_metadata, 'seq_lens_cpu', None)
+    seq_lens = (seq_lens if seq_lens is not None else attn_metadata.seq_lens).tolist()
+    first_pages = attn_metadata.block_table[:len(seq_lens), 0].tolist()
+    vals = (qsl, seq_lens, first_pages)
+    try:
+        _META_HOST['ref'], _META_HOST['vals'] = weakref.ref(attn_metadata), vals
+    except TypeError:                                   # not weak-referenceable: no reuse
+        _META_HOST['ref'], _META_HOST['vals'] = None, None
+    return vals
+
+
 @torch.no_grad()
 def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_metadata) -> bool:
     """Block-sparse attention for the long prefill chunks of this batch; other requests in the
@@ -559,11 +585,7 @@ def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_me
         return False
     if torch.cuda.is_current_stream_capturing():
         return False
-    # host copies of the metadata when the backend keeps them (no device read), else the device tensors
-    qsl = getattr(attn_metadata, 'query_start_loc_cpu', None)
-    qsl = (qsl if qsl is not None else attn_metadata.query_start_loc).tolist()
-    seq_lens = getattr(attn_metadata, 'seq_lens_cpu', None)
-    seq_lens = (seq_lens if seq_lens is not None else attn_metadata.seq_lens).tolist()
+    qsl, seq_lens, first_pages = _host_metadata(attn_metadata)
     nreq = len(seq_lens)
     eligible = [r for r in range(nreq) if qsl[r + 1] - qsl[r] >= cfg['min_q'] and seq_lens[r] >= cfg['min_kv']]
     if not eligible:
@@ -575,7 +597,6 @@ def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_me
     sp = _state(H, Hk, D, query.device)
     page = key_cache.shape[1]
     bt = attn_metadata.block_table
-    first_pages = bt[:nreq, 0].tolist()
     for r in range(nreq):
         kv_len = seq_lens[r]
         n = qsl[r + 1] - qsl[r]

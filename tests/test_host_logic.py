@@ -282,6 +282,41 @@ def test_cached_block_means_random_sequences(ksp):
     check()
 
 
+def test_host_metadata_read_once_per_step(ksp):
+    """The hook reads query_start_loc / seq_lens / first pages from the device once per metadata object
+    (vLLM passes one object to every layer of a step), never reuses them for another object, and does
+    not cache objects that cannot be weakly referenced."""
+    import gc
+
+    class Counted:
+        def __init__(self, values):
+            self.values, self.reads = values, 0
+
+        def tolist(self):
+            self.reads += 1
+            return list(self.values)
+
+        def __getitem__(self, idx):                      # block_table[:n, 0]
+            return self
+
+    class Meta:
+        def __init__(self, qsl, seq, pages):
+            self.query_start_loc, self.seq_lens, self.block_table = Counted(qsl), Counted(seq), Counted(pages)
+
+    m = Meta([0, 5], [9], [3])
+    for _ in range(4):                                   # four layers of one step
+        assert ksp._host_metadata(m) == ([0, 5], [9], [3])
+    assert (m.query_start_loc.reads, m.seq_lens.reads, m.block_table.reads) == (1, 1, 1)
+    del m
+    gc.collect()
+    m2 = Meta([0, 7], [11], [4])                          # next step (possibly at the same address)
+    assert ksp._host_metadata(m2) == ([0, 7], [11], [4])
+    ns = types.SimpleNamespace(query_start_loc=Counted([0, 1]), seq_lens=Counted([2]), block_table=Counted([5]))
+    ksp._host_metadata(ns)
+    ksp._host_metadata(ns)
+    assert ns.seq_lens.reads == 2                        # no weak reference: read every time
+
+
 def test_block_masks_rejects_unpadded_input(ksp):
     sp = ksp.SparsePrefill(8, 2, 128, 'cpu')
     ksp.BLOCK = 64
