@@ -317,6 +317,53 @@ def test_host_metadata_read_once_per_step(ksp):
     assert ns.seq_lens.reads == 2                        # no weak reference: read every time
 
 
+def test_cached_kv8_random_sequences(ksp, monkeypatch):
+    """Property test: over any sequence of calls - contiguous chunks (with the full history or only
+    the chunk's rows), restarts, gaps, scale changes, growth past the capacity - the e4m3 K/V the
+    cache returns equal a fresh quantisation of rows [0, kv_len) with the current scales."""
+    from hypothesis import given, settings, strategies as st
+    from sm120_attn import ops
+
+    def fake_quantize(x, scale, mode, out, transpose=False, rows_pad=0):
+        out.copy_((x.float() * scale.reshape(1, 1, 1)).round().clamp(-100, 100).to(torch.int8).view(torch.uint8))
+
+    monkeypatch.setattr(ops, 'quantize', fake_quantize)
+    g = torch.Generator().manual_seed(5)
+    k = torch.randn(40000, 2, 8, generator=g).to(torch.bfloat16)
+    v = torch.randn(40000, 2, 8, generator=g).to(torch.bfloat16)
+
+    def fresh(x, kv_len, s):
+        out = torch.empty(kv_len, 2, 8, dtype=torch.uint8)
+        fake_quantize(x[:kv_len], torch.tensor([1.0 / s]), 0, out)
+        return out
+
+    @settings(max_examples=40, deadline=None, derandomize=True)
+    @given(steps=st.lists(st.tuples(st.integers(1, 5000), st.sampled_from(['next', 'next_rows', 'restart', 'gap', 'rescale'])),
+                          min_size=1, max_size=7))
+    def check(steps):
+        ksp._KV8_CACHE.clear()
+        end, sc = 0, (0.1, 0.02, 0.03)
+        for n, kind in steps:
+            if kind == 'rescale':
+                sc = (0.1, sc[1] * 1.5, sc[2])
+            q_start = 0 if kind == 'restart' or end == 0 else end + (777 if kind == 'gap' else 0)
+            kv_len = q_start + n
+            if kv_len > k.shape[0]:
+                return
+            if kind == 'next_rows' and q_start > 0:
+                entry = ksp._KV8_CACHE.get(('P', 0))
+                if entry is None or entry['rows'] != q_start or entry['scales'] != (sc[1], sc[2]):
+                    continue                                   # chunk-only rows need a warm entry
+                r0 = q_start - q_start % 16
+                k8, v8 = ksp._cached_kv8('P', 0, k[r0:kv_len], v[r0:kv_len], q_start, kv_len, sc, k_row0=r0)
+            else:
+                k8, v8 = ksp._cached_kv8('P', 0, k, v, q_start, kv_len, sc)
+            assert torch.equal(k8, fresh(k, kv_len, sc[1])) and torch.equal(v8, fresh(v, kv_len, sc[2]))
+            end = kv_len
+    check()
+    ksp._KV8_CACHE.clear()
+
+
 def test_block_masks_rejects_unpadded_input(ksp):
     sp = ksp.SparsePrefill(8, 2, 128, 'cpu')
     ksp.BLOCK = 64
