@@ -11,6 +11,7 @@ import argparse
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
@@ -46,10 +47,15 @@ def build(verbose: bool = False, force: bool = False) -> Path:
                     '-Xcompiler', '-fvisibility=hidden']
     if verbose:
         flags += ['-Xptxas', '-v']
-    for src in SOURCES:
+    def compile_one(src):
         obj = build_dir / (Path(src).stem + '.o')
         cmd = [nvcc()] + flags + ['-c', str(CSRC / src), '-o', str(obj)]
-        r = subprocess.run(cmd, capture_output=True, text=True)
+        return src, obj, subprocess.run(cmd, capture_output=True, text=True)
+
+    # the translation units are independent: compile them concurrently, report in source order
+    with ThreadPoolExecutor(max_workers=min(len(SOURCES), os.cpu_count() or 1)) as pool:
+        results = list(pool.map(compile_one, SOURCES))
+    for src, obj, r in results:
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)
             raise RuntimeError(f'nvcc failed on {src}')
