@@ -863,29 +863,63 @@ def cpu_baseline(strength):
             'sample': desc}
 
 
+def cpu_selection_sample(strength):
+    """The selection path of the `selection` workload on the host cores with the oracle (numpy): K-chunk
+    block means appended to a cache holding the history, Q pooling, per-head tau selection, at the full
+    shape; returns (GB/s of the same algorithmic bytes as the GPU arm, description, threads)."""
+    import numpy as np
+    import torch
+    import oracle as O
+    import synth
+    q, k, _, _ = synth.make_qkv(N_Q, KV, H_FULL, HK_FULL, D, block=BLOCK, q_start=Q_START, seed=3000,
+                                strength=strength, hot=6, with_v=False)
+    qf, kf = q.float().numpy(), k.float().numpy()
+    kc = O.KMeanCacheOracle(BLOCK)
+    kc.update('cpu-sel', 0, kf[:Q_START], 0, Q_START)
+    t0 = time.perf_counter()
+    km = kc.update('cpu-sel', 0, kf[Q_START:], Q_START, KV)
+    qm = O.q_block_means(qf, Q_START, BLOCK)
+    masks = O.select_masks(qm, km, Q_START, BLOCK, H_FULL, HK_FULL, TAU)
+    sec = time.perf_counter() - t0
+    MB, NB = N_Q // BLOCK, KV // BLOCK
+    nnz = int(masks.sum())
+    nbytes = 2 * N_Q * H_FULL * D + 2 * N_Q * HK_FULL * D + 4 * HK_FULL * NB * D + 4 * HK_FULL * MB * D + \
+        4 * (H_FULL * MB + 1) + 4 * nnz
+    desc = (f'oracle (numpy) selection path of the whole chunk: K-chunk means, Q pooling, tau selection of '
+            f'{H_FULL * MB} rows over {NB} blocks ({sec:.2f} s)')
+    return nbytes / sec / 1e9, desc, torch.get_num_threads()
+
+
 def run_reference(args):
     rank = int(os.environ.get('RANK', '0'))
     world = int(os.environ.get('WORLD_SIZE', '1'))
     if rank != 0:
         return
+    if args.workload not in ('chunk', 'selection'):
+        print(json.dumps({'impl': 'reference', 'unavailable': f'no CPU arm for the {args.workload} workload: the '
+                          'reference CPU path is timed for the default (chunk) and selection workloads'}), flush=True)
+        return
+    sample = cpu_sample if args.workload == 'chunk' else (lambda st, seconds_budget=0: cpu_selection_sample(st))
+    unit = 'TFLOPS' if args.workload == 'chunk' else 'GB/s'
     vals = []
     desc, threads = '', 0
     for _ in range(max(0, args.warmup)):                       # short untimed samples (BLAS threads, caches)
-        cpu_sample(args.strength, seconds_budget=2.0)
+        sample(args.strength, seconds_budget=2.0)
     for _ in range(max(1, min(args.steps, 2))):
-        v, desc, threads = cpu_sample(args.strength, seconds_budget=10.0)
+        v, desc, threads = sample(args.strength, seconds_budget=10.0)
         vals.append(v)
     value = sum(vals) / len(vals)
     line = {
-        'metric': METRIC, 'value': round(value, 6), 'unit': 'TFLOPS', 'impl': 'reference', 'n_gpus': world,
+        'metric': METRIC, 'value': round(value, 6), 'unit': unit, 'impl': 'reference', 'n_gpus': world,
         'steps': len(vals), 'warmup': max(0, args.warmup), 'higher_is_better': True, 'scaling': args.scaling,
         'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic (seeded, same workload as the b200 arm)',
-        'config': {'workload': f'sparse prefill chunk (configs[1] shape): q {N_Q} @ {Q_START} vs {KV} keys, '
+        'config': {'workload': f'{"sparse prefill chunk" if args.workload == "chunk" else "selection path"} '
+                               f'(configs[1] shape): q {N_Q} @ {Q_START} vs {KV} keys, '
                                f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection',
                    'global_batch': 1, 'seq_len': KV, 'parallelism': 'host cores of rank 0'},
-        'cpu_baseline': {'value': round(value, 6), 'unit': 'TFLOPS', 'cores': os.cpu_count(), 'threads': threads,
+        'cpu_baseline': {'value': round(value, 6), 'unit': unit, 'cores': os.cpu_count(), 'threads': threads,
                          'kind': 'port', 'sample': desc},
-        'e2e': {'value': round(value, 6), 'unit': 'TFLOPS', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+        'e2e': {'value': round(value, 6), 'unit': unit, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
 
