@@ -34,3 +34,21 @@ def test_reference_arm_selection_and_unavailable():
     for workload in ('dense', 'chunked', 'hook', 'ttft', 'decoder_kernels'):
         u = _run('--impl', 'reference', '--workload', workload)
         assert u['impl'] == 'reference' and u['unavailable'], workload
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """The driver launches the reference arm like the GPU arm for N > 1: rank 0 alone runs and prints one
+    line, the other ranks exit 0 without work."""
+    import socket
+    with socket.socket() as sk:
+        sk.bind(('127.0.0.1', 0))
+        port = sk.getsockname()[1]
+    r = subprocess.run([sys.executable, '-m', 'torch.distributed.run', '--nnodes=1', '--nproc-per-node', '2',
+                        '--master-addr', '127.0.0.1', '--master-port', str(port), str(ROOT / 'bench.py'),
+                        '--impl', 'reference', '--gpus', '2', '--steps', '1', '--warmup', '0', '--workload', 'selection'],
+                       capture_output=True, text=True, timeout=300, cwd=str(ROOT))
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith('{')]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d['impl'] == 'reference' and d['n_gpus'] == 2 and d['value'] > 0
