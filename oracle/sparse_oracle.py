@@ -38,7 +38,8 @@ F32 = np.float32
 # Number formats
 # ---------------------------------------------------------------------------------------------
 def bf16_bits(x) -> np.ndarray:
-    """float32 -> bf16 bit patterns (uint16), round to nearest even; NaN stays NaN."""
+    """float32 -> bf16 bit patterns (uint16), round to nearest even; NaN stays NaN (the bf16 arithmetic of
+    `q * (1.0 / sq)` before the e4m3 cast, sparse_prefill.py:230-233)."""
     b = np.ascontiguousarray(x, dtype=F32).view(np.uint32).astype(np.uint64)
     nan = np.isnan(np.asarray(x, dtype=F32))
     r = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
@@ -55,7 +56,8 @@ def bf16_round(x) -> np.ndarray:
 
 
 def e4m3_round(x) -> np.ndarray:
-    """Values of float8_e4m3fn(x) with torch's cast semantics (RNE, |x| > 464 -> NaN)."""
+    """Values of float8_e4m3fn(x) with torch's cast semantics (RNE, |x| > 464 -> NaN), the cast of
+    sparse_prefill.py:230-233 and kernels/kai_fa_fp8.py:327."""
     x = np.asarray(x, dtype=np.float64)
     a = np.abs(x)
     out = np.empty_like(a)
@@ -466,7 +468,8 @@ def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None,
 
 
 def causal_blocks(qs: int, MB: int, block: int) -> int:
-    """Number of causal (head-independent) blocks for MB query blocks starting at aligned qs."""
+    """Number of causal (head-independent) blocks for MB query blocks starting at aligned qs: the
+    per-head term of the `blocks_total` statistic (sparse_prefill.py:182, :242)."""
     return int((qs // block) * MB + MB * (MB + 1) // 2)
 
 
