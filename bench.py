@@ -15,9 +15,10 @@ the K timed steps) - the reference's "sparse TFLOPS" definition (tests/test_fa_b
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
 
-Multi-GPU: units are KV-head groups with no data-path collective.  Default `--scaling weak`: every
-rank owns 8 KV heads (64 query heads) of a problem with 8N KV heads, so per-GPU work is the 1-GPU
-workload at every N.  `--scaling strong` splits the 8 KV heads of one problem over the N GPUs.
+Multi-GPU: units are KV-head groups with no data-path collective.  Default `--scaling strong`: the
+8 KV heads of one problem are split over the N GPUs (8/N KV heads and their query heads per rank,
+the partition of a tensor-parallel deployment), value = the problem's FLOPs / the slowest rank's
+time.  `--scaling weak`: every rank owns 8 KV heads (64 query heads) of a problem with 8N KV heads.
 `--impl reference` times the reference algorithm's CPU restatement (oracle/, numpy) on the host
 cores on a bounded sample of the same workload (rank 0 only).
 
@@ -52,9 +53,15 @@ Q_START = KV - N_Q
 # Kernels of this package launched per step: K-chunk block means, Q block means + e4m3, scores,
 # selection, K e4m3, V e4m3, attention.
 LAUNCHES_PER_STEP = 7
-# DRAM bytes (read + write) of one attention launch of this workload, from the ncu capture summarised
-# in profiles/attn_fwd_fp8_sparse_prefill.md (220.3 MB read + 108.4 MB written).
-ATTN_DRAM_BYTES = 328640000
+ATTN_KERNEL = 'attn_fwd_kernel<fp8>'
+# DRAM bytes (read + write) per attention launch measured by one ncu capture
+# (`dram__bytes_read.sum + dram__bytes_write.sum` of the attention kernel in
+# `bench.py --steps 2 --warmup 3 --no-cpu-baseline --profile-range`), keyed by what fixes them:
+# (kernel, injection strength, query heads per GPU).  A line whose configuration has no capture
+# reports traffic null rather than another configuration's figure.
+ATTN_DRAM_CAPTURES = {
+    ('attn_fwd_kernel<fp8>', 'unit', 64): 328640000,       # 220.3 MB read + 108.4 MB written
+}
 
 
 def peaks():
@@ -121,6 +128,93 @@ def make_rank_inputs(hk, seed, strength, device):
     q, k, v, _ = synth.make_qkv(N_Q, KV, hk * (H_FULL // HK_FULL), hk, D, block=BLOCK, q_start=Q_START, seed=seed,
                                 strength=strength, hot=6, device=device)
     return q.contiguous(), k.contiguous(), v.contiguous()
+
+
+def check_chunk_slice(q, k, v, out, counts, lists, scales, h, hk, tiles=2):
+    """Correctness check of one benchmarked chunk, run once outside the timed region: the last `tiles`
+    128-row query tiles of the query heads of KV head 0, against a torch fp32 reference on the GPU.
+
+    * selection: pooled fp32 scores, softmax, descending sort and float64 cumulative mass (the tau rule
+      of sparse_prefill.py:64-84) must give the kernel's block lists, except blocks whose cumulative
+      mass lies within 1e-4 of tau or that tie the boundary probability;
+    * attention: fp32 softmax attention on the same e4m3 operands (the glue's quantisation) and the
+      kernel's lists must be within rel-L2 3e-2 of the kernel's bf16 output.
+    Returns a dict of the figures; 'ok' is False when either check fails.
+    """
+    import torch
+    from sm120_attn import ops
+    from sm120_attn._native import SA_QUANT_MUL_BF16
+    g = h // hk
+    MB, NB = N_Q // BLOCK, KV // BLOCK
+    dev = q.device
+    scale = D ** -0.5
+    tile_ids = list(range(MB - tiles, MB))
+    rows = torch.arange((MB - tiles) * BLOCK, N_Q, device=dev)
+    kf = k[:, 0].float()                                                    # [KV, D] of KV head 0
+    km = kf.view(NB, BLOCK, D).mean(1)
+    cnt, lst = counts.view(h, MB), lists.view(h, MB, -1)
+    sel_bad, mism = 0, 0
+    for hh in range(g):
+        for m in tile_ids:
+            qm = q[m * BLOCK:(m + 1) * BLOCK, hh].float().mean(0)
+            gi = Q_START // BLOCK + m
+            logit = (km[:gi + 1] @ qm) * scale
+            p = torch.softmax(logit, 0)
+            ps, order = torch.sort(p, descending=True)
+            csum = torch.cumsum(ps.double(), 0)
+            keep = int((csum.float() < TAU).sum().item()) + 1
+            ref = torch.zeros(NB, dtype=torch.bool, device=dev)
+            ref[order[:keep]] = True
+            ref[gi] = True
+            ref[0] = True
+            got = torch.zeros(NB, dtype=torch.bool, device=dev)
+            c = int(cnt[hh, m].item())
+            got[lst[hh, m, :c].long()] = True
+            for j in torch.nonzero(got != ref).flatten().tolist():
+                mism += 1
+                pos = int((order == j).nonzero().item()) if j <= gi else -1
+                if pos < 0:
+                    sel_bad += 1
+                    continue
+                inc = float(csum[pos])
+                exc = inc - float(ps[pos])
+                edge = [float(ps[t]) for t in (keep - 1, keep) if 0 <= t <= gi]
+                if not (abs(inc - TAU) < 1e-4 or abs(exc - TAU) < 1e-4 or
+                        any(abs(float(ps[pos]) - e) <= 1e-5 * e for e in edge)):
+                    sel_bad += 1
+    # attention on the kernel's lists and the glue's e4m3 operands
+    sq, sk, sv = scales
+    inv = torch.tensor([1.0 / sq, 1.0 / sk, 1.0 / sv], dtype=torch.float32, device=dev)
+    q8 = torch.empty(len(rows), g, D, dtype=torch.uint8, device=dev)
+    ops.quantize(q[rows][:, :g].contiguous(), inv[0:1], SA_QUANT_MUL_BF16, q8)
+    k8 = torch.empty(KV, 1, D, dtype=torch.uint8, device=dev)
+    v8 = torch.empty(KV, 1, D, dtype=torch.uint8, device=dev)
+    ops.quantize(k[:, 0:1], inv[1:2], SA_QUANT_MUL_BF16, k8)
+    ops.quantize(v[:, 0:1], inv[2:3], SA_QUANT_MUL_BF16, v8)
+    f8 = torch.float8_e4m3fn
+    qd = q8.view(f8).float() * sq
+    kd = k8.view(f8).float()[:, 0] * sk
+    vd = v8.view(f8).float()[:, 0] * sv
+    pos_k = torch.arange(KV, device=dev)
+    num = den = 0.0
+    for hh in range(g):
+        s_ = (qd[:, hh] @ kd.T) * scale                                     # [rows, KV]
+        allowed = pos_k[None, :] <= (Q_START + rows)[:, None]
+        blk = torch.zeros(tiles, NB, dtype=torch.bool, device=dev)
+        for i, m in enumerate(tile_ids):
+            c = int(cnt[hh, m].item())
+            blk[i, lst[hh, m, :c].long()] = True
+        allowed &= blk.repeat_interleave(BLOCK, 0).repeat_interleave(BLOCK, 1)
+        s_ = s_.masked_fill(~allowed, float('-inf'))
+        ref = torch.softmax(s_, -1) @ vd
+        got = out[rows, hh].float()
+        num += float(((got - ref) ** 2).sum())
+        den += float((ref ** 2).sum())
+    rel = (num / max(den, 1e-30)) ** 0.5
+    return {'ok': sel_bad == 0 and rel < 3e-2, 'rows_checked': int(len(rows)) * g, 'heads': g,
+            'mask_mismatches': mism, 'mask_unexplained': sel_bad, 'attn_rel_l2': round(rel, 5),
+            'reference': 'torch fp32 on the GPU (selection tau rule; masked softmax attention on the same e4m3 '
+                         'operands)', 'tolerance': 'masks exact outside the 1e-4 tau band / ties; rel-L2 3e-2'}
 
 
 def run_b200(args):
@@ -199,6 +293,10 @@ def run_b200(args):
     kept = kept_blocks / causal_blocks
     flops = causal_flops(h, D, N_Q, KV) * kept
     tile_flops = kept_blocks * 4.0 * D * 128 * 128
+    # bytes the attention launch must move at least: q8 and the first KV rows of k8 / v8 read once,
+    # the block lists read, the bf16 output written
+    algo_bytes = N_Q * h * D + 2 * KV * hk * D + 2 * N_Q * h * D + 4 * h * (N_Q // BLOCK) + \
+        4 * kept_blocks
     # ---------------- end-to-end through the public API with pinned host buffers.  Every step copies
     # its chunk's q, k and v in from pinned host memory and its output back; two device buffer sets
     # and two copy streams let step i+1's upload and step i-1's download run under step i's compute
@@ -263,9 +361,14 @@ def run_b200(args):
     h2d = q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2
     d2h = o_h.numel() * 2
     ops.check_status(dev)
+    # ---------------- correctness of the benchmarked output (outside the timed regions): the last
+    # e2e step wrote bufs[(steps - 1) % 2] from the same inputs as every step
+    out_last = bufs[(args.steps - 1) % 2][3]
+    check = check_chunk_slice(q, k, v, out_last, sp.last_counts, sp.last_lists, scales, h, hk)
     # ---------------- reductions over ranks
-    (ms_total, e2e_ms, attn_avg), (flops_all, tile_all) = reduce_over_ranks(
-        [ms_total, e2e_ms, sum(attn_ms) / max(len(attn_ms), 1)], [flops, tile_flops], device=dev)
+    (ms_total, e2e_ms, attn_avg, neg_min), (flops_all, tile_all, n_failed) = reduce_over_ranks(
+        [ms_total, e2e_ms, sum(attn_ms) / max(len(attn_ms), 1), -ms_total],
+        [flops, tile_flops, 0.0 if check['ok'] else 1.0], device=dev)
     hbm, bf16, how = peaks()
     fp8_peak = 2.0 * bf16
     value = flops_all * args.steps / (ms_total * 1e-3) / 1e12
@@ -289,17 +392,20 @@ def run_b200(args):
                         f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection',
             'global_batch': 1, 'seq_len': KV, 'chunk': N_Q,
             'parallelism': f'kv-head shards x{world} ({args.scaling}), no collective on the data path',
+            'gpus_active': world, 'kv_heads_per_gpu': hk,
+            'ms_per_step_fastest_rank': round(-neg_min / args.steps, 4),
             'kept_fraction': round(kept, 4),
             'l2': 'inputs larger than L2 (q 134 MB, k 134 MB, v 134 MB per GPU); no flush',
         },
         'roofline': {
-            'bound': 'tensor', 'kernel': 'attn_fwd_kernel<fp8>',
+            'bound': 'tensor', 'kernel': ATTN_KERNEL,
             'achieved': round(achieved, 1), 'peak': round(fp8_peak, 1), 'unit': 'TFLOP/s',
             'frac': round(achieved / fp8_peak, 4),
             'peak_source': f'2 x {how} bf16 dense burst ({bf16} TF/s, MEASURED_PEAKS.json): B200 e4m3 dense rate is '
                            'twice bf16',
             'attn_ms_per_launch': round(attn_avg, 4),
-            'traffic': ATTN_DRAM_BYTES,
+            'traffic': ATTN_DRAM_CAPTURES.get((ATTN_KERNEL, args.strength, h)),
+            'algorithmic_bytes': algo_bytes,
         },
         'e2e': {'value': round(e2e_val, 2), 'unit': 'TFLOPS', 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
                 'ms_per_step': round(e2e_ms / args.steps, 4),
@@ -308,6 +414,15 @@ def run_b200(args):
         'gpu_launches': LAUNCHES_PER_STEP * args.steps,
         'clocks': clk,
     }
+    line['check'] = check
+    if n_failed:
+        if rank == 0:
+            print(f'bench: output check failed on {int(n_failed)} rank(s): {check}; no result line', file=sys.stderr,
+                  flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        raise SystemExit(3)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line['cpu_baseline'] = cpu_baseline(args.strength)
     if rank == 0:
@@ -930,7 +1045,9 @@ def main():
     ap.add_argument('--steps', type=int, default=20)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--scaling', default='weak', choices=['weak', 'strong'])
+    ap.add_argument('--scaling', default='strong', choices=['weak', 'strong'],
+                    help='strong (default): the 8 KV heads of one problem split over the GPUs; weak: every GPU '
+                         'runs a whole 8-KV-head problem')
     ap.add_argument('--strength', default='unit', choices=['unit', 'strong'])
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--profile-range', action='store_true',

@@ -118,7 +118,8 @@ SA_API size_t sa_select_workspace_bytes(int num_heads, int MB, int nb_total);
  *     q blocks fit up to 2560 key blocks.)
  *   - The first call made with a given device current looks up the buffer's address on that
  *     device; later calls on that device only reuse it.  Make that first call before capturing
- *     any stream.
+ *     any stream.  The address is tied to the device's CUDA context: after cudaDeviceReset (a
+ *     new primary context loads the library's module again) the next call looks it up anew.
  *   - Nothing in the buffer needs to start at zero: each call writes every entry it reads.
  *   - All calls on one device share the buffer: calls whose work overlaps on the GPU (different
  *     streams, or host threads without ordering) race.  Order them on one stream.

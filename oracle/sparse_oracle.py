@@ -297,14 +297,18 @@ def masks_to_lists(masks: np.ndarray):
 
 
 def compare_masks(test: np.ndarray, ref: np.ndarray, aux: dict, tau: float, num_kv_heads: int,
-                  pair: bool = False, tol: float = 1e-4, tie_rtol: float = 1e-5):
+                  pair: bool = False, tol: float = 1e-4, tie_rtol: float = 1e-5, report: dict | None = None):
     """Mask parity with the tau-boundary exemption.
 
     test/ref: per-query-head masks [H, MB', NB] (MB' = MB/2 when `pair`).  A mismatching block is
     exempt when, in the oracle's sorted order of a contributing (head, q-block) row, its cumulative
-    mass (inclusive or exclusive) lies within `tol` of tau, or its probability ties (relative
-    `tie_rtol`) the probability at the keep boundary - torch.sort is not stable, so the reference
-    does not define which of equal-probability blocks it keeps.  Returns (mismatches, unexplained).
+    mass (inclusive or exclusive) lies within `tol` of tau (the exemption the parity bar states), or
+    its probability ties (relative `tie_rtol`) the probability at the keep boundary - torch.sort is
+    not stable, so the reference does not define which of equal-probability blocks it keeps.
+    Returns (mismatches, unexplained).  When `report` is a dict it receives how many mismatches each
+    exemption absorbed: 'tau_band' (checked first) and 'tie' (only blocks outside the tau band), plus
+    'mismatches' and 'unexplained' counts, so that the second exemption cannot hide a real error
+    unnoticed.
     """
     probs, order, keep = aux['probs'], aux['order'], aux['keep']
     Hk, MB, g, NB = probs.shape
@@ -313,24 +317,29 @@ def compare_masks(test: np.ndarray, ref: np.ndarray, aux: dict, tau: float, num_
     np.put_along_axis(pos, order, np.arange(NB)[None, None, None, :].repeat(Hk, 0).repeat(MB, 1).repeat(g, 2), -1)
     bad = np.argwhere(test != ref)
     unexplained = []
+    n_band = n_tie = 0
     for h, mm, jj in bad:
         hk, i = divmod(int(h), g)
-        rows = (2 * mm, 2 * mm + 1) if pair else (mm,)
-        ok = False
+        rows = [m for m in ((2 * mm, 2 * mm + 1) if pair else (mm,)) if m < MB]
+        band = tie = False
         for m in rows:
-            if m >= MB:
-                continue
             p = pos[hk, m, i, jj]
             inc = csum64[hk, m, i, p]
             exc = inc - float(probs[hk, m, i, jj])
-            kb = int(keep[hk, m, i])
-            edge = [float(probs[hk, m, i, order[hk, m, i, t]]) for t in (kb - 1, kb) if 0 <= t < NB]
-            pj = float(probs[hk, m, i, jj])
-            if abs(inc - tau) < tol or abs(exc - tau) < tol or any(abs(pj - e) <= tie_rtol * max(e, 1e-30) for e in edge):
-                ok = True
-                break
-        if not ok:
+            band = band or abs(inc - tau) < tol or abs(exc - tau) < tol
+        if not band:
+            for m in rows:
+                kb = int(keep[hk, m, i])
+                edge = [float(probs[hk, m, i, order[hk, m, i, t]]) for t in (kb - 1, kb) if 0 <= t < NB]
+                pj = float(probs[hk, m, i, jj])
+                tie = tie or any(abs(pj - e) <= tie_rtol * max(e, 1e-30) for e in edge)
+        n_band += band
+        n_tie += tie
+        if not (band or tie):
             unexplained.append((int(h), int(mm), int(jj)))
+    if report is not None:
+        report.update({'mismatches': int(len(bad)), 'tau_band': int(n_band), 'tie': int(n_tie),
+                       'unexplained': len(unexplained)})
     return len(bad), unexplained
 
 

@@ -488,13 +488,18 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     p.vss = vss;
     p.softmax_scale = softmax_scale;
     p.status = status;
-    static bool attr_done[64] = {};
+    static PerContext attr;                                  // shared-memory opt-in, once per device context
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-        if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
-        if (dev >= 0 && dev < 64) attr_done[dev] = true;
+    void* ctx = nullptr;
+    if ((rc = current_device_context(name, &dev, &ctx))) return rc;
+    {
+        std::lock_guard<std::mutex> lock(attr.mu);
+        if (attr.ctx[dev] != ctx) {
+            cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 C::SMEM_BYTES);
+            if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+            attr.ctx[dev] = ctx;
+        }
     }
     dim3 grid(n_tiles, H);
     attn_fwd_kernel<FP8><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, p);

@@ -42,6 +42,30 @@ int num_sms() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+int current_device_context(const char* who, int* dev, void** ctx) {
+    typedef int (*CtxGetCurrent)(void**);
+    static CtxGetCurrent get_ctx = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_ctx = reinterpret_cast<CtxGetCurrent>(fn);
+    });
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: cudaGetDevice: %s", who, cudaGetErrorString(e));
+    if (*dev < 0 || *dev >= SA_MAX_DEVICES) return fail(SA_ERR_UNSUPPORTED, "%s: device %d", who, *dev);
+    *ctx = nullptr;
+    if (!get_ctx) return fail(SA_ERR_CUDA, "%s: cuCtxGetCurrent unavailable", who);
+    if (get_ctx(ctx) == 0 && *ctx) return SA_OK;
+    // no context bound to this thread yet: cudaSetDevice makes the device's primary context current
+    if ((e = cudaSetDevice(*dev)) != cudaSuccess)
+        return fail(SA_ERR_CUDA, "%s: cudaSetDevice: %s", who, cudaGetErrorString(e));
+    if (get_ctx(ctx) != 0 || !*ctx) return fail(SA_ERR_CUDA, "%s: no current CUDA context", who);
+    return SA_OK;
+}
+
 }  // namespace sa
 
 extern "C" int sa_version(void) { return 1; }

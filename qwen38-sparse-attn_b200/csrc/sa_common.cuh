@@ -11,6 +11,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/sparse_attn_b200.h"
 
 #ifndef SA_WAIT_TIMEOUT_NS
@@ -27,6 +29,20 @@ int fail(int code, const char* fmt, ...);
 int check_launch(const char* what);
 int num_sms();                          // SM count of the current device (cached after the first call)
 bool aligned16(const void* p);
+
+// One-time per-device set-up (a kernel attribute, a symbol's device address), recorded together with
+// the CUDA context it was made in.  After cudaDeviceReset (or any destruction of the primary
+// context) the device gets a new context in which the module is loaded afresh, so a record made in
+// another context is stale and the set-up is redone.  All members are guarded by `mu`.
+constexpr int SA_MAX_DEVICES = 64;
+struct PerContext {
+    std::mutex mu;
+    void* ctx[SA_MAX_DEVICES] = {};
+    void* value[SA_MAX_DEVICES] = {};
+};
+// The calling thread's current device and context (the context is created if the runtime has not
+// made it yet).  Returns SA_OK, or an SA_ERR_* code with the error text set.
+int current_device_context(const char* who, int* dev, void** ctx);
 
 // ------------------------------------------------------------------------------------------
 // Small device utilities

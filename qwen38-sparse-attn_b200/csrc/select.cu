@@ -667,13 +667,15 @@ extern "C" int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_he
 
     cudaError_t e = cudaSuccess;
     {
-        static bool smem_set[64] = {};                            // once per device (idempotent)
+        static PerContext attr;                                   // shared-memory opt-in, once per device context
         int dev = 0;
-        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return fail(SA_ERR_CUDA, "sa_select: %s", cudaGetErrorString(e));
-        if (dev >= 64 || !smem_set[dev]) {
+        void* ctx = nullptr;
+        if (int rc = current_device_context("sa_select", &dev, &ctx)) return rc;
+        std::lock_guard<std::mutex> lock(attr.mu);
+        if (attr.ctx[dev] != ctx) {
             e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM);
             if (e != cudaSuccess) return fail(SA_ERR_CUDA, "sa_select: %s", cudaGetErrorString(e));
-            if (dev < 64) smem_set[dev] = true;
+            attr.ctx[dev] = ctx;
         }
     }
     dim3 sgrid((nb_total + SC_COLS - 1) / SC_COLS, (MB * g + SC_ROWS - 1) / SC_ROWS, num_kv_heads);
@@ -715,24 +717,25 @@ extern "C" int sa_select_static(const float* qm, int64_t qm_block_stride, int64_
                                 int num_kv_heads, int head_dim, int MB, int nb_total, int qblk0, float scale, float tau,
                                 int mode, int32_t* counts, int32_t* lists, int64_t list_stride, uint8_t* masks,
                                 void* stream) {
-    static std::mutex mu;
-    static void* scratch[64] = {};
+    // device address of the scratch array, looked up once per device and context: a new context
+    // (after cudaDeviceReset) loads the module again, possibly at another address
+    static PerContext scratch;
     int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return fail(SA_ERR_CUDA, "sa_select_static: %s", cudaGetErrorString(e));
-    if (dev < 0 || dev >= 64) return fail(SA_ERR_UNSUPPORTED, "sa_select_static: device %d", dev);
+    void* ctx = nullptr;
+    if (int rc = current_device_context("sa_select_static", &dev, &ctx)) return rc;
     void* ws = nullptr;
     {
-        std::lock_guard<std::mutex> lock(mu);
-        if (!scratch[dev]) {
-            e = cudaGetSymbolAddress(&scratch[dev], g_select_scratch);
-            if (e != cudaSuccess) {
-                scratch[dev] = nullptr;
+        std::lock_guard<std::mutex> lock(scratch.mu);
+        if (scratch.ctx[dev] != ctx) {
+            void* addr = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&addr, g_select_scratch);
+            if (e != cudaSuccess)
                 return fail(SA_ERR_CUDA, "sa_select_static: scratch address on device %d: %s", dev,
                             cudaGetErrorString(e));
-            }
+            scratch.value[dev] = addr;
+            scratch.ctx[dev] = ctx;
         }
-        ws = scratch[dev];
+        ws = scratch.value[dev];
     }
     const size_t need = sa_select_workspace_bytes(num_heads, MB, nb_total);
     if (need > STATIC_SCRATCH_BYTES)

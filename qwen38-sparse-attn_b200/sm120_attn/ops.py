@@ -13,6 +13,10 @@ from . import _native as N
 
 _STATUS: dict = {}
 
+# Keys per online-softmax step of the FP8 attention kernel: P is rounded to e4m3 against the running
+# row maximum of each step, so numerical models of the kernel follow this granularity.
+FP8_KEYS_PER_TILE = 64
+
 
 def _p(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)

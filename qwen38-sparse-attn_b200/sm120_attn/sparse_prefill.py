@@ -171,6 +171,7 @@ class SparsePrefill:
         ops.attn_bf16(q, k[:kv_len], v[:kv_len], o, kv_len, front, qs, counts, lists, B, self.scale, q_block=B)
         if ev1 is not None:
             ev1.record()
+        self.last_counts, self.last_lists = counts, lists
         t2 = self._tick()
         if self.timing:
             self.stats['select_ms'] += t1 - t0
@@ -246,7 +247,7 @@ class SparsePrefill:
         ops.attn_fp8(q8, k8, v8, o, kv_len, front, qs, counts, lists, B, sc[0:1], sc[1:2], sc[2:3], self.scale)
         if ev1 is not None:
             ev1.record()
-        self.last_counts = counts
+        self.last_counts, self.last_lists = counts, lists
         t2 = self._tick()
         if self.timing:
             self.stats['select_ms'] += t1 - t0
