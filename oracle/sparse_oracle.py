@@ -406,7 +406,7 @@ def attention_ref(q, k, v, q_pos0: int, masks=None, q_block: int = 64, kv_block:
 
 def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None, lists=None,
                                q_block: int = 128, kv_block: int = 64, q_front: int = 0, tile: int = 128,
-                               key_tile: int = 64, group: int = 1):
+                               key_tile: int = 64, group: int = 1, partner_of=None):
     """Numerical model of the block-sparse FP8 forward (kai_fa_fp8.py:248-292, kai_fa_fp8_tma.py:256-272).
 
     Walks each (head, 128-row tile)'s block list from the last entry to the first in `key_tile`-key
@@ -416,7 +416,11 @@ def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None,
     the exp2 domain,
     P scaled by 448 and rounded to e4m3 before the PV product, the row sum over unrounded P, and
     `O * (sv / 448) / rowsum` (0 for an empty row).  The order and granularity of the walk set where
-    P is rounded, so they follow the CUDA kernel.  Inputs are e4m3 bit patterns q8 [n, H, D],
+    P is rounded, so they follow the CUDA kernel.  `partner_of(h, t)` -> (h2, t2) or None models a
+    kernel that walks two query tiles together: the steps are formed from the union of both tiles'
+    64-key blocks (descending, `group` per step), and each tile takes the keys of its own blocks in
+    every step that holds any (the partner's blocks are masked out for it).
+    Inputs are e4m3 bit patterns q8 [n, H, D],
     k8 [N, Hk, D], v8 [N, Hk, D]; per-head scale arrays or scalars.  Dense when counts is None.
     Returns fp32 [n, H, D].
     """
@@ -441,19 +445,29 @@ def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None,
             qpos = qpos0 + t * tile + np.arange(tile)
             qt = np.zeros((tile, D))
             qt[valid_rows] = qv[rows[valid_rows], h]
-            if counts is None:
-                nkeys = min(qpos0 + (t + 1) * tile, N)
-                starts = list(range(0, nkeys, key_tile))[::-1]
-            else:
-                r = h * (-(-(q_front + n) // q_block)) + (t * tile) // q_block
-                starts = []
+            def own_starts(hh, tt):
+                if counts is None:
+                    nkeys = min(qpos0 + (tt + 1) * tile, N)
+                    return list(range(0, nkeys, key_tile))[::-1]
+                r = hh * (-(-(q_front + n) // q_block)) + (tt * tile) // q_block
+                out_s = []
                 for b in [int(x) for x in lists[r, :counts[r]]][::-1]:
-                    starts += list(range(b * kv_block, (b + 1) * kv_block, key_tile))[::-1]
+                    out_s += list(range(b * kv_block, (b + 1) * kv_block, key_tile))[::-1]
+                return out_s
+            starts = own_starts(h, t)
+            mate = partner_of(h, t) if partner_of is not None else None
+            if mate is None:
+                steps = [starts[gi:gi + group] for gi in range(0, len(starts), group)]
+            else:
+                union = sorted(set(starts) | set(own_starts(*mate)), reverse=True)
+                mine = set(starts)
+                steps = [[k0 for k0 in union[gi:gi + group] if k0 in mine] for gi in range(0, len(union), group)]
+                steps = [st for st in steps if st]
             m = np.full(tile, -np.inf)
             l = np.zeros(tile)
             o = np.zeros((tile, D))
-            for gi in range(0, len(starts), group):
-                keys = np.concatenate([np.arange(k0, k0 + key_tile) for k0 in starts[gi:gi + group]])
+            for step in steps:
+                keys = np.concatenate([np.arange(k0, k0 + key_tile) for k0 in step])
                 kk = np.zeros((len(keys), D))
                 vk = np.zeros((len(keys), D))
                 inr = keys < N

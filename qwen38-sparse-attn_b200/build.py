@@ -19,7 +19,7 @@ CSRC = HERE / 'csrc'
 INCLUDE = HERE.parent / 'include'
 OUT_DIR = HERE / 'sm120_attn' / '_lib'
 LIB = OUT_DIR / 'libsa_b200.so'
-SOURCES = ['common.cu', 'prep.cu', 'select.cu', 'attn_fwd.cu', 'decoder.cu']
+SOURCES = ['common.cu', 'prep.cu', 'select.cu', 'attn_fwd.cu', 'attn_pair.cu', 'decoder.cu']
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 
 

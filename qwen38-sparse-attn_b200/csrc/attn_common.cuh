@@ -25,6 +25,12 @@ struct Params {
     int32_t* status;
 };
 
+// Paired-tile attention kernel (attn_pair.cu): two 128-row query tiles per CTA sharing each K/V
+// stage.  Takes the tensor maps launch_attn built (64-row K/V boxes) and validated parameters.
+template <bool FP8>
+int launch_attn_pair(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV, const Params& p,
+                     cudaStream_t stream, const char* name);
+
 namespace {
 
 constexpr int KEY_NONE = 1 << 30;   // key base of an absent tile: every key masked, TMA zero-fills

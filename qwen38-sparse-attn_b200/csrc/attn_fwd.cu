@@ -20,6 +20,8 @@
 
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "attn_common.cuh"
@@ -432,6 +434,19 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
 // ------------------------------------------------------------------------------------------------
 // Host side: tensor maps and launch
 // ------------------------------------------------------------------------------------------------
+// Which kernel serves a call: the paired-tile kernel (attn_pair.cu) for FP8, this file's one-tile
+// kernel for BF16.  SA_ATTN_KERNEL=tile or =pair forces one for both (read once per process).
+bool use_pair_kernel(bool fp8) {
+    static int forced = -1;                                  // -1 default, 0 tile, 1 pair
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char* e = std::getenv("SA_ATTN_KERNEL");
+        if (e && !std::strcmp(e, "tile")) forced = 0;
+        if (e && !std::strcmp(e, "pair")) forced = 1;
+    });
+    return forced < 0 ? fp8 : forced == 1;
+}
+
 template <bool FP8>
 int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t krs, int64_t khs, const void* v,
                 int64_t vrs, int64_t vhs, void* out, int64_t ors, int64_t ohs, int n_q, int H, int Hk, int D, int kv_len,
@@ -488,6 +503,7 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     p.vss = vss;
     p.softmax_scale = softmax_scale;
     p.status = status;
+    if (use_pair_kernel(FP8)) return launch_attn_pair<FP8>(tmQ, tmK, tmV, p, stream, name);
     static PerContext attr;                                  // shared-memory opt-in, once per device context
     int dev = 0;
     void* ctx = nullptr;

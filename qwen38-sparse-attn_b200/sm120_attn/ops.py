@@ -6,6 +6,7 @@ Every function here launches CUDA work from `_lib/libsa_b200.so` on
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -13,9 +14,19 @@ from . import _native as N
 
 _STATUS: dict = {}
 
-# Keys per online-softmax step of the FP8 attention kernel: P is rounded to e4m3 against the running
-# row maximum of each step, so numerical models of the kernel follow this granularity.
-FP8_KEYS_PER_TILE = 64
+
+
+def attn_schedule(fp8: bool = True):
+    """(keys per online-softmax step, paired tiles) of the attention kernel this process launches.
+
+    P is rounded (e4m3) against the running row maximum of each step, so numerical models of the
+    kernel follow this granularity.  The paired-tile kernel (the FP8 default) walks two query tiles
+    that share a KV head together: two query heads (h, h ^ 1) of one tile when the GQA group size is
+    even, else tiles (t, t ^ 1) of one head.  SA_ATTN_KERNEL=tile|pair overrides the choice (the
+    library reads the same variable once per process)."""
+    kind = os.environ.get('SA_ATTN_KERNEL', '')
+    paired = kind == 'pair' or (kind != 'tile' and fp8)
+    return (128 if paired else 64), paired
 
 
 def _p(t):

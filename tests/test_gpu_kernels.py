@@ -13,6 +13,7 @@ import torch
 
 import oracle as O
 import synth
+from kmodel import fp8_model_kwargs
 
 pytestmark = pytest.mark.gpu
 
@@ -218,7 +219,8 @@ def _deq(bits, s):
 def test_attn_fp8_dense(n, kv, H, Hk, per_head):
     _, (q8, k8, v8), scales = _fp8_case(n, kv, H, Hk, seed=n + kv, per_head=per_head)
     out = _run_fp8(q8, k8, v8, scales, kv, 0, kv - n)
-    model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, kv - n, q_block=128, kv_block=64)
+    model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, kv - n, q_block=128, kv_block=64,
+                                         **fp8_model_kwargs(H, Hk, -(-n // 128)))
     ref = O.attention_ref(_deq(q8, scales[0]), _deq(k8, scales[1]), _deq(v8, scales[2]), kv - n)
     assert rel_l2(out, model) < 1e-2, rel_l2(out, model)
     assert rel_l2(out, ref) < 3e-2, rel_l2(out, ref)
@@ -239,7 +241,8 @@ def test_attn_fp8_sparse(kv_block, n, kv, q_front, density):
     ref = O.attention_ref(_deq(q8, scales[0]), _deq(k8, scales[1]), _deq(v8, scales[2]), q_pos0, masks,
                           q_block=128, kv_block=kv_block, q_front=q_front)
     model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, q_pos0, counts.cpu().numpy(), lists.cpu().numpy(),
-                                         q_block=128, kv_block=kv_block, q_front=q_front)
+                                         q_block=128, kv_block=kv_block, q_front=q_front,
+                                         **fp8_model_kwargs(H, Hk, n_tiles))
     assert rel_l2(out, model) < 1e-2, rel_l2(out, model)
     assert rel_l2(out, ref) < 3e-2, rel_l2(out, ref)
 
@@ -372,7 +375,8 @@ def test_attn_fp8_random_shapes(n, kv, H, Hk, kv_block, density, front, seed):
     ref = O.attention_ref(_deq(q8, scales[0]), _deq(k8, scales[1]), _deq(v8, scales[2]), q_pos0, masks,
                           q_block=128, kv_block=kv_block, q_front=front)
     model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, q_pos0, counts.cpu().numpy(), lists.cpu().numpy(),
-                                         q_block=128, kv_block=kv_block, q_front=front)
+                                         q_block=128, kv_block=kv_block, q_front=front,
+                                         **fp8_model_kwargs(H, Hk, n_tiles))
     assert rel_l2(out, model) < 1e-2, rel_l2(out, model)
     assert rel_l2(out, ref) < 3e-2, rel_l2(out, ref)
 

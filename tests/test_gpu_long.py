@@ -19,6 +19,7 @@ import torch
 
 import oracle as O
 import synth
+from kmodel import fp8_model_kwargs
 
 pytestmark = pytest.mark.gpu
 
@@ -72,7 +73,6 @@ def _selected(inputs, kernel):
 
 
 def test_fp8_sparse_65536_keys(inputs):
-    from sm120_attn import ops as _ops_mod
     sp, ops, (qd, kd, vd), km = _selected(inputs, 'sm120fp8')
     q, k, v = inputs
     amax = [float(np.abs(f32(t)).max()) for t in (q, k, v)]
@@ -93,7 +93,7 @@ def test_fp8_sparse_65536_keys(inputs):
     assert np.isfinite(got).all()
     ref = O.attention_ref(*deq, KV - TILES * 128, masks, q_block=128, kv_block=BLK)
     model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, KV - TILES * 128, cs, ls, q_block=128, kv_block=BLK,
-                                         group=_ops_mod.FP8_KEYS_PER_TILE // 64)
+                                         **fp8_model_kwargs(len(heads), 1, TILES))
     print(f'fp8 65536 keys: kept {cs.sum() / (len(heads) * TILES * nb):.3f}, rel-L2 vs fp32 {rel_l2(got, ref):.3e}, '
           f'vs P-rounding model {rel_l2(got, model):.3e}')
     assert rel_l2(got, model) < 1e-2
@@ -125,7 +125,7 @@ def test_fp8_dense_65536_keys_per_head_scales(inputs):
     got = f32(out)[-TILES * 128:, heads]
     ref = O.attention_ref(*deq, KV - TILES * 128)
     model = O.attention_fp8_kernel_model(q8s, k8s, v8s, sqs, sks, svs, KV - TILES * 128, q_block=128, kv_block=64,
-                                         group=ops.FP8_KEYS_PER_TILE // 64)
+                                         **fp8_model_kwargs(len(heads), 1, TILES))
     print(f'fp8 dense 65536 keys: rel-L2 vs fp32 {rel_l2(got, ref):.3e}, vs P-rounding model {rel_l2(got, model):.3e}')
     assert rel_l2(got, model) < 1e-2
     assert rel_l2(got, ref) < 3e-2
