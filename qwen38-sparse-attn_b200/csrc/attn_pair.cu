@@ -74,7 +74,7 @@ struct PCfg {
     // to 448) must stay <= 448, so the FP8 kernel rescales on every increase.
     static constexpr float RESCALE_SLACK = FP8 ? 0.f : 8.f;
     // FP8: exponential pairs per group of EXP_GROUP computed with the polynomial on the FMA pipe
-    static constexpr int EXP_GROUP = 4;
+    static constexpr int EXP_GROUP = 8;
 };
 
 // ------------------------------------------------------------------------------------------------
@@ -210,32 +210,63 @@ struct PairWalk {
     }
 };
 
-__device__ __forceinline__ bool uses(const Step& s, int i) { return ((s.mk[0] | s.mk[1]) >> (2 * i)) & 3u; }
 
-// Unit -> (head, tile) of its two query tiles (head -1: absent), late (heavier) tiles first.
+
+// Unit -> (head, tile) of its two query tiles (head -1: absent).  Units run in groups of
+// UNIT_TILES consecutive query tiles from the last group to the first (late tiles hold the most
+// blocks), and within a group KV head by KV head, so the CTAs resident at one time read the keys and
+// values of a few KV heads (they stay in L2) while heavy tiles still start first.
+constexpr int UNIT_TILES = 8;
+
 __device__ __forceinline__ void unit_tiles(const Params& p, int unit, int (&h)[2], int (&m)[2]) {
     const int g = p.H / p.Hk;
-    if ((g & 1) == 0) {
-        const int per_tile = p.H / 2;
-        const int t = unit / per_tile, pr = unit - t * per_tile;
-        m[0] = m[1] = p.n_tiles - 1 - t;
-        h[0] = 2 * pr;
-        h[1] = 2 * pr + 1;
+    const bool even = (g & 1) == 0;
+    // per (KV head, tile): g/2 head pairs; odd g: g heads, tiles taken two at a time
+    const int per_kv = even ? g / 2 : g;
+    const int tile_slots = even ? p.n_tiles : (p.n_tiles + 1) / 2;      // tiles, or tile pairs
+    const int grp_span = even ? UNIT_TILES : UNIT_TILES / 2;
+    const int n_groups = (tile_slots + grp_span - 1) / grp_span;
+    // the top group (run first) may hold fewer slots than grp_span; the groups below it are full
+    const int top_span = tile_slots - (n_groups - 1) * grp_span;
+    const int top_units = top_span * p.Hk * per_kv;
+    int grp, rem, span;
+    if (unit < top_units) {
+        grp = n_groups - 1;
+        rem = unit;
+        span = top_span;
     } else {
-        const int pairs = (p.n_tiles + 1) / 2;
-        const int a = pairs - 1 - unit / p.H;
-        h[0] = h[1] = unit % p.H;
-        m[0] = 2 * a;
-        m[1] = 2 * a + 1;
+        const int u2 = unit - top_units, full_units = grp_span * p.Hk * per_kv;
+        grp = n_groups - 2 - u2 / full_units;
+        rem = u2 % full_units;
+        span = grp_span;
+    }
+    const int kvh = rem / (span * per_kv);
+    rem -= kvh * span * per_kv;
+    const int slot = grp * grp_span + (span - 1 - rem / per_kv);         // later slots first
+    const int j = rem % per_kv;
+    if (even) {
+        m[0] = m[1] = slot;
+        h[0] = kvh * g + 2 * j;
+        h[1] = h[0] + 1;
+    } else {
+        h[0] = h[1] = kvh * g + j;
+        m[0] = 2 * slot;
+        m[1] = 2 * slot + 1;
         if (m[1] >= p.n_tiles) h[1] = -1;
     }
 }
 
 // Register split: the kernel launches 384 threads x 168 registers (64512); the producer / issuer
-// warpgroup gives up 96 per thread (72 left), the two softmax warpgroups take 48 more (216):
-// 128 x 72 + 256 x 216 = 64512, the launch total, so the increase never waits.
-__device__ __forceinline__ void reg_dealloc_producer() { asm volatile("setmaxnreg.dec.sync.aligned.u32 72;" ::: "memory"); }
+// warpgroup gives up 104 per thread (64 left), the two softmax warpgroups take 48 more (216):
+// 128 x 64 + 256 x 216 = 63488, within the launch total, so the increase never waits.
+__device__ __forceinline__ void reg_dealloc_producer() { asm volatile("setmaxnreg.dec.sync.aligned.u32 64;" ::: "memory"); }
 __device__ __forceinline__ void reg_alloc_softmax() { asm volatile("setmaxnreg.inc.sync.aligned.u32 216;" ::: "memory"); }
+
+// Step descriptor in shared memory: the two halves' key bases and masks; kb[0] == KEY_END ends a walk.
+struct __align__(16) StepDesc {
+    int kb[2];
+    uint32_t mk[2];
+};
 
 template <bool FP8>
 __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -252,10 +283,15 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
     uint64_t* bEmpty = bFull + C::NST;
     uint64_t* bS = bEmpty + C::NST;                                // [2] S of tile i ready
     uint64_t* bP = bS + 2;                                         // [2] P of tile i written (128 arrivals)
-    uint64_t* bOF = bP + 2;                                        // single phase: last MMA done
+    uint64_t* bD = bP + 2;                                         // [2] step descriptor of tile i posted
+    uint64_t* bOF = bD + 2;                                        // single phase: last MMA done
     uint64_t* bDrain = bOF + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bDrain + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    // descriptors: one per stage (written by the producer before it arms the stage), and a
+    // two-entry ring per query tile (written by the issuer before it issues the tile's Q.K^T)
+    StepDesc* stage_desc = reinterpret_cast<StepDesc*>(reinterpret_cast<uint8_t*>(bars) + 256);
+    StepDesc* tile_desc = stage_desc + C::NST;                     // [2 tiles][2 slots]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int hq[2], mq[2];
@@ -265,10 +301,11 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(bQ), 1);
         for (int i = 0; i < C::NST; ++i) { mbar_init(smem_u32(bFull + i), 1); mbar_init(smem_u32(bEmpty + i), 1); }
-        mbar_init(smem_u32(bS), 1);
-        mbar_init(smem_u32(bS + 1), 1);
-        mbar_init(smem_u32(bP), 128);
-        mbar_init(smem_u32(bP + 1), 128);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(bS + i), 1);
+            mbar_init(smem_u32(bP + i), 128);
+            mbar_init(smem_u32(bD + i), 1);
+        }
         mbar_init(smem_u32(bOF), 1);
         mbar_init(smem_u32(bDrain), 1);
         *abort_flag = 0;
@@ -286,7 +323,8 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
     if (warp >= 8) {
         reg_dealloc_producer();
         if (warp == 8) {
-            // ------------------------------------------------------------ TMA producer
+            // ------------------------------------------------------------ TMA producer: walks the
+            // merged block lists, loads each step's K and V halves, posts the step descriptor
             PairWalk walk{{make_tile_walk(p, hq[0], mq[0]), make_tile_walk(p, hq[1], mq[1])}, false};
             int par[C::NST];
             bool used[C::NST];
@@ -303,13 +341,23 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
             }
             __syncwarp();
             Step s;
-            for (int t = 0; walk.next(s, p.kv_block); ++t) {
+            for (int t = 0;; ++t) {
+                const bool have = walk.next(s, p.kv_block);
                 const int st = t % C::NST;
                 if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bEmpty + st), ((t / C::NST) & 1) ^ 1, abort_flag,
                                                         p.status, SA_DEV_WAIT_KV)))
                     break;
+                if (!have) {                                         // end of the walk
+                    if (elect_one()) {
+                        stage_desc[st].kb[0] = KEY_END;
+                        mbar_arrive(smem_u32(bFull + st));
+                    }
+                    __syncwarp();
+                    break;
+                }
                 uint8_t* dst = sKV + st * C::STAGE;
                 if (elect_one()) {
+                    stage_desc[st] = StepDesc{{s.kb[0], s.kb[1]}, {s.mk[0], s.mk[1]}};
                     mbar_arrive_expect_tx(smem_u32(bFull + st), C::STAGE);
                     for (int hf = 0; hf < 2; ++hf) {
                         // an absent half loads keys 0..63 (finite data); its scores are masked out
@@ -326,7 +374,7 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                 par[st] = (t / C::NST) & 1;
                 used[st] = true;
             }
-            if ((walk.bad || walk.w[0].bad || walk.w[1].bad) && lane == 0 && p.status) atomicOr(p.status, SA_DEV_BAD_LIST);
+            if (walk.bad && lane == 0 && p.status) atomicOr(p.status, SA_DEV_BAD_LIST);
             if (*abort_flag) {
                 mbar_drain(smem_u32(bQ), 0);
                 for (int i = 0; i < C::NST; ++i)
@@ -334,15 +382,14 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
             }
         } else if (warp == 9) {
             // ------------------------------------------------------------ MMA issuer
-            PairWalk walk{{make_tile_walk(p, hq[0], mq[0]), make_tile_walk(p, hq[1], mq[1])}, false};
             bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bQ), 0, abort_flag, p.status, SA_DEV_WAIT_Q));
-            bool pend[2] = {false, false};                           // P.V of the previous step owed
-            bool o_init[2] = {false, false};                         // O accumulates after its first P.V
-            int cnt[2] = {0, 0};                                     // steps taken by tile i
+            bool pend0 = false, pend1 = false;                       // P.V of the previous step owed
+            bool init0 = false, init1 = false;                       // O accumulates after its first P.V
+            int cnt0 = 0, cnt1 = 0;                                  // steps taken by tile 0 / 1
             int prev_st = 0;
             bool any = false;
-            auto issue_pv = [&](int i, int su) -> bool {
-                if (!__all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bP + i), (cnt[i] - 1) & 1, abort_flag, p.status,
+            auto issue_pv = [&](int i, int su, int cnt, bool& init) -> bool {
+                if (!__all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bP + i), (cnt - 1) & 1, abort_flag, p.status,
                                                              SA_DEV_WAIT_P)))
                     return false;
                 tc_fence_after();
@@ -353,12 +400,18 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                     for (int k = 0; k < C::PV_STEPS; ++k)
                         mma_ts<FP8>(tmem + C::o_col(i), a_tm + k * (C::UK * C::E / 4),
                                     smem_desc_mnmajor(v_base + k * C::UK * 128, C::V_REG), C::IDESC_PV,
-                                    (o_init[i] || k > 0) ? 1u : 0u);
+                                    (init || k > 0) ? 1u : 0u);
                 }
                 __syncwarp();
-                o_init[i] = true;
-                pend[i] = false;
+                init = true;
                 return true;
+            };
+            auto post = [&](int i, int cnt, const StepDesc& d) {     // hand tile i its step descriptor
+                if (elect_one()) {
+                    tile_desc[2 * i + (cnt & 1)] = d;
+                    mbar_arrive(smem_u32(bD + i));
+                }
+                __syncwarp();
             };
             auto issue_qk = [&](int i, int st) {
                 const uint32_t q_base = smem_u32(sQ + i * C::Q_BYTES);
@@ -374,36 +427,52 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                     tc_commit(smem_u32(bS + i));
                 }
                 __syncwarp();
-                ++cnt[i];
-                pend[i] = true;
             };
-            Step s;
+            const StepDesc end_desc{{KEY_END, KEY_END}, {0u, 0u}};
             for (int u = 0; ok; ++u) {
-                const bool have = walk.next(s, p.kv_block);
                 const int st = u % C::NST;
-                const bool use0 = have && uses(s, 0), use1 = have && uses(s, 1);
-                if (pend[0] && !(ok = issue_pv(0, prev_st))) break;
-                if (!have) {
-                    if (pend[1] && !(ok = issue_pv(1, prev_st))) break;
-                    break;
-                }
+                if (pend0 && !(ok = issue_pv(0, prev_st, cnt0, init0))) break;
+                pend0 = false;
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bFull + st), (u / C::NST) & 1, abort_flag,
                                                                   p.status, SA_DEV_WAIT_KV))))
                     break;
+                const StepDesc d = stage_desc[st];
+                if (d.kb[0] == KEY_END) {
+                    if (pend1 && !(ok = issue_pv(1, prev_st, cnt1, init1))) break;
+                    pend1 = false;
+                    break;
+                }
                 tc_fence_after();
                 any = true;
-                if (use0) issue_qk(0, st);
-                if (pend[1] && !(ok = issue_pv(1, prev_st))) break;
+                const bool use0 = ((d.mk[0] | d.mk[1]) & 3u) != 0u, use1 = ((d.mk[0] | d.mk[1]) & 12u) != 0u;
+                if (use0) {
+                    post(0, cnt0, d);
+                    issue_qk(0, st);
+                    ++cnt0;
+                    pend0 = true;
+                }
+                if (pend1 && !(ok = issue_pv(1, prev_st, cnt1, init1))) break;
+                pend1 = false;
                 if (u > 0) {
                     if (elect_one()) tc_commit(smem_u32(bEmpty + prev_st));   // both P.V of step u-1 issued
                     __syncwarp();
                 }
-                if (use1) issue_qk(1, st);
+                if (use1) {
+                    post(1, cnt1, d);
+                    issue_qk(1, st);
+                    ++cnt1;
+                    pend1 = true;
+                }
                 prev_st = st;
             }
-            if (ok && any) {
-                if (elect_one()) tc_commit(smem_u32(bOF));
-                __syncwarp();
+            if (ok) {
+                // end markers for the softmax warpgroups (their last P arrived before the last P.V)
+                post(0, cnt0, end_desc);
+                post(1, cnt1, end_desc);
+                if (any) {
+                    if (elect_one()) tc_commit(smem_u32(bOF));
+                    __syncwarp();
+                }
             }
             if (*abort_flag) {
                 if (elect_one()) tc_commit(smem_u32(bDrain));
@@ -437,49 +506,46 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
         }
         const float pbias = FP8 ? LOG2_448 : 0.f;
         float m_run = -INFINITY, l_run = 0.f;
-        bool ok = true;
+        bool ok = present;
         int t = 0;                                                   // steps this tile took
-        PairWalk walk{{make_tile_walk(p, hq[0], mq[0]), make_tile_walk(p, hq[1], mq[1])}, false};
-        Step s;
-        while (present && walk.next(s, p.kv_block)) {
-            if (!uses(s, i)) continue;
+        while (ok) {
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bD + i), t & 1, abort_flag, p.status, SA_DEV_WAIT_S));
+            if (!ok) break;
+            const StepDesc d = tile_desc[2 * i + (t & 1)];
+            if (d.kb[0] == KEY_END) break;
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bS + i), t & 1, abort_flag, p.status, SA_DEV_WAIT_S));
             if (!ok) break;
             tc_fence_after();
-            float x[128];
-            {
-                uint32_t u[32];
+            uint32_t u[128];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    tmem_ld32(tS + 32 * c, u);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) x[32 * c + j] = __uint_as_float(u[j]);
-                }
-            }
+            for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
+            tmem_wait_ld();
             // masking: a half this row did not select, keys past the row's position or past kv_len
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
-                const int kb = s.kb[hf];
-                const bool sel = (s.mk[hf] & my_bit) != 0u;
+                const int kb = d.kb[hf];
+                const bool sel = (d.mk[hf] & my_bit) != 0u;
                 if (!sel || kb + 63 > qpos_min || kb + 63 >= p.kv_len) {
                     const int lim = sel ? vis - kb : -1;             // visible columns: c <= lim
 #pragma unroll
                     for (int c = 0; c < 64; ++c)
-                        if (c > lim) x[64 * hf + c] = -INFINITY;
+                        if (c > lim) u[64 * hf + c] = 0xff800000u;  // -inf
                 }
             }
             float mx;
             {
                 float a[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) a[j] = fmax3(x[j], x[16 + j], x[32 + j]);
+                for (int j = 0; j < 16; ++j)
+                    a[j] = fmax3(__uint_as_float(u[j]), __uint_as_float(u[16 + j]), __uint_as_float(u[32 + j]));
 #pragma unroll
-                for (int j = 0; j < 16; ++j) a[j] = fmax3(a[j], x[48 + j], x[64 + j]);
+                for (int j = 0; j < 16; ++j)
+                    a[j] = fmax3(a[j], __uint_as_float(u[48 + j]), __uint_as_float(u[64 + j]));
 #pragma unroll
-                for (int j = 0; j < 16; ++j) a[j] = fmax3(a[j], x[80 + j], x[96 + j]);
+                for (int j = 0; j < 16; ++j)
+                    a[j] = fmax3(a[j], __uint_as_float(u[80 + j]), __uint_as_float(u[96 + j]));
 #pragma unroll
-                for (int j = 0; j < 16; ++j) a[j] = fmaxf(a[j], x[112 + j]);
+                for (int j = 0; j < 16; ++j) a[j] = fmaxf(a[j], __uint_as_float(u[112 + j]));
 #pragma unroll
                 for (int j = 0; j < 5; ++j) a[j] = fmax3(a[3 * j], a[3 * j + 1], a[3 * j + 2]);
                 mx = fmax3(fmax3(a[0], a[1], a[2]), fmaxf(a[3], a[4]), a[15]);
@@ -493,38 +559,36 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
             float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                              make_float2(0.f, 0.f)};
             auto exp_pair = [&](int c) -> float2 {
-                const float2 e = ffma2(make_float2(x[c], x[c + 1]), sl2v, biasv);
+                const float2 e = ffma2(make_float2(__uint_as_float(u[c]), __uint_as_float(u[c + 1])), sl2v, biasv);
                 // FP8: one exponential pair in EXP_GROUP on the FMA pipe (exp2_poly's 7.5e-5 relative
                 // error is far below e4m3's rounding), easing the MUFU unit
                 const bool on_fma = FP8 && ((c >> 1) % C::EXP_GROUP) == C::EXP_GROUP - 1;
-                const float2 pr = on_fma ? make_float2(exp2_poly(e.x), exp2_poly(e.y))
-                                         : make_float2(ex2_approx(e.x), ex2_approx(e.y));
+                const float2 pr = on_fma ? exp2_poly2(e) : make_float2(ex2_approx(e.x), ex2_approx(e.y));
                 acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pr);
                 return pr;
             };
-            {
+            if constexpr (FP8) {
+                // 128 keys -> 32 columns of 4 e4m3 values (key 4c+j in byte j of column c)
                 uint32_t pk[32];
-                if constexpr (FP8) {
-                    // 128 keys -> 32 columns of 4 e4m3 values (key 4c+j in byte j of column c)
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const float2 p01 = exp_pair(4 * c);
+                    const float2 p23 = exp_pair(4 * c + 2);
+                    pk[c] = static_cast<uint32_t>(pack_e4m3x2(p01.x, p01.y)) |
+                            (static_cast<uint32_t>(pack_e4m3x2(p23.x, p23.y)) << 16);
+                }
+                tmem_st32(tS, pk);
+            } else {
+                // 128 keys -> 64 columns of 2 bf16 values (key 2c+j in half j of column c)
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t pk[32];
 #pragma unroll
                     for (int c = 0; c < 32; ++c) {
-                        const float2 p01 = exp_pair(4 * c);
-                        const float2 p23 = exp_pair(4 * c + 2);
-                        pk[c] = static_cast<uint32_t>(pack_e4m3x2(p01.x, p01.y)) |
-                                (static_cast<uint32_t>(pack_e4m3x2(p23.x, p23.y)) << 16);
+                        const float2 pr = exp_pair(64 * hh + 2 * c);
+                        pk[c] = pack_bf16x2(pr.x, pr.y);
                     }
-                    tmem_st32(tS, pk);
-                } else {
-                    // 128 keys -> 64 columns of 2 bf16 values (key 2c+j in half j of column c)
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-                        for (int c = 0; c < 32; ++c) {
-                            const float2 pr = exp_pair(64 * hh + 2 * c);
-                            pk[c] = pack_bf16x2(pr.x, pr.y);
-                        }
-                        tmem_st32(tS + 32 * hh, pk);
-                    }
+                    tmem_st32(tS + 32 * hh, pk);
                 }
             }
             const float2 s01 = fadd2(acc[0], acc[1]), s23 = fadd2(acc[2], acc[3]);
@@ -534,14 +598,16 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                 // O rescale in TMEM.  S(t) complete implies the P.V of this tile's previous step is
                 // complete (the issuer issued it before this step's Q.K^T), and this step's P.V waits
                 // for the P barrier below.
-                uint32_t u[32];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    tmem_ld32(tO + 32 * c, u);
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t o[64];
+                    tmem_ld32(tO + 64 * c, *reinterpret_cast<uint32_t(*)[32]>(o));
+                    tmem_ld32(tO + 64 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(__uint_as_float(u[j]) * alpha);
-                    tmem_st32(tO + 32 * c, u);
+                    for (int j = 0; j < 64; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+                    tmem_st32(tO + 64 * c, *reinterpret_cast<uint32_t(*)[32]>(o));
+                    tmem_st32(tO + 64 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
                 }
             }
             tmem_wait_st();
@@ -560,19 +626,19 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                          static_cast<int64_t>(h) * p.o_head_stride;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-            uint32_t u[32];
+            uint32_t o[32];
             if (have_o) {
-                tmem_ld32(tO + c * 32, u);
+                tmem_ld32(tO + c * 32, o);
                 tmem_wait_ld();
             } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) u[j] = 0u;
+                for (int j = 0; j < 32; ++j) o[j] = 0u;
             }
             if (row_ok) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                    pk[j] = pack_bf16x2(__uint_as_float(u[2 * j]) * inv, __uint_as_float(u[2 * j + 1]) * inv);
+                    pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
                 uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);

@@ -130,6 +130,20 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return d;
 }
 
+// exp2_poly on a pair of values with packed f32x2 arithmetic (same reduction and coefficients; two
+// results for about the instruction count of one).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    x = make_float2(fmaxf(x.x, -120.f), fmaxf(x.y, -120.f));
+    const float2 magic = make_float2(12582912.f, 12582912.f), neg_magic = make_float2(-12582912.f, -12582912.f);
+    const float2 y = fadd2(x, magic);
+    const float2 f = ffma2(fadd2(y, neg_magic), make_float2(-1.f, -1.f), x);
+    float2 p = ffma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.242611125f, 0.242611125f));
+    p = ffma2(p, f, make_float2(0.693260968f, 0.693260968f));
+    p = ffma2(p, f, make_float2(0.999928057f, 0.999928057f));
+    return make_float2(__int_as_float(__float_as_int(p.x) + __float_as_int(y.x) * 8388608),
+                       __int_as_float(__float_as_int(p.y) + __float_as_int(y.y) * 8388608));
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
