@@ -25,8 +25,9 @@ struct Params {
     int32_t* status;
 };
 
-// Paired-tile attention kernel (attn_pair.cu): two 128-row query tiles per CTA sharing each K/V
-// stage.  Takes the tensor maps launch_attn built (64-row K/V boxes) and validated parameters.
+// Paired-tile attention kernel (attn_pair.cu, FP8 only): two 128-row query tiles per CTA sharing
+// each K/V stage.  Takes the tensor maps launch_attn built (64-row K/V boxes) and validated
+// parameters.
 template <bool FP8>
 int launch_attn_pair(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV, const Params& p,
                      cudaStream_t stream, const char* name);

@@ -434,17 +434,16 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
 // ------------------------------------------------------------------------------------------------
 // Host side: tensor maps and launch
 // ------------------------------------------------------------------------------------------------
-// Which kernel serves a call: the paired-tile kernel (attn_pair.cu) for FP8, this file's one-tile
-// kernel for BF16.  SA_ATTN_KERNEL=tile or =pair forces one for both (read once per process).
-bool use_pair_kernel(bool fp8) {
-    static int forced = -1;                                  // -1 default, 0 tile, 1 pair
+// Which kernel serves an FP8 call: the paired-tile kernel (attn_pair.cu) unless SA_ATTN_KERNEL=tile
+// selects this file's one-tile kernel (read once per process).  BF16 always uses the one-tile kernel.
+bool use_pair_kernel() {
+    static bool pair = true;
     static std::once_flag once;
     std::call_once(once, [] {
         const char* e = std::getenv("SA_ATTN_KERNEL");
-        if (e && !std::strcmp(e, "tile")) forced = 0;
-        if (e && !std::strcmp(e, "pair")) forced = 1;
+        if (e && !std::strcmp(e, "tile")) pair = false;
     });
-    return forced < 0 ? fp8 : forced == 1;
+    return pair;
 }
 
 template <bool FP8>
@@ -503,7 +502,9 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     p.vss = vss;
     p.softmax_scale = softmax_scale;
     p.status = status;
-    if (use_pair_kernel(FP8)) return launch_attn_pair<FP8>(tmQ, tmK, tmV, p, stream, name);
+    if constexpr (FP8) {
+        if (use_pair_kernel()) return launch_attn_pair<true>(tmQ, tmK, tmV, p, stream, name);
+    }
     static PerContext attr;                                  // shared-memory opt-in, once per device context
     int dev = 0;
     void* ctx = nullptr;
