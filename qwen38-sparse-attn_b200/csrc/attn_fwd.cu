@@ -66,6 +66,11 @@ struct Cfg {
 };
 
 
+#ifndef SA_TILE_EXP_POLY
+#define SA_TILE_EXP_POLY 3           // exponential pairs in eight on the FMA pipe (FP8)
+#endif
+constexpr int TILE_EXP_POLY = SA_TILE_EXP_POLY;
+
 template <bool FP8>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                           const __grid_constant__ CUtensorMap tmK,
@@ -336,11 +341,10 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                              make_float2(0.f, 0.f)};
             auto exp_pair = [&](int c) -> float2 {
                 const float2 e = ffma2(make_float2(x[c], x[c + 1]), sl2v, biasv);
-                // FP8: one pair in eight on the FMA pipe, easing the MUFU unit (exp2_poly's 7.5e-5
-                // relative error is far below e4m3's rounding)
-                const bool on_fma = FP8 && ((c >> 1) & 7) == 7;
-                const float2 pr = on_fma ? make_float2(exp2_poly(e.x), exp2_poly(e.y))
-                                         : make_float2(ex2_approx(e.x), ex2_approx(e.y));
+                // FP8: TILE_EXP_POLY pairs in eight on the FMA pipe, easing the MUFU unit (exp2_poly's
+                // 7.5e-5 relative error is far below e4m3's rounding)
+                const bool on_fma = FP8 && ((c >> 1) & 7) >= 8 - TILE_EXP_POLY;
+                const float2 pr = on_fma ? exp2_poly2(e) : make_float2(ex2_approx(e.x), ex2_approx(e.y));
                 acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pr);
                 return pr;
             };
@@ -434,14 +438,15 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
 // ------------------------------------------------------------------------------------------------
 // Host side: tensor maps and launch
 // ------------------------------------------------------------------------------------------------
-// Which kernel serves an FP8 call: the paired-tile kernel (attn_pair.cu) unless SA_ATTN_KERNEL=tile
-// selects this file's one-tile kernel (read once per process).  BF16 always uses the one-tile kernel.
+// Which kernel serves an FP8 call: this file's one-tile kernel, or the paired-tile kernel
+// (attn_pair.cu) when SA_ATTN_KERNEL=pair (read once per process; measured slower on the benchmark
+// shapes, kept as an option).  BF16 always uses the one-tile kernel.
 bool use_pair_kernel() {
-    static bool pair = true;
+    static bool pair = false;
     static std::once_flag once;
     std::call_once(once, [] {
         const char* e = std::getenv("SA_ATTN_KERNEL");
-        if (e && !std::strcmp(e, "tile")) pair = false;
+        if (e && !std::strcmp(e, "pair")) pair = true;
     });
     return pair;
 }

@@ -1,5 +1,5 @@
-// Kernel (c), paired-tile form: block-sparse causal FlashAttention forward (FP8 e4m3) on sm_100a
-// tensor cores, two 128-row query tiles per CTA sharing every K/V stage.
+// Kernel (c), paired-tile form: block-sparse causal FlashAttention forward on sm_100a tensor cores,
+// two 128-row query tiles per CTA sharing every K/V stage.
 //
 // A CTA owns one work unit: two query tiles that read the same KV head - two query heads of one
 // GQA group at the same 128-row tile, or (odd group sizes) two neighbouring tiles of one head.  The
@@ -8,24 +8,27 @@
 // The producer loads each step's K and V once into a stage ring; each query tile runs its own
 // online softmax over the steps it selected.  One CTA per SM (all 512 tensor-memory columns):
 //
-//   TMEM columns   [0,128) S of tile 0   [128,256) S of tile 1   [256,384) O of tile 0   [384,512) O of tile 1
-//   shared memory  Q0, Q1, P0, P1 (e4m3, 128 rows x 128 keys, 128B-swizzled), K/V stage ring
+//   TMEM columns   [0,128) S/P of tile 0   [128,256) S/P of tile 1
+//                  [256,384) O of tile 0   [384,512) O of tile 1
 //   warps 0-3      softmax + epilogue of tile 0 (thread r owns row r = TMEM lane r)
 //   warps 4-7      softmax + epilogue of tile 1
-//   warp 8         TMA producer: walks the lists, loads Q once and K and V of each step (two 64-key
-//                  halves each), posts each step's descriptor with its stage
+//   warp 8         TMA producer: Q tiles once, then K and V of each step (two 64-key halves each)
 //   warp 9         TMEM allocator and single-thread tcgen05.mma issuer
 //   warps 10-11    idle (they complete the warpgroup that holds the producer and the issuer)
 //
-// P goes through shared memory, not back into the S columns: a tile's softmax releases its S
-// columns as soon as it has loaded them, so the issuer computes the next S = Q K^T while that
-// softmax is still on its exponentials, and O += P V runs from shared memory (both operands) once
-// P is written.  Per step u the issuer runs S0(u), S1(u), O0 += P0(u-1) V(u-1), O1 += P1(u-1) V(u-1)
-// (each only for a tile that selected the step); the tensor core never waits on a P.V -> Q.K^T
-// turnaround, only on the softmax itself.
+// Per step u the issuer runs  O0 += P0(u-1) V(u-1),  S0(u) = Q0 K(u)^T,  O1 += P1(u-1) V(u-1),
+// S1(u) = Q1 K(u)^T  (each only for a tile that selected the step), so one tile's P.V and next
+// Q.K^T run on the tensor core while the other tile's softmax works: the two softmax warpgroups
+// alternate and every step keeps N = 128 for both contractions.  P is written back into the S
+// columns (e4m3 x 448, or bf16), the next S of a tile overwrites them only after the P.V that reads
+// them (tcgen05 operations of one thread execute in issue order).
 //
 // Every mbarrier wait is bounded (sa_common.cuh); on expiry the CTA drains its copies and MMAs,
 // frees TMEM, writes zeros for its rows and sets a status bit.
+//
+// FP8 only, selected with SA_ATTN_KERNEL=pair.  On the benchmark shapes it runs 2-5% slower than the
+// one-tile kernel of attn_fwd.cu (the default): a tile waits for its own P.V and next Q.K^T before
+// each step (its S columns hold P), and the exponentials, not the tensor core, bound both designs.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -42,36 +45,42 @@ namespace {
 
 template <bool FP8>
 struct PCfg {
-    static_assert(FP8, "the paired-tile kernel is FP8 only (bf16 P, Q and K/V stages exceed shared memory)");
-    static constexpr int E = 1;                           // bytes per operand element
+    static constexpr int E = FP8 ? 1 : 2;                 // bytes per operand element
     static constexpr int D = 128;                         // head_dim
     static constexpr int BM = 128;                        // query rows per tile (TMEM lanes)
     static constexpr int BN = 128;                        // keys per step (two 64-key halves)
     static constexpr int HALF = 64;
-    static constexpr int NST = 4;                         // K+V stages
-    static constexpr int UK = 32;                         // MMA K per instruction (e4m3)
+    static constexpr int NST = FP8 ? 5 : 2;               // K+V stages
+    static constexpr int UK = FP8 ? 32 : 16;              // MMA K per instruction
     static constexpr int QK_STEPS = D / UK;
     static constexpr int PV_STEPS = BN / UK;
-    static constexpr int Q_BYTES = BM * 128;              // 128 rows x 128 B (head_dim 128 e4m3)
-    static constexpr int P_BYTES = BM * 128;              // 128 rows x 128 keys e4m3
-    static constexpr int K_BYTES = BN * 128;              // 128 keys x 128 B (halves at +8 KB)
-    static constexpr int V_BYTES = BN * 128;
-    static constexpr int HALF_BYTES = HALF * 128;         // one 64-key half
+    static constexpr int REG_ELEMS = 128 / E;             // head_dim elements per 128-byte swizzle row
+    static constexpr int NREG = D / REG_ELEMS;            // swizzle regions along head_dim
+    static constexpr int Q_REG = BM * 128;                // one Q region: 128 rows x 128 B
+    static constexpr int Q_BYTES = NREG * Q_REG;
+    static constexpr int K_REG = BN * 128;                // one K region: 128 keys x 128 B (halves at +8 KB)
+    static constexpr int K_BYTES = NREG * K_REG;
+    static constexpr int V_REG = BN * 128;                // one V region: 128 keys x 128 B of head_dim
+    static constexpr int V_BYTES = NREG * V_REG;
+    static constexpr int HALF_BYTES = HALF * 128;         // one 64-key half of one region
     static constexpr int STAGE = K_BYTES + V_BYTES;
-    static constexpr int SMEM_TILES = 2 * Q_BYTES + 2 * P_BYTES + NST * STAGE;
-    static constexpr int SMEM_BYTES = SMEM_TILES + 1024 /*barriers, descriptors*/ + 1024 /*alignment*/;
-    static constexpr uint32_t IDESC_QK = instr_desc(128, BN, 0u);
-    static constexpr uint32_t IDESC_PV = instr_desc(128, D, 0u) | (1u << 16);   // B (V) MN-major
+    static constexpr int SMEM_TILES = 2 * Q_BYTES + NST * STAGE;
+    static constexpr int SMEM_BYTES = SMEM_TILES + 1024 /*barriers*/ + 1024 /*alignment*/;
+    static constexpr uint32_t FMT = FP8 ? 0u : 1u;
+    static constexpr uint32_t IDESC_QK = instr_desc(128, BN, FMT);
+    static constexpr uint32_t IDESC_PV = instr_desc(128, D, FMT) | (1u << 16);   // B (V) MN-major
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr int THREADS = 384;
-    // TMEM columns of tile i: S at s_col(i), O at o_col(i)
+    // TMEM columns of tile i: S/P at s_col(i), O at o_col(i)
     __host__ __device__ static constexpr uint32_t s_col(int i) { return 128u * i; }
     __host__ __device__ static constexpr uint32_t o_col(int i) { return 256u + 128u * i; }
-    // e4m3 P (scaled to 448) must stay <= 448, so O is rescaled on every increase of the row max
-    // Of every 8 exponential pairs, EXP_POLY are computed with the polynomial on the FMA pipe and
-    // the rest on the MUFU unit.
+    // Rescale O only when the running row max grows by more than this (log2 units); e4m3 P (scaled
+    // to 448) must stay <= 448, so the FP8 kernel rescales on every increase.
+    static constexpr float RESCALE_SLACK = FP8 ? 0.f : 8.f;
+    // FP8: of every 8 exponential pairs, EXP_POLY are computed with the polynomial on the FMA pipe
+    // and the rest on the MUFU unit
 #ifndef SA_EXP_POLY
-#define SA_EXP_POLY 1
+#define SA_EXP_POLY 2
 #endif
     static constexpr int EXP_POLY = SA_EXP_POLY;
 };
@@ -267,10 +276,6 @@ struct __align__(16) StepDesc {
     uint32_t mk[2];
 };
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" :: "r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
 template <bool FP8>
 __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                            const __grid_constant__ CUtensorMap tmK,
@@ -279,17 +284,14 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem;                                            // [2][Q_BYTES]
-    uint8_t* sP = sQ + 2 * C::Q_BYTES;                             // [2][P_BYTES]
-    uint8_t* sKV = sP + 2 * C::P_BYTES;                            // stage s: K at s*STAGE, V after it
+    uint8_t* sKV = sQ + 2 * C::Q_BYTES;                            // stage s: K at s*STAGE, V after it
     uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + C::NST * C::STAGE);
     uint64_t* bQ = bars;
     uint64_t* bFull = bars + 1;
     uint64_t* bEmpty = bFull + C::NST;
-    uint64_t* bS = bEmpty + C::NST;                                // [2] S of tile i ready (commit)
-    uint64_t* bSfree = bS + 2;                                     // [2] S of tile i loaded by its softmax
-    uint64_t* bP = bSfree + 2;                                     // [2] P of tile i written
-    uint64_t* bPfree = bP + 2;                                     // [2] O += P V of tile i done (commit)
-    uint64_t* bD = bPfree + 2;                                     // [2] step descriptor of tile i posted
+    uint64_t* bS = bEmpty + C::NST;                                // [2] S of tile i ready
+    uint64_t* bP = bS + 2;                                         // [2] P of tile i written (128 arrivals)
+    uint64_t* bD = bP + 2;                                         // [2] step descriptor of tile i posted
     uint64_t* bOF = bD + 2;                                        // single phase: last MMA done
     uint64_t* bDrain = bOF + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bDrain + 1);
@@ -309,9 +311,7 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
         for (int i = 0; i < C::NST; ++i) { mbar_init(smem_u32(bFull + i), 1); mbar_init(smem_u32(bEmpty + i), 1); }
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(bS + i), 1);
-            mbar_init(smem_u32(bSfree + i), 128);
             mbar_init(smem_u32(bP + i), 128);
-            mbar_init(smem_u32(bPfree + i), 1);
             mbar_init(smem_u32(bD + i), 1);
         }
         mbar_init(smem_u32(bOF), 1);
@@ -343,7 +343,9 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                 const int nq = hq[1] >= 0 ? 2 : 1;
                 mbar_arrive_expect_tx(smem_u32(bQ), nq * C::Q_BYTES);
                 for (int i = 0; i < nq; ++i)
-                    tma_load_3d(smem_u32(sQ + i * C::Q_BYTES), &tmQ, smem_u32(bQ), 0, hq[i], mq[i] * 128 - p.q_front);
+                    for (int r = 0; r < C::NREG; ++r)
+                        tma_load_3d(smem_u32(sQ + i * C::Q_BYTES + r * C::Q_REG), &tmQ, smem_u32(bQ),
+                                    r * C::REG_ELEMS, hq[i], mq[i] * 128 - p.q_front);
             }
             __syncwarp();
             Step s;
@@ -368,9 +370,12 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                     for (int hf = 0; hf < 2; ++hf) {
                         // an absent half loads keys 0..63 (finite data); its scores are masked out
                         const int kb = s.kb[hf] == KEY_NONE ? 0 : s.kb[hf];
-                        tma_load_3d(smem_u32(dst + hf * C::HALF_BYTES), &tmK, smem_u32(bFull + st), 0, hk, kb);
-                        tma_load_3d(smem_u32(dst + C::K_BYTES + hf * C::HALF_BYTES), &tmV, smem_u32(bFull + st), 0,
-                                    hk, kb);
+                        for (int r = 0; r < C::NREG; ++r) {
+                            tma_load_3d(smem_u32(dst + r * C::K_REG + hf * C::HALF_BYTES), &tmK, smem_u32(bFull + st),
+                                        r * C::REG_ELEMS, hk, kb);
+                            tma_load_3d(smem_u32(dst + C::K_BYTES + r * C::V_REG + hf * C::HALF_BYTES), &tmV,
+                                        smem_u32(bFull + st), r * C::REG_ELEMS, hk, kb);
+                        }
                     }
                 }
                 __syncwarp();
@@ -385,15 +390,30 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
             }
         } else if (warp == 9) {
             // ------------------------------------------------------------ MMA issuer
-            // Per step u: S0(u), S1(u) (each once its softmax has loaded the previous S), then
-            // O0 += P0(u-1) V(u-1), O1 += P1(u-1) V(u-1) (each once its P is written), then the
-            // release of step u-1's stage.
             bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bQ), 0, abort_flag, p.status, SA_DEV_WAIT_Q));
-            int nqk[2] = {0, 0};                                     // Q.K^T issued per tile
-            int npv[2] = {0, 0};                                     // P.V issued per tile
-            bool pend[2] = {false, false};                           // P.V of the previous step owed
+            bool pend0 = false, pend1 = false;                       // P.V of the previous step owed
+            bool init0 = false, init1 = false;                       // O accumulates after its first P.V
+            int cnt0 = 0, cnt1 = 0;                                  // steps taken by tile 0 / 1
             int prev_st = 0;
             bool any = false;
+            auto issue_pv = [&](int i, int su, int cnt, bool& init) -> bool {
+                if (!__all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bP + i), (cnt - 1) & 1, abort_flag, p.status,
+                                                             SA_DEV_WAIT_P)))
+                    return false;
+                tc_fence_after();
+                const uint32_t v_base = smem_u32(sKV + su * C::STAGE + C::K_BYTES);
+                const uint32_t a_tm = tmem + C::s_col(i);
+                if (elect_one()) {
+#pragma unroll
+                    for (int k = 0; k < C::PV_STEPS; ++k)
+                        mma_ts<FP8>(tmem + C::o_col(i), a_tm + k * (C::UK * C::E / 4),
+                                    smem_desc_mnmajor(v_base + k * C::UK * 128, C::V_REG), C::IDESC_PV,
+                                    (init || k > 0) ? 1u : 0u);
+                }
+                __syncwarp();
+                init = true;
+                return true;
+            };
             auto post = [&](int i, int cnt, const StepDesc& d) {     // hand tile i its step descriptor
                 if (elect_one()) {
                     tile_desc[2 * i + (cnt & 1)] = d;
@@ -401,76 +421,62 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                 }
                 __syncwarp();
             };
-            auto issue_qk = [&](int i, int st, const StepDesc& d) -> bool {
-                if (nqk[i] > 0 && !__all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bSfree + i), (nqk[i] - 1) & 1,
-                                                                           abort_flag, p.status, SA_DEV_WAIT_S)))
-                    return false;
-                post(i, nqk[i], d);
-                tc_fence_after();
+            auto issue_qk = [&](int i, int st) {
                 const uint32_t q_base = smem_u32(sQ + i * C::Q_BYTES);
                 const uint32_t k_base = smem_u32(sKV + st * C::STAGE);
                 if (elect_one()) {
 #pragma unroll
-                    for (int k = 0; k < C::QK_STEPS; ++k)
-                        mma_ss<true>(tmem + C::s_col(i), smem_desc_kmajor(q_base + k * C::UK, 128),
-                                     smem_desc_kmajor(k_base + k * C::UK, 128), C::IDESC_QK, k > 0 ? 1u : 0u);
+                    for (int k = 0; k < C::QK_STEPS; ++k) {
+                        const uint32_t off = (k * C::UK * C::E / 128) * C::Q_REG + (k * C::UK * C::E) % 128;
+                        const uint32_t koff = (k * C::UK * C::E / 128) * C::K_REG + (k * C::UK * C::E) % 128;
+                        mma_ss<FP8>(tmem + C::s_col(i), smem_desc_kmajor(q_base + off, 128),
+                                    smem_desc_kmajor(k_base + koff, 128), C::IDESC_QK, k > 0 ? 1u : 0u);
+                    }
                     tc_commit(smem_u32(bS + i));
                 }
                 __syncwarp();
-                ++nqk[i];
-                return true;
-            };
-            auto issue_pv = [&](int i, int su) -> bool {
-                if (!__all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bP + i), npv[i] & 1, abort_flag, p.status,
-                                                             SA_DEV_WAIT_P)))
-                    return false;
-                tc_fence_after();
-                const uint32_t p_base = smem_u32(sP + i * C::P_BYTES);
-                const uint32_t v_base = smem_u32(sKV + su * C::STAGE + C::K_BYTES);
-                if (elect_one()) {
-#pragma unroll
-                    for (int k = 0; k < C::PV_STEPS; ++k)
-                        mma_ss<true>(tmem + C::o_col(i), smem_desc_kmajor(p_base + k * C::UK, 128),
-                                     smem_desc_mnmajor(v_base + k * C::UK * 128, C::V_BYTES), C::IDESC_PV,
-                                     (npv[i] > 0 || k > 0) ? 1u : 0u);
-                    tc_commit(smem_u32(bPfree + i));
-                }
-                __syncwarp();
-                ++npv[i];
-                return true;
             };
             const StepDesc end_desc{{KEY_END, KEY_END}, {0u, 0u}};
             for (int u = 0; ok; ++u) {
                 const int st = u % C::NST;
+                if (pend0 && !(ok = issue_pv(0, prev_st, cnt0, init0))) break;
+                pend0 = false;
                 if (!(ok = __all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bFull + st), (u / C::NST) & 1, abort_flag,
                                                                   p.status, SA_DEV_WAIT_KV))))
                     break;
                 const StepDesc d = stage_desc[st];
-                const bool end = d.kb[0] == KEY_END;
-                bool use[2] = {false, false};
-                if (!end) {
-                    tc_fence_after();
-                    any = true;
-                    use[0] = ((d.mk[0] | d.mk[1]) & 3u) != 0u;
-                    use[1] = ((d.mk[0] | d.mk[1]) & 12u) != 0u;
-                    if (use[0] && !(ok = issue_qk(0, st, d))) break;
-                    if (use[1] && !(ok = issue_qk(1, st, d))) break;
+                if (d.kb[0] == KEY_END) {
+                    if (pend1 && !(ok = issue_pv(1, prev_st, cnt1, init1))) break;
+                    pend1 = false;
+                    break;
                 }
-                if (pend[0] && !(ok = issue_pv(0, prev_st))) break;
-                if (pend[1] && !(ok = issue_pv(1, prev_st))) break;
+                tc_fence_after();
+                any = true;
+                const bool use0 = ((d.mk[0] | d.mk[1]) & 3u) != 0u, use1 = ((d.mk[0] | d.mk[1]) & 12u) != 0u;
+                if (use0) {
+                    post(0, cnt0, d);
+                    issue_qk(0, st);
+                    ++cnt0;
+                    pend0 = true;
+                }
+                if (pend1 && !(ok = issue_pv(1, prev_st, cnt1, init1))) break;
+                pend1 = false;
                 if (u > 0) {
-                    if (elect_one()) tc_commit(smem_u32(bEmpty + prev_st));   // every MMA of step u-1 issued
+                    if (elect_one()) tc_commit(smem_u32(bEmpty + prev_st));   // both P.V of step u-1 issued
                     __syncwarp();
                 }
-                if (end) break;
-                pend[0] = use[0];
-                pend[1] = use[1];
+                if (use1) {
+                    post(1, cnt1, d);
+                    issue_qk(1, st);
+                    ++cnt1;
+                    pend1 = true;
+                }
                 prev_st = st;
             }
             if (ok) {
-                // end markers for the softmax warpgroups (posted after their last P.V)
-                post(0, nqk[0], end_desc);
-                post(1, nqk[1], end_desc);
+                // end markers for the softmax warpgroups (their last P arrived before the last P.V)
+                post(0, cnt0, end_desc);
+                post(1, cnt1, end_desc);
                 if (any) {
                     if (elect_one()) tc_commit(smem_u32(bOF));
                     __syncwarp();
@@ -491,8 +497,6 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
         const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
         const uint32_t tS = tmem + lane_off + C::s_col(i);
         const uint32_t tO = tmem + lane_off + C::o_col(i);
-        // this row's P in shared memory: 128B-swizzled rows (16-byte chunk j of row r at chunk j ^ (r & 7))
-        const uint32_t p_row = smem_u32(sP + i * C::P_BYTES) + (r >> 3) * 1024 + (r & 7) * 128;
         const int h = hq[i], m = mq[i];
         const bool present = h >= 0;
         const int qpos = p.q_offset + m * 128 + r;
@@ -501,9 +505,14 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
         const uint32_t my_bit = 1u << (2 * i + (r >= 64 ? 1 : 0));
         float sl2 = 0.f, out_scale = 1.f;
         if (present) {
-            sl2 = p.softmax_scale * __ldg(p.q_scale + h * p.qss) * __ldg(p.k_scale + hk * p.kss) * LOG2E;
-            out_scale = __ldg(p.v_scale + hk * p.vss);
+            if constexpr (FP8) {
+                sl2 = p.softmax_scale * __ldg(p.q_scale + h * p.qss) * __ldg(p.k_scale + hk * p.kss) * LOG2E;
+                out_scale = __ldg(p.v_scale + hk * p.vss);
+            } else {
+                sl2 = p.softmax_scale * LOG2E;
+            }
         }
+        const float pbias = FP8 ? LOG2_448 : 0.f;
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = present;
         int t = 0;                                                   // steps this tile took
@@ -519,8 +528,6 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
 #pragma unroll
             for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
             tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(smem_u32(bSfree + i));                        // the issuer may overwrite S now
             // masking: a half this row did not select, keys past the row's position or past kv_len
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
@@ -552,56 +559,66 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                 mx = fmax3(fmax3(a[0], a[1], a[2]), fmaxf(a[3], a[4]), a[15]);
             }
             const float cand = mx * sl2;
-            const bool grow = cand > m_run || m_run == -INFINITY;
+            const bool grow = cand > m_run + C::RESCALE_SLACK || m_run == -INFINITY;
             const float m_new = grow ? fmaxf(m_run, cand) : m_run;
             const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
             const float alpha = ex2_approx(m_run - m_use);
-            const float2 sl2v = make_float2(sl2, sl2), biasv = make_float2(LOG2_448 - m_use, LOG2_448 - m_use);
+            const float2 sl2v = make_float2(sl2, sl2), biasv = make_float2(pbias - m_use, pbias - m_use);
             float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                              make_float2(0.f, 0.f)};
             auto exp_pair = [&](int c) -> float2 {
                 const float2 e = ffma2(make_float2(__uint_as_float(u[c]), __uint_as_float(u[c + 1])), sl2v, biasv);
-                // EXP_POLY pairs in 8 on the FMA pipe (exp2_poly's 7.5e-5 relative error is far below
-                // e4m3's rounding), easing the MUFU unit
-                const bool on_fma = ((c >> 1) & 7) >= 8 - C::EXP_POLY;
+                // FP8: EXP_POLY pairs in 8 on the FMA pipe (exp2_poly's 7.5e-5 relative error is far
+                // below e4m3's rounding), easing the MUFU unit
+                const bool on_fma = FP8 && ((c >> 1) & 7) >= 8 - C::EXP_POLY;
                 const float2 pr = on_fma ? exp2_poly2(e) : make_float2(ex2_approx(e.x), ex2_approx(e.y));
                 acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pr);
                 return pr;
             };
-            // 128 keys -> 32 words of 4 e4m3 values (key 4c+j in byte j of word c)
-            uint32_t pk[32];
+            if constexpr (FP8) {
+                // 128 keys -> 32 columns of 4 e4m3 values (key 4c+j in byte j of column c)
+                uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                const float2 p01 = exp_pair(4 * c);
-                const float2 p23 = exp_pair(4 * c + 2);
-                pk[c] = static_cast<uint32_t>(pack_e4m3x2(p01.x, p01.y)) |
-                        (static_cast<uint32_t>(pack_e4m3x2(p23.x, p23.y)) << 16);
+                for (int c = 0; c < 32; ++c) {
+                    const float2 p01 = exp_pair(4 * c);
+                    const float2 p23 = exp_pair(4 * c + 2);
+                    pk[c] = static_cast<uint32_t>(pack_e4m3x2(p01.x, p01.y)) |
+                            (static_cast<uint32_t>(pack_e4m3x2(p23.x, p23.y)) << 16);
+                }
+                tmem_st32(tS, pk);
+            } else {
+                // 128 keys -> 64 columns of 2 bf16 values (key 2c+j in half j of column c)
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        const float2 pr = exp_pair(64 * hh + 2 * c);
+                        pk[c] = pack_bf16x2(pr.x, pr.y);
+                    }
+                    tmem_st32(tS + 32 * hh, pk);
+                }
             }
             const float2 s01 = fadd2(acc[0], acc[1]), s23 = fadd2(acc[2], acc[3]);
             l_run = l_run * alpha + ((s01.x + s01.y) + (s23.x + s23.y));
             m_run = m_new;
-            if (t > 0) {
-                // the previous O += P V must be complete: it reads the P buffer rewritten below and
-                // accumulates into the O rescaled below
-                ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bPfree + i), (t - 1) & 1, abort_flag, p.status,
-                                                       SA_DEV_WAIT_O));
-                if (!ok) break;
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha < 1.f)) {
+            if (t > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
+                // O rescale in TMEM.  S(t) complete implies the P.V of this tile's previous step is
+                // complete (the issuer issued it before this step's Q.K^T), and this step's P.V waits
+                // for the P barrier below.
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) tmem_ld32(tO + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t o[64];
+                    tmem_ld32(tO + 64 * c, *reinterpret_cast<uint32_t(*)[32]>(o));
+                    tmem_ld32(tO + 64 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 128; ++j) u[j] = __float_as_uint(__uint_as_float(u[j]) * alpha);
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) tmem_st32(tO + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
-                    tmem_wait_st();
+                    for (int j = 0; j < 64; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+                    tmem_st32(tO + 64 * c, *reinterpret_cast<uint32_t(*)[32]>(o));
+                    tmem_st32(tO + 64 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(o + 32));
                 }
             }
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                st_shared_v4(p_row + ((j ^ (r & 7)) << 4), pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-            fence_proxy_async_smem();                                  // P visible to the tensor core
+            tmem_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(bP + i));
             ++t;
@@ -626,13 +643,13 @@ __global__ void __launch_bounds__(384, 1) attn_pair_kernel(const __grid_constant
                 for (int j = 0; j < 32; ++j) o[j] = 0u;
             }
             if (row_ok) {
-                uint32_t pk2[16];
+                uint32_t pk[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
-                    pk2[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
+                    pk[j] = pack_bf16x2(__uint_as_float(o[2 * j]) * inv, __uint_as_float(o[2 * j + 1]) * inv);
                 uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk2[4 * j], pk2[4 * j + 1], pk2[4 * j + 2], pk2[4 * j + 3]);
+                for (int j = 0; j < 4; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
             }
         }
     }

@@ -20,11 +20,12 @@ def attn_schedule(fp8: bool = True):
     """(keys per online-softmax step, paired tiles) of the attention kernel this process launches.
 
     P is rounded (e4m3) against the running row maximum of each step, so numerical models of the
-    kernel follow this granularity.  The paired-tile kernel (FP8) walks two query tiles that share a
-    KV head together: two query heads (h, h ^ 1) of one tile when the GQA group size is even, else
-    tiles (t, t ^ 1) of one head.  SA_ATTN_KERNEL=tile selects the one-tile kernel for FP8 (the
-    library reads the same variable once per process); BF16 always uses the one-tile kernel."""
-    paired = fp8 and os.environ.get('SA_ATTN_KERNEL', '') != 'tile'
+    kernel follow this granularity.  The default one-tile kernel takes 64-key steps.  The paired-tile
+    kernel (FP8, SA_ATTN_KERNEL=pair; the library reads the same variable once per process) walks
+    two query tiles that share a KV head together, 128 keys per step: two query heads (h, h ^ 1) of
+    one tile when the GQA group size is even, else tiles (t, t ^ 1) of one head.  BF16 always uses
+    the one-tile kernel."""
+    paired = fp8 and os.environ.get('SA_ATTN_KERNEL', '') == 'pair'
     return (128 if paired else 64), paired
 
 
