@@ -20,8 +20,12 @@ Decode and short chunks never enter this module's kernels (`try_sparse_forward` 
 from __future__ import annotations
 
 import json
+import math
 import os
+import time
 import weakref
+from pathlib import Path
+from typing import Callable, NamedTuple
 
 import torch
 
@@ -47,13 +51,19 @@ class SparsePrefill:
             raise ValueError(f'fp8_pipeline {fp8_pipeline!r}: expected tma | cpasync')
         self.kernel = _KERNEL_ALIASES[kernel]
         self.fp8_pipeline = fp8_pipeline     # accepted for compatibility: one TMA/tcgen05 kernel serves both
-        self.H, self.Hk, self.D = num_heads, num_kv_heads, head_dim
-        self.g = num_heads // num_kv_heads
-        self.tau, self.min_kv, self.min_q = tau, min_kv, min_q
-        self.scale = head_dim ** -0.5
-        self.wrapper = None
-        self.stats = {'calls': 0, 'blocks_total': 0, 'blocks_kept': 0, 'plan_ms': 0.0, 'run_ms': 0.0, 'select_ms': 0.0}
-        self._kept_acc = None
+        # shape: query heads H, KV heads Hk (GQA group g = H / Hk), head_dim D, softmax scale D^-1/2
+        self.H = num_heads
+        self.Hk = num_kv_heads
+        self.D = head_dim
+        self.g, self.scale = self.H // self.Hk, 1.0 / math.sqrt(head_dim)
+        # selection threshold and the eligibility limits of the hook
+        self.tau = tau
+        self.min_q, self.min_kv = min_q, min_kv
+        self.wrapper = None                  # the retired FlashInfer planner's slot (always None)
+        # counters of the reference's stats dictionary; the *_ms entries grow only with timing=True
+        self.stats = dict.fromkeys(('calls', 'blocks_total', 'blocks_kept'), 0)
+        self.stats.update(dict.fromkeys(('plan_ms', 'run_ms', 'select_ms'), 0.0))
+        self._kept_acc = None                # device tensor: kept blocks summed over calls
         self.timing = False
         # Optional list: when set, every forward appends (start, end) CUDA events recorded on the
         # launching stream around the attention kernel (profiling without host syncs).
@@ -67,7 +77,8 @@ class SparsePrefill:
         return s, e
 
     def eligible(self, q_len: int, kv_len: int) -> bool:
-        return q_len >= self.min_q and kv_len >= self.min_kv
+        """Long enough for the sparse path: at least min_q queries over at least min_kv keys."""
+        return not (q_len < self.min_q or kv_len < self.min_kv)
 
     # -------------------------------------------------------------------------------------------
     # selection
@@ -93,18 +104,16 @@ class SparsePrefill:
 
     @torch.no_grad()
     def block_masks(self, q: torch.Tensor, k, q_start: int, valid=None, union: bool = True, km=None):
-        """q [n, H, D]; k [Hk, N, D] (head-major) or [N, Hk, D] (NHD) with N a multiple of BLOCK;
-        q_start = absolute position of q[0]. Returns bool masks [Hk, MB, NB] (union over the query
-        heads of each KV head) or [H, MB, NB] per query head when union=False.
-        """
+        """Selected blocks of a chunk whose first query sits at absolute position q_start (a multiple of
+        BLOCK; the caller pads q [n, H, D] to whole blocks, `valid` = (first row, row count) of the
+        real queries).  Keys: the cached means km [Hk, NB, D], or k given head-major [Hk, N, D] or
+        NHD [N, Hk, D] (N a multiple of BLOCK).  Returns a bool tensor [Hk, MB, NB] (each KV head's
+        union over its query heads) or, with union=False, [H, MB, NB] (one row per query head)."""
         n = q.shape[0]
-        if km is not None:                                   # cached block means [Hk, NB, D] (fp32)
-            NB = km.shape[1]
-        else:
-            head_major = k.shape[0] == self.Hk and k.shape[1] != self.Hk
-            kn = k.permute(1, 0, 2) if head_major else k     # NHD view
-            NB = kn.shape[0] // BLOCK
-            km = self._km_from_keys(kn, NB)
+        if km is None:                                       # pool the given keys (NHD view of either layout)
+            nhd = k.permute(1, 0, 2) if (k.shape[0] == self.Hk and k.shape[1] != self.Hk) else k
+            km = self._km_from_keys(nhd, nhd.shape[0] // BLOCK)
+        NB = km.shape[1]
         MB = _cdiv(n, BLOCK)
         assert n % BLOCK == 0 and q_start % BLOCK == 0, 'callers pad q to whole blocks'
         if valid is None:
@@ -125,10 +134,10 @@ class SparsePrefill:
     @torch.no_grad()
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_start: int,
                 out: torch.Tensor | None = None) -> torch.Tensor:
-        """q [n, H, D] bf16 at absolute positions q_start..; k, v [kv_len, Hk, D] (NHD)."""
-        if self.kernel == 'sm120':
-            return self.forward_sm120(q, k, v, q_start, out)
-        return self.forward_sm120fp8(q, k, v, q_start, out)
+        """Block-sparse attention of q [n, H, D] (bf16, positions q_start..) over NHD k, v [kv_len, Hk, D]
+        with the kernel this instance was made for."""
+        run = self.forward_sm120fp8 if self.kernel == 'sm120fp8' else self.forward_sm120
+        return run(q, k, v, q_start, out)
 
     def _out(self, out, n, dev):
         if out is not None and out.stride(-1) == 1 and out.stride(0) % 8 == 0 and out.stride(1) % 8 == 0 \
@@ -138,14 +147,13 @@ class SparsePrefill:
 
     @torch.no_grad()
     def forward_sm120(self, q, k, v, q_start, out=None, km=None):
-        """Per-query-head block-sparse attention, BF16 kernel.
-
-        k, v: NHD [T, Hk, D] with T >= q_start + n (rows beyond the sequence are ignored);
-        km: optional cached block means [Hk, ceil((q_start+n)/BLOCK), D] (fp32). No host syncs.
-        """
+        """BF16 kernel, one block list per query head and BLOCK-row query block.  k and v are NHD
+        [T, Hk, D]; rows T > q_start + n are not read.  km: the request's cached fp32 block means
+        [Hk, ceil((q_start + n) / BLOCK), D], else they are pooled here from k.  Makes no host sync."""
         n = q.shape[0]
         kv_len = q_start + n
-        assert k.shape[0] >= kv_len
+        if k.shape[0] < kv_len:
+            raise AssertionError('k holds fewer rows than q_start + n')
         B = BLOCK
         front = q_start % B
         M = _cdiv(front + n, B) * B
@@ -156,7 +164,7 @@ class SparsePrefill:
         if km is None:
             km = self._km_from_keys(k, _cdiv(kv_len, B))
         if FP8_EMULATE:
-            q, k, v = _fp8_round(q, FP8_EMULATE, 'q'), _fp8_round(k, FP8_EMULATE, 'k'), _fp8_round(v, FP8_EMULATE, 'v')
+            q, k, v = (_fp8_round(t, FP8_EMULATE, name) for t, name in ((q, 'q'), (k, 'k'), (v, 'v')))
         NB = km.shape[1]
         qm = self._pool_q(q, q_start, qs, MB)
         counts = torch.empty(self.H * MB, dtype=torch.int32, device=dev)
@@ -172,13 +180,7 @@ class SparsePrefill:
         if ev1 is not None:
             ev1.record()
         self.last_counts, self.last_lists = counts, lists
-        t2 = self._tick()
-        if self.timing:
-            self.stats['select_ms'] += t1 - t0
-            self.stats['run_ms'] += t2 - t1
-        self.stats['calls'] += 1
-        self.stats['blocks_total'] += int(self.H * ((qs // B) * MB + MB * (MB + 1) // 2))
-        self._kept_acc = counts.sum() if self._kept_acc is None else self._kept_acc + counts.sum()
+        self._account(t0, t1, self._tick(), qs // B, MB, counts.sum())
         if out is None:
             return o
         if copy_back:
@@ -187,10 +189,10 @@ class SparsePrefill:
 
     @torch.no_grad()
     def forward_sm120fp8(self, q, k, v, q_start, out=None, km=None, scales=None, kv8=None, k_rows=None):
-        """FP8 (e4m3) path, 128-row query blocks; k, v NHD [T, Hk, D] bf16, quantised here.
+        """FP8 (e4m3) kernel over 128-row query blocks; k, v NHD [T, Hk, D] bf16, quantised here.
 
-        scales: (sq, sk, sv) python floats (per-request, per-layer, cached by the caller); without
-        them per-call amax scales are used (three device syncs).  kv8: optional (k8, v8) uint8
+        scales: the request's (sq, sk, sv) as Python floats (the hook caches them per layer and
+        request); when absent they are taken from this call's amax (three device syncs).  kv8: optional (k8, v8) uint8
         [kv_len, Hk, D] already quantised with these scales (`_cached_kv8`); then k and v are not
         read here and may be None (with km and scales given), k_rows then standing for k.shape[0]
         (the selection covers ceil(k_rows / BLOCK) key blocks, as with the key tensor itself).
@@ -248,130 +250,165 @@ class SparsePrefill:
         if ev1 is not None:
             ev1.record()
         self.last_counts, self.last_lists = counts, lists
-        t2 = self._tick()
-        if self.timing:
-            self.stats['select_ms'] += t1 - t0
-            self.stats['run_ms'] += t2 - t1
-        self.stats['calls'] += 1
-        self.stats['blocks_total'] += int(self.H * ((qs // B) * MB + MB * (MB + 1) // 2))
-        kept = counts.sum() * (BM // B)
-        self._kept_acc = kept if self._kept_acc is None else self._kept_acc + kept
+        self._account(t0, t1, self._tick(), qs // B, MB, counts.sum() * (BM // B))
         if out is None:
             return o
         if copy_back:
             out.copy_(o)
         return out
 
+    def _account(self, t0, t1, t2, qblk0, MB, kept):
+        """Statistics of one call: blocks a dense causal walk would visit (per query head: every block
+        before the chunk for each of its MB query blocks, plus the causal triangle), kept blocks (a
+        device tensor, summed without a sync), and with timing the select / run milliseconds."""
+        if self.timing:
+            self.stats['select_ms'] += t1 - t0
+            self.stats['run_ms'] += t2 - t1
+        self.stats['calls'] += 1
+        self.stats['blocks_total'] += int(self.H * (qblk0 * MB + MB * (MB + 1) // 2))
+        self._kept_acc = kept if self._kept_acc is None else self._kept_acc + kept
+
     def kept_fraction(self):
-        """Blocks kept / causal blocks over all calls so far (one device sync)."""
-        if self._kept_acc is None or not self.stats['blocks_total']:
-            return None
-        return int(self._kept_acc.item()) / self.stats['blocks_total']
+        """Blocks kept / causal blocks over all calls so far (one device sync); None before any call."""
+        total = self.stats['blocks_total']
+        return None if (self._kept_acc is None or total == 0) else int(self._kept_acc.item()) / total
 
     def _tick(self):
-        if not self.timing:
-            return 0.0
-        torch.cuda.synchronize()
-        import time
-        return time.time() * 1000.0
+        """Host milliseconds after a device sync, only with timing=True (0 otherwise)."""
+        if self.timing:
+            torch.cuda.synchronize()
+            return time.perf_counter() * 1e3
+        return 0.0
 
 
 def reference(q, k, v, q_start, masks=None):
-    """fp32 reference: causal attention of q [n,H,D] (positions q_start..) over k,v [Hk,N,D], optional
-    per-KV-head block masks [Hk, MB, NB] (sparse_prefill.py:262-279).  Plain PyTorch: a checker, not a
-    product path."""
+    """fp32 causal attention of q [n, H, D] (positions q_start..) over head-major k, v [Hk, N, D], with
+    optional per-KV-head block masks [Hk, MB, NB]: query row i uses mask row i // BLOCK (counted from
+    q[0]), key j mask column j // BLOCK (the reference's `reference`, sparse_prefill.py:262-279).  Plain
+    PyTorch: a checker, not a product path."""
     n, H, D = q.shape
     Hk, N, _ = k.shape
     g = H // Hk
-    pos_q = q_start + torch.arange(n, device=q.device)
-    pos_k = torch.arange(N, device=q.device)
-    allowed = pos_k[None, :] <= pos_q[:, None]
-    outs = []
-    for h in range(H):
-        s = (q[:, h].float() @ k[h // g].float().T) * D ** -0.5
-        mask = allowed.clone()
+    dev = q.device
+    rows, keys = torch.arange(n, device=dev), torch.arange(N, device=dev)
+    causal = keys[None, :] <= (rows + q_start)[:, None]                 # [n, N]
+    out = torch.empty(n, H, D, dtype=torch.float32, device=dev)
+    for hk in range(Hk):                                                 # one GQA group at a time
+        allowed = causal
         if masks is not None:
-            bm = masks[h // g]
-            mask &= bm.repeat_interleave(BLOCK, 0)[:n].repeat_interleave(BLOCK, 1)[:, :N]
-        s.masked_fill_(~mask, float('-inf'))
-        outs.append(torch.softmax(s, -1) @ v[h // g].float())
-    return torch.stack(outs, 1)
+            allowed = causal & masks[hk][(rows // BLOCK)[:, None], (keys // BLOCK)[None, :]]
+        heads = slice(hk * g, (hk + 1) * g)
+        scores = torch.einsum('ngd,jd->gnj', q[:, heads].float(), k[hk].float()) * D ** -0.5
+        probs = torch.softmax(scores.masked_fill(~allowed, float('-inf')), dim=-1)
+        out[:, heads] = torch.einsum('gnj,jd->ngd', probs, v[hk].float())
+    return out
 
 
-# ---------------------------------------------------------------------------
-# vLLM glue: dynamic block-sparse path for long prefill chunks in the
-# FlashAttention backend. Enabled by SM120_SPARSE_ATTN (default on);
-# SM120_SPARSE_TAU, SM120_SPARSE_MIN_KV, SM120_SPARSE_MIN_Q tune it.
-# ---------------------------------------------------------------------------
+# ===============================================================================================
+# Serving side: knobs, one SparsePrefill per attention shape, per-request caches keyed by
+# (layer, first KV page), and the prefill hook vLLM's FlashAttention backend calls.
+# ===============================================================================================
 _CONFIG = None
 _STATE: dict = {}
-FP8_EMULATE = os.environ.get('SM120_SPARSE_FP8_EMULATE', '')      # '' | 'tensor' | 'token' (experiment switch)
+FP8_EMULATE = os.environ.get('SM120_SPARSE_FP8_EMULATE', '')      # '' | 'tensor' | 'token' (numerics experiment)
 
 
-def _fp8_round(x, mode, which):
-    """Round a [rows, heads, D] bf16 tensor through float8_e4m3fn with amax scaling (sparse_prefill.py:334-348).
-
-    mode 'tensor': one scale per tensor; mode 'token': per (row, head) scales for q/k and per
-    (head, channel) scales for v.  Numerics experiment only.
-    """
-    xf = x.float()
-    if mode == 'tensor':
-        amax = xf.abs().amax().clamp_min(1e-6)
-    elif which == 'v':
-        amax = xf.abs().amax(dim=0, keepdim=True).clamp_min(1e-6)
-    else:
-        amax = xf.abs().amax(dim=2, keepdim=True).clamp_min(1e-6)
-    scale = amax / 448.0
-    return ((xf / scale).to(torch.float8_e4m3fn).float() * scale).to(x.dtype)
+def _flag(value) -> bool:
+    return str(value) not in ('0', 'false', 'False')
 
 
-_DEBUG_LEFT = [int(os.environ.get('SM120_SPARSE_DEBUG', '0'))]
+def _flag_or_empty(value) -> bool:
+    return _flag(value) and str(value) != ''
 
 
-def _debug(msg):
-    if _DEBUG_LEFT[0] > 0:
-        _DEBUG_LEFT[0] -= 1
-        print('[sm120-sparse] ' + msg, flush=True)
+class _Knob(NamedTuple):
+    name: str            # key of config() and of the JSON file
+    env: str             # environment variable; it wins over the file
+    default: object
+    parse: Callable
 
 
-def config():
-    """SM120_SPARSE_* environment variables, with optional defaults from the JSON file named by
-    SM120_SPARSE_CONFIG (sparse_prefill.py:358-381)."""
+# The reference's SM120_SPARSE_* knobs (sparse_prefill.py:358-381) plus the FP8 KV cache switch.
+_KNOBS = (
+    _Knob('enabled', 'SM120_SPARSE_ATTN', 1, _flag),
+    _Knob('tau', 'SM120_SPARSE_TAU', 0.95, float),
+    _Knob('min_kv', 'SM120_SPARSE_MIN_KV', 8192, int),
+    _Knob('min_q', 'SM120_SPARSE_MIN_Q', 1024, int),
+    _Knob('kernel', 'SM120_SPARSE_KERNEL', 'sm120fp8', str),
+    _Knob('fp8_pipeline', 'SM120_SPARSE_FP8_PIPELINE', 'tma', str),
+    _Knob('fp8_kv_cache', 'SM120_SPARSE_FP8_KV_CACHE', 0, _flag_or_empty),   # keep e4m3 K/V per request
+)
+
+
+def config() -> dict:
+    """The knobs, read once: environment variable, else the JSON file named by SM120_SPARSE_CONFIG
+    (for launchers that do not forward the environment), else the default."""
     global _CONFIG
     if _CONFIG is None:
-        file_cfg = {}
         path = os.environ.get('SM120_SPARSE_CONFIG')
-        if path:
-            with open(path) as f:
-                file_cfg = json.load(f)
-
-        def pick(env, key, default, cast):
-            if env in os.environ:
-                return cast(os.environ[env])
-            return cast(file_cfg.get(key, default))
-        _CONFIG = {
-            'enabled': pick('SM120_SPARSE_ATTN', 'enabled', 1, lambda v: str(v) not in ('0', 'false', 'False')),
-            'tau': pick('SM120_SPARSE_TAU', 'tau', 0.95, float),
-            'min_kv': pick('SM120_SPARSE_MIN_KV', 'min_kv', 8192, int),
-            'min_q': pick('SM120_SPARSE_MIN_Q', 'min_q', 1024, int),
-            'kernel': pick('SM120_SPARSE_KERNEL', 'kernel', 'sm120fp8', str),
-            'fp8_pipeline': pick('SM120_SPARSE_FP8_PIPELINE', 'fp8_pipeline', 'tma', str),
-            # new: keep e4m3 K/V per (layer, request) and quantise each chunk's rows once
-            'fp8_kv_cache': pick('SM120_SPARSE_FP8_KV_CACHE', 'fp8_kv_cache', 0,
-                                 lambda v: str(v) not in ('0', 'false', 'False', '')),
-        }
-        print('[sm120-sparse] config %r' % (_CONFIG,), flush=True)
+        from_file = json.loads(Path(path).read_text()) if path else {}
+        _CONFIG = {kn.name: kn.parse(os.environ[kn.env] if kn.env in os.environ else from_file.get(kn.name, kn.default))
+                   for kn in _KNOBS}
+        print(f'[sm120-sparse] config {_CONFIG!r}', flush=True)
     return _CONFIG
 
 
 def _state(num_heads, num_kv_heads, head_dim, device):
-    key = (num_heads, num_kv_heads, head_dim, str(device))
-    if key not in _STATE:
-        cfg = config()
-        _STATE[key] = SparsePrefill(num_heads, num_kv_heads, head_dim, device, tau=cfg['tau'],
-                                    min_kv=cfg['min_kv'], min_q=cfg['min_q'], kernel=cfg['kernel'],
-                                    fp8_pipeline=cfg['fp8_pipeline'])
-    return _STATE[key]
+    """The SparsePrefill serving one (heads, KV heads, head_dim, device) shape, built on first use with
+    the knobs of config()."""
+    shape = (num_heads, num_kv_heads, head_dim, str(device))
+    sp = _STATE.get(shape)
+    if sp is None:
+        knobs = config()
+        sp = _STATE[shape] = SparsePrefill(num_heads, num_kv_heads, head_dim, device,
+                                           **{k: knobs[k] for k in ('tau', 'min_kv', 'min_q', 'kernel', 'fp8_pipeline')})
+    return sp
+
+
+# amax axes of the SM120_SPARSE_FP8_EMULATE rounding: one scale per tensor, or per (row, head) for
+# q and k and per (head, channel) for v
+_EMULATE_AXES = {'tensor': dict(q=None, k=None, v=None), 'token': dict(q=(2,), k=(2,), v=(0,))}
+
+
+def _fp8_round(x, mode, which):
+    """x [rows, heads, D] through float8_e4m3fn and back with amax/448 scaling (the reference's
+    FP8-emulation experiment, sparse_prefill.py:334-348); `which` is 'q', 'k' or 'v'."""
+    xf = x.float()
+    axes = _EMULATE_AXES['tensor' if mode == 'tensor' else 'token'][which]
+    magnitude = xf.abs()
+    peak = magnitude.amax() if axes is None else magnitude.amax(dim=axes, keepdim=True)
+    step = peak.clamp_min(1e-6) / 448.0
+    return (xf / step).to(torch.float8_e4m3fn).to(torch.float32).mul_(step).to(x.dtype)
+
+
+class _DebugLines:
+    """Prints at most `budget` lines prefixed '[sm120-sparse]' (SM120_SPARSE_DEBUG=N)."""
+
+    def __init__(self, budget: int):
+        self.budget = budget
+
+    def __call__(self, msg: str) -> None:
+        if self.budget > 0:
+            self.budget -= 1
+            print(f'[sm120-sparse] {msg}', flush=True)
+
+
+_debug = _DebugLines(int(os.environ.get('SM120_SPARSE_DEBUG', '0')))
+
+
+def _request_entry(cache: dict, key, q_start: int, continues, make):
+    """Per-request cache discipline shared by the block-mean, scale and FP8 KV caches: the entry of
+    (layer, first page) is reused when `continues(entry)` says the request's previous chunk ended at
+    q_start (a recycled first page of another request never does), else a fresh one from `make()`
+    replaces it, the oldest entry of the cache being dropped when it holds _KMEAN_MAX_ENTRIES.
+    Returns (entry, fresh)."""
+    entry = cache.get(key)
+    if entry is not None and q_start > 0 and continues(entry):
+        return entry, False
+    if len(cache) >= _KMEAN_MAX_ENTRIES:
+        del cache[next(iter(cache))]
+    entry = cache[key] = make()
+    return entry, True
 
 
 _KMEAN_CACHE: dict = {}
@@ -379,48 +416,43 @@ _KMEAN_MAX_ENTRIES = 128
 
 
 def _cached_block_means(layer_key, first_page, key_chunk, q_start, kv_len, key_all=None):
-    """Maintain per-(layer, request) K block means [Hk, NB, D] (fp32), updated from the chunk's keys
-    (sparse_prefill.py:398-447).
+    """fp32 block means [Hk, NB, D] of a request's keys, NB = ceil((q_start + n) / BLOCK), kept per
+    (layer, request) and extended by each chunk (sparse_prefill.py:398-447).
 
-    A request is identified by its first physical page. An entry is only trusted when it was built
-    contiguously by this request (its last chunk ended exactly at q_start); otherwise it is rebuilt
-    from the full key history `key_all` [kv_len, Hk, D].  Chunk boundaries unaligned to BLOCK make
-    the boundary block's mean use only the rows of the current chunk.
+    key_chunk [n, Hk, D] holds the keys at positions q_start..; the entry grows by the chunk's blocks.
+    A request whose cached entry does not end at q_start (new request, recycled first page, skipped
+    chunks) is rebuilt from key_all [>= q_start, Hk, D], its history.  As in the reference, a chunk
+    that starts inside a block replaces that block's mean by the mean of its own rows there; only a
+    rebuild averages the block's history rows and chunk rows together.
     """
     B = BLOCK
     n, Hk, D = key_chunk.shape
-    cache_key = (layer_key, first_page)
-    entry = _KMEAN_CACHE.get(cache_key)
-    b0, b1 = q_start // B, -(-(q_start + n) // B)
-    if entry is None or q_start == 0 or entry['nb'] < b0 or entry.get('last_kv') != q_start:
-        if len(_KMEAN_CACHE) >= _KMEAN_MAX_ENTRIES:
-            _KMEAN_CACHE.pop(next(iter(_KMEAN_CACHE)))
-        cap = max(4096, b1)
-        entry = {'km': torch.zeros(Hk, cap, D, dtype=torch.float32, device=key_chunk.device), 'nb': 0, 'last_kv': 0}
-        _KMEAN_CACHE[cache_key] = entry
-        if q_start > 0:
-            if key_all is None:
-                raise RuntimeError('stale block-mean cache entry and no key history to rebuild it')
-            hist = key_all[:q_start]
-            full, rem = q_start // B, q_start % B
-            if full:
-                ops.block_means(hist[:full * B], 0, B, entry['km'], 0)
-            if rem:   # partial block: completed below from `front` rows of the chunk
-                ops.block_means(hist[full * B:], full * B, B, entry['km'], 0)
-            entry['nb'] = full + (1 if rem else 0)
-            if rem:
-                key_chunk = torch.cat([hist[full * B:], key_chunk], 0)
-                q_start, n = full * B, n + rem
-                b0 = full
-    if entry['km'].shape[1] < b1:
-        grown = torch.zeros(Hk, max(b1, 2 * entry['km'].shape[1]), D, dtype=torch.float32, device=key_chunk.device)
-        grown[:, :entry['km'].shape[1]] = entry['km']
+    end_block = -(-(q_start + n) // B)
+    dev = key_chunk.device
+
+    def fresh():
+        return {'km': torch.zeros(Hk, max(4096, end_block), D, dtype=torch.float32, device=dev), 'nb': 0,
+                'last_kv': 0}
+    entry, rebuilt = _request_entry(_KMEAN_CACHE, (layer_key, first_page), q_start,
+                                    lambda e: e['nb'] >= q_start // B and e.get('last_kv') == q_start, fresh)
+    rows, pos0 = key_chunk, q_start                  # rows whose block means are (re)computed below
+    if rebuilt and q_start > 0:
+        if key_all is None:
+            raise RuntimeError('stale block-mean cache entry and no key history to rebuild it')
+        whole = q_start - q_start % B                # history rows that fill complete blocks
+        if whole:
+            ops.block_means(key_all[:whole], 0, B, entry['km'], 0)
+        if whole < q_start:                          # the block the chunk continues: history + chunk rows
+            rows, pos0 = torch.cat([key_all[whole:q_start], key_chunk], 0), whole
+    held = entry['km'].shape[1]
+    if held < end_block:                             # capacity doubles (at least to end_block)
+        grown = entry['km'].new_zeros(Hk, max(end_block, 2 * held), D)
+        grown[:, :held] = entry['km']
         entry['km'] = grown
-    if n:
-        ops.block_means(key_chunk, q_start, B, entry['km'], 0)
-    entry['nb'] = b1
-    entry['last_kv'] = kv_len
-    return entry['km'][:, :b1]
+    if rows.shape[0]:
+        ops.block_means(rows, pos0, B, entry['km'], 0)
+    entry['nb'], entry['last_kv'] = end_block, kv_len
+    return entry['km'][:, :end_block]
 
 
 _SCALE_TENSORS: dict = {}
@@ -478,19 +510,21 @@ def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
     """
     sk, sv = float(scales[1]), float(scales[2])
     key = (layer_key, first_page)
-    entry = _KV8_CACHE.get(key)
     Hk, D = k.shape[1], k.shape[2]
     dev = k.device
-    if entry is None or q_start == 0 or entry['rows'] != q_start or entry['scales'] != (sk, sv):
-        if k_row0:
-            raise RuntimeError('stale FP8 KV cache entry and no key/value rows before %d to rebuild it' % k_row0)
-        if len(_KV8_CACHE) >= _KMEAN_MAX_ENTRIES:
-            _KV8_CACHE.pop(next(iter(_KV8_CACHE)))
-        cap = max(kv_len, 8192)
-        entry = {'k8': torch.empty(cap, Hk, D, dtype=torch.uint8, device=dev),
-                 'v8': torch.empty(cap, Hk, D, dtype=torch.uint8, device=dev), 'rows': 0, 'scales': (sk, sv),
-                 'inv': _scale_tensor(dev, scales[0], sk, sv)[1:3]}
-        _KV8_CACHE[key] = entry
+
+    def continues(e):
+        return e['rows'] == q_start and e['scales'] == (sk, sv)
+    prior = _KV8_CACHE.get(key)
+    if k_row0 and not (prior is not None and q_start > 0 and continues(prior)):
+        raise RuntimeError('stale FP8 KV cache entry and no key/value rows before %d to rebuild it' % k_row0)
+
+    def fresh():
+        rows = max(kv_len, 8192)
+        return {'k8': torch.empty(rows, Hk, D, dtype=torch.uint8, device=dev),
+                'v8': torch.empty(rows, Hk, D, dtype=torch.uint8, device=dev), 'rows': 0, 'scales': (sk, sv),
+                'inv': _scale_tensor(dev, scales[0], sk, sv)[1:3]}
+    entry, _ = _request_entry(_KV8_CACHE, key, q_start, continues, fresh)
     lo = entry['rows']
     if entry['k8'].shape[0] < kv_len:
         cap = max(kv_len, 2 * entry['k8'].shape[0])
@@ -523,17 +557,15 @@ SCALE_MARGIN = 1.5
 
 
 def _cached_scales(layer_key, first_page, q, k, v, q_start):
-    """Per-(layer, request) e4m3 scales (amax/448 x margin) from the request's first sparse chunk
-    (sparse_prefill.py:450-469); one host sync when an entry is (re)built."""
-    key = (layer_key, first_page)
-    entry = _SCALE_CACHE.get(key)
-    if q_start == 0 or entry is None or entry['last_kv'] != q_start:
-        if len(_SCALE_CACHE) >= _KMEAN_MAX_ENTRIES:
-            _SCALE_CACHE.pop(next(iter(_SCALE_CACHE)))
-        amax = torch.cat([ops.absmax(t if t.stride(-1) == 1 else t.contiguous(), per_head=False)
-                          for t in (q, k, v)]).clamp_min(1e-6).tolist()
-        entry = {'scales': tuple(a * SCALE_MARGIN / 448.0 for a in amax), 'last_kv': 0}
-        _SCALE_CACHE[key] = entry
+    """e4m3 scales (sq, sk, sv) of a request, fixed at its first sparse chunk: amax of that chunk's q and
+    of k, v (the history so far) / 448, times SCALE_MARGIN for the rows still to come
+    (sparse_prefill.py:450-469).  One host sync when an entry is made."""
+    def fresh():
+        peaks = torch.cat([ops.absmax(t if t.stride(-1) == 1 else t.contiguous(), per_head=False)
+                           for t in (q, k, v)]).clamp_min(1e-6).tolist()
+        return {'scales': tuple(a * SCALE_MARGIN / 448.0 for a in peaks), 'last_kv': 0}
+    entry, _ = _request_entry(_SCALE_CACHE, (layer_key, first_page), q_start,
+                              lambda e: e['last_kv'] == q_start, fresh)
     entry['last_kv'] = q_start + q.shape[0]
     return entry['scales']
 
@@ -563,89 +595,108 @@ def _host_metadata(attn_metadata):
     return vals
 
 
-@torch.no_grad()
-def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_metadata) -> bool:
-    """Block-sparse attention for the long prefill chunks of this batch; other requests in the
-    same batch (short chunks, decode steps) get a per-request dense FlashAttention call
-    (sparse_prefill.py:472-535).
-
-    query/key/output: this batch's [num_actual_tokens, ...] tensors; key_cache/value_cache:
-    [num_blocks, page, Hk, D]. Returns False (nothing written) when no request qualifies.
-    """
-    cfg = config()
+def _hook_applies(impl, attn_metadata, cfg) -> bool:
+    """Checks that need no device read: the knob is on, the layer is causal full attention, the batch
+    holds a chunk long enough somewhere, and no CUDA graph is being captured (decode batches are
+    captured; reading the metadata there would be a device-to-host copy during capture)."""
     if not cfg['enabled']:
         return False
     window = getattr(impl, 'sliding_window', None)
-    windowed = window is not None and any(int(w) >= 0 for w in window)   # full attention is (-1, -1)
-    if attn_metadata.causal is not True or windowed:
-        _debug('fallback: causal=%r window=%r' % (attn_metadata.causal, window))
+    if attn_metadata.causal is not True or (window is not None and any(int(w) >= 0 for w in window)):
+        _debug(f'not causal full attention (causal={attn_metadata.causal!r}, window={window!r}): dense path')
         return False
-    # Host-side checks first: no device-to-host copies during CUDA graph capture and no sync for
-    # batches that cannot qualify.
-    if attn_metadata.max_query_len < cfg['min_q'] or attn_metadata.max_seq_len < cfg['min_kv']:
+    long_enough = attn_metadata.max_query_len >= cfg['min_q'] and attn_metadata.max_seq_len >= cfg['min_kv']
+    return long_enough and not torch.cuda.is_current_stream_capturing()
+
+
+class _Request(NamedTuple):
+    index: int           # row of the block table
+    q0: int              # its rows in this batch's query / key / output tensors
+    q1: int
+    kv_len: int          # keys of the request after this chunk
+    first_page: int      # identifies the request in the per-request caches
+
+    @property
+    def n(self) -> int:
+        return self.q1 - self.q0
+
+    @property
+    def q_start(self) -> int:
+        return self.kv_len - self.n
+
+
+@torch.no_grad()
+def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_metadata) -> bool:
+    """Prefill hook of vLLM's FlashAttention backend (sparse_prefill.py:472-535): writes the attention
+    output of every request of the batch and returns True when at least one request has a chunk of
+    >= min_q queries over >= min_kv keys; those run block-sparse, the others (short chunks, decode
+    steps) get the backend's dense paged call.  Returns False, writing nothing, otherwise.
+
+    query, key, output are the batch's token-major tensors (num_actual_tokens rows); the paged caches
+    key_cache and value_cache are [num_blocks, page, Hk, D].
+    """
+    cfg = config()
+    if not _hook_applies(impl, attn_metadata, cfg):
         return False
-    if torch.cuda.is_current_stream_capturing():
+    starts, seq_lens, first_pages = _host_metadata(attn_metadata)
+    requests = [_Request(r, starts[r], starts[r + 1], seq_lens[r], first_pages[r]) for r in range(len(seq_lens))]
+    sparse = [rq.n >= cfg['min_q'] and rq.kv_len >= cfg['min_kv'] for rq in requests]
+    if not any(sparse):
         return False
-    qsl, seq_lens, first_pages = _host_metadata(attn_metadata)
-    nreq = len(seq_lens)
-    eligible = [r for r in range(nreq) if qsl[r + 1] - qsl[r] >= cfg['min_q'] and seq_lens[r] >= cfg['min_kv']]
-    if not eligible:
-        return False
-    _debug('sparse path: %d/%d requests, q_lens=%s kv_lens=%s' % (
-        len(eligible), nreq, [qsl[i + 1] - qsl[i] for i in range(nreq)], seq_lens))
-    H, D = query.shape[1], query.shape[2]
-    Hk = key_cache.shape[2]
-    sp = _state(H, Hk, D, query.device)
-    page = key_cache.shape[1]
-    bt = attn_metadata.block_table
-    for r in range(nreq):
-        kv_len = seq_lens[r]
-        n = qsl[r + 1] - qsl[r]
-        q_r = query[qsl[r]:qsl[r + 1]]
-        o_r = output[qsl[r]:qsl[r + 1]]
-        if r not in eligible:
-            _dense_request(impl, q_r, key_cache, value_cache, o_r, bt[r], n, kv_len)
-            continue
-        npages = -(-kv_len // page)
-        q_start = kv_len - n
-        if sp.kernel == 'sm120fp8' and cfg['fp8_kv_cache'] and _fp8_warm(id(impl), first_pages[r], q_start):
-            # Block means, scales and the e4m3 history are cached: only this chunk's pages are read
-            # (the reference gathers the whole history every chunk, sparse_prefill.py:521-522).
-            p0 = q_start // page
-            pages = bt[r, p0:npages].long()
-            kc = key_cache[pages].reshape(-1, Hk, D)
-            vc = value_cache[pages].reshape(-1, Hk, D)
-            km = _cached_block_means(id(impl), first_pages[r], key[qsl[r]:qsl[r + 1]], q_start, kv_len)
-            scales = _cached_scales(id(impl), first_pages[r], q_r, None, None, q_start)
-            kv8 = _cached_kv8(id(impl), first_pages[r], kc, vc, q_start, kv_len, scales, k_row0=p0 * page)
-            sp.forward_sm120fp8(q_r, None, None, q_start, out=o_r, km=km, scales=scales, kv8=kv8,
-                                k_rows=npages * page)
-            continue
-        pages = bt[r, :npages].long()
-        k = key_cache[pages].reshape(npages * page, Hk, D)    # one gather copy, NHD
-        v = value_cache[pages].reshape(npages * page, Hk, D)
-        km = _cached_block_means(id(impl), first_pages[r], key[qsl[r]:qsl[r + 1]], kv_len - n, kv_len, key_all=k)
-        if sp.kernel == 'sm120fp8':
-            scales = _cached_scales(id(impl), first_pages[r], q_r, k[:kv_len], v[:kv_len], kv_len - n)
-            kv8 = (_cached_kv8(id(impl), first_pages[r], k, v, kv_len - n, kv_len, scales)
-                   if cfg['fp8_kv_cache'] else None)
-            sp.forward_sm120fp8(q_r, k, v, kv_len - n, out=o_r, km=km, scales=scales, kv8=kv8)
+    _debug(f'{sum(sparse)} of {len(requests)} requests block-sparse; chunk lengths '
+           f'{[rq.n for rq in requests]}, key lengths {[rq.kv_len for rq in requests]}')
+    sp = _state(query.shape[1], key_cache.shape[2], query.shape[2], query.device)
+    table = attn_metadata.block_table
+    for rq, is_sparse in zip(requests, sparse):
+        q_r, o_r = query[rq.q0:rq.q1], output[rq.q0:rq.q1]
+        if is_sparse:
+            _sparse_request(sp, cfg, id(impl), rq, q_r, key[rq.q0:rq.q1], key_cache, value_cache, o_r,
+                            table[rq.index])
         else:
-            sp.forward_sm120(q_r, k, v, kv_len - n, out=o_r, km=km)
+            _dense_request(impl, q_r, key_cache, value_cache, o_r, table[rq.index], rq.n, rq.kv_len)
     return True
 
 
+def _sparse_request(sp, cfg, layer, rq, q_r, key_r, key_cache, value_cache, o_r, pages_row):
+    """One long prefill chunk through the block-sparse path.  The caches of (layer, first page) carry
+    the request's block means, e4m3 scales and (with fp8_kv_cache) e4m3 K/V from chunk to chunk."""
+    page, Hk, D = key_cache.shape[1], key_cache.shape[2], key_cache.shape[3]
+    npages = -(-rq.kv_len // page)
+    q_start = rq.q_start
+    fp8 = sp.kernel == 'sm120fp8'
+    if fp8 and cfg['fp8_kv_cache'] and _fp8_warm(layer, rq.first_page, q_start):
+        # block means, scales and the e4m3 history all continue at this chunk: read only the pages
+        # the chunk wrote (the reference gathers the whole history every chunk, sparse_prefill.py:521)
+        p0 = q_start // page
+        own = pages_row[p0:npages].long()
+        k_new, v_new = key_cache[own].reshape(-1, Hk, D), value_cache[own].reshape(-1, Hk, D)
+        km = _cached_block_means(layer, rq.first_page, key_r, q_start, rq.kv_len)
+        scales = _cached_scales(layer, rq.first_page, q_r, None, None, q_start)
+        kv8 = _cached_kv8(layer, rq.first_page, k_new, v_new, q_start, rq.kv_len, scales, k_row0=p0 * page)
+        sp.forward_sm120fp8(q_r, None, None, q_start, out=o_r, km=km, scales=scales, kv8=kv8, k_rows=npages * page)
+        return
+    pages = pages_row[:npages].long()
+    k_all = key_cache[pages].reshape(npages * page, Hk, D)      # the request's keys and values, NHD
+    v_all = value_cache[pages].reshape(npages * page, Hk, D)
+    km = _cached_block_means(layer, rq.first_page, key_r, q_start, rq.kv_len, key_all=k_all)
+    if not fp8:
+        sp.forward_sm120(q_r, k_all, v_all, q_start, out=o_r, km=km)
+        return
+    scales = _cached_scales(layer, rq.first_page, q_r, k_all[:rq.kv_len], v_all[:rq.kv_len], q_start)
+    kv8 = _cached_kv8(layer, rq.first_page, k_all, v_all, q_start, rq.kv_len, scales) if cfg['fp8_kv_cache'] else None
+    sp.forward_sm120fp8(q_r, k_all, v_all, q_start, out=o_r, km=km, scales=scales, kv8=kv8)
+
+
 def _dense_request(impl, query, key_cache, value_cache, output, bt_row, n, kv_len):
-    """Dense paged FlashAttention for one request of a mixed batch: the backend's own call
-    (sparse_prefill.py:538-550)."""
+    """Dense paged attention for one request of a mixed batch through the call the backend itself makes
+    (vLLM's flash_attn_varlen_func; sparse_prefill.py:538-550)."""
     from vllm.vllm_flash_attn import flash_attn_varlen_func
     dev = query.device
-    cu = torch.tensor([0, n], dtype=torch.int32, device=dev)
-    su = torch.tensor([kv_len], dtype=torch.int32, device=dev)
     window = getattr(impl, 'sliding_window', None)
-    flash_attn_varlen_func(q=query, k=key_cache, v=value_cache, out=output, cu_seqlens_q=cu, max_seqlen_q=n,
-                           seqused_k=su, max_seqlen_k=kv_len, softmax_scale=impl.scale, causal=True,
-                           alibi_slopes=getattr(impl, 'alibi_slopes', None),
-                           window_size=list(window) if window is not None else None,
-                           block_table=bt_row.unsqueeze(0), softcap=getattr(impl, 'logits_soft_cap', 0.0),
-                           fa_version=getattr(impl, 'vllm_flash_attn_version', 2))
+    args = dict(q=query, k=key_cache, v=value_cache, out=output,
+                cu_seqlens_q=torch.tensor([0, n], dtype=torch.int32, device=dev), max_seqlen_q=n,
+                seqused_k=torch.tensor([kv_len], dtype=torch.int32, device=dev), max_seqlen_k=kv_len,
+                softmax_scale=impl.scale, causal=True, alibi_slopes=getattr(impl, 'alibi_slopes', None),
+                window_size=list(window) if window is not None else None, block_table=bt_row.unsqueeze(0),
+                softcap=getattr(impl, 'logits_soft_cap', 0.0), fa_version=getattr(impl, 'vllm_flash_attn_version', 2))
+    flash_attn_varlen_func(**args)
