@@ -50,9 +50,9 @@ METRIC = 'sparse prefill attention TFLOPS (exec blocks) + prefill TTFT @64K/128K
 H_FULL, HK_FULL, D = 64, 8, 128
 N_Q, KV, BLOCK, TAU = 8192, 65536, 128, 0.95
 Q_START = KV - N_Q
-# Kernels of this package launched per step: K-chunk block means, Q block means + e4m3, scores,
-# selection, K e4m3, V e4m3, attention.
-LAUNCHES_PER_STEP = 7
+# Kernels of this package launched per step: K-chunk block means, the one-pass query selection (with
+# the fused e4m3 copy of q), K e4m3, V e4m3, attention.
+LAUNCHES_PER_STEP = 5
 ATTN_KERNEL = 'attn_fwd_kernel<fp8>'
 # DRAM bytes (read + write) per attention launch measured by one ncu capture
 # (`dram__bytes_read.sum + dram__bytes_write.sum` of the attention kernel in
@@ -558,19 +558,19 @@ def _selection(args, h, hk, dev, rank):
 
     def step(qq=q, kk=kc):
         km = ksp._cached_block_means(layer, 0, kk, Q_START, KV)
-        qm = sp._pool_q(qq, Q_START, Q_START, MB)
-        ops.select(qm, km, h, hk, NB, Q_START // BLOCK, sp.scale, TAU, SA_SELECT_PER_HEAD, counts=counts, lists=lists)
+        sp._select(qq, Q_START, Q_START // BLOCK, MB, km, NB, SA_SELECT_PER_HEAD, counts=counts, lists=lists)
     for _ in range(args.warmup):
         rewind()
         step()
     ms = _timed(step, args.steps, dev, int(os.environ.get('WORLD_SIZE', '1')), before=rewind)
     nnz = int(counts.sum().item())
     nbytes = 2 * N_Q * h * D + 2 * N_Q * hk * D + 4 * hk * NB * D + 4 * hk * MB * D + 4 * h * MB + 4 * nnz
-    qm = sp._pool_q(q, Q_START, Q_START, MB)
     km = ksp._KMEAN_CACHE[(layer, 0)]['km'][:, :NB]
-    sel_ms = _kernel_ms(lambda: ops.select(qm, km, h, hk, NB, Q_START // BLOCK, sp.scale, TAU, SA_SELECT_PER_HEAD,
-                                           counts=counts, lists=lists), dev)
-    sel_bytes = 4 * h * MB * D + 4 * hk * NB * D + 4 * h * MB + 4 * nnz
+    fused = ops.select_q_supported(h, hk, D, NB, SA_SELECT_PER_HEAD)
+    sel_ms = _kernel_ms(lambda: sp._select(q, Q_START, Q_START // BLOCK, MB, km, NB, SA_SELECT_PER_HEAD, counts=counts,
+                                           lists=lists), dev)
+    # the one-pass kernel reads the query chunk and the key means and writes the CSR lists
+    sel_bytes = 2 * N_Q * h * D + 4 * hk * NB * D + 4 * h * MB + 4 * nnz
     q_h, k_h = q.cpu().pin_memory(), kc.cpu().pin_memory()
     c_h = torch.empty(counts.shape, dtype=counts.dtype).pin_memory()
     l_h = torch.empty(lists.shape, dtype=lists.dtype).pin_memory()
@@ -587,14 +587,16 @@ def _selection(args, h, hk, dev, rank):
     e2e_ms = _timed(e2e, args.steps, dev, int(os.environ.get('WORLD_SIZE', '1')), before=rewind)
     ops.check_status(dev)
     return {'ms': ms, 'e2e_ms': e2e_ms, 'work': nbytes, 'unit': 'GB/s', 'scale': 1e9,
-            'kernel': 'select_kernel', 'kernel_ms': sel_ms, 'kernel_work': sel_bytes, 'bound': 'hbm',
-            'h2d': q_h.numel() * 2 + k_h.numel() * 2, 'd2h': c_h.numel() * 4 + l_h.numel() * 4, 'launches': 3,
+            'kernel': 'select_fused_kernel' if fused else 'block_means_kernel + score_kernel + select_kernel',
+            'kernel_ms': sel_ms, 'kernel_work': sel_bytes, 'bound': 'hbm',
+            'h2d': q_h.numel() * 2 + k_h.numel() * 2, 'd2h': c_h.numel() * 4 + l_h.numel() * 4,
+            'launches': 2 if fused else 3,
             'config': {'workload': f'selection path (configs[1] shape): K-chunk means into the cache, Q pooling, '
                                    f'per-head selection to CSR; q {N_Q} @ {Q_START} vs {KV} keys, H {h}/Hk {hk}/D {D}, '
                                    f'block {BLOCK}, tau {TAU}, {args.strength} injection',
                        'bytes_per_step': nbytes, 'nnz': nnz,
                        'note': 'value = algorithmic bytes (q + k chunk read, km read/append, CSR write) / time; '
-                               'roofline on select_kernel alone (qm, km, CSR bytes)'}}
+                               'roofline on the query-side selection launch alone (q, km read, CSR write)'}}
 
 
 def _chunked(args, h, hk, dev, rank):

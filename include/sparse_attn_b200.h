@@ -107,6 +107,29 @@ SA_API int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_head_s
 SA_API size_t sa_select_workspace_bytes(int num_heads, int MB, int nb_total);
 
 /*
+ * (a)+(b) in one pass: block selection straight from the query rows.  Replaces the query pooling
+ * and scoring of sm120_attn/sparse_prefill.py:58-84 (`block_masks`) like sa_block_means_bf16 +
+ * sa_select, without the pooled-query tensor or the logits workspace: one CTA per (query block, or
+ * pair of query blocks for SA_SELECT_PAIR_UNION; KV head) pools its rows, scores them against km
+ * in shared memory and selects.
+ * q: bf16 [n, num_heads, head_dim] at absolute positions q_start .. q_start+n-1, which must lie in
+ * the query blocks qblk0 .. qblk0+MB-1 of `block` rows; each block's mean is taken over the rows
+ * of q it holds (0 for a block without rows).  km, nb_km, nb_total, scale, tau, mode, counts,
+ * lists, list_stride, masks: as sa_select (query block m is block qblk0 + m).  q8 (optional):
+ * e4m3 copy of every query row as in sa_block_means_bf16 (inv_scale per head or scalar).
+ * Returns SA_ERR_UNSUPPORTED, launching nothing, for shapes outside the kernel's limits (head_dim
+ * 128; at most 16 query heads per KV head; rows of at most 1024 key blocks; query blocks per unit
+ * x query heads per KV head x nb_total rounded up to 32 at most 16384); use sa_block_means_bf16 +
+ * sa_select there.
+ */
+SA_API int sa_select_q(const void* q, int64_t q_row_stride, int64_t q_head_stride, int n, int q_start, int block,
+              int qblk0, int MB, const float* km, int64_t km_head_stride, int64_t km_block_stride, int nb_km,
+              int num_heads, int num_kv_heads, int head_dim, int nb_total, float scale, float tau, int mode,
+              int32_t* counts, int32_t* lists, int64_t list_stride, uint8_t* masks, uint8_t* q8,
+              int64_t q8_row_stride, int64_t q8_head_stride, const float* inv_scale, int inv_scale_stride,
+              void* stream);
+
+/*
  * sa_select without a workspace argument: the same selection, with its scratch taken from a
  * 40 MiB (41943040-byte) buffer that is compiled into the library, one per device.  It has no
  * counterpart in the reference, whose selection allocates through PyTorch.  It is meant for

@@ -66,8 +66,10 @@ struct Cfg {
 };
 
 
+// exponential pairs in eight computed on the FMA pipe (FP8).  1 measured fastest on the power-capped
+// benchmark chunk (11.52 ms vs 11.69 / 11.70 ms for 2 / 3 on one box); short runs favour 3.
 #ifndef SA_TILE_EXP_POLY
-#define SA_TILE_EXP_POLY 3           // exponential pairs in eight on the FMA pipe (FP8)
+#define SA_TILE_EXP_POLY 1
 #endif
 constexpr int TILE_EXP_POLY = SA_TILE_EXP_POLY;
 

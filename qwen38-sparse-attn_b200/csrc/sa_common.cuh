@@ -153,6 +153,44 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
                        __int_as_float(__float_as_int(p.y) + __float_as_int(y.y) * 8388608));
 }
 
+// ------------------------------------------------------------------------------------------
+// Streaming bf16 rows and their e4m3 quantisation (prep.cu, select.cu)
+// ------------------------------------------------------------------------------------------
+// 16-byte load that bypasses L1 (each row is read once).
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// eight bf16 values -> fp32
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+}
+
+// value before the e4m3 cast under a quantisation mode (SA_QUANT_*)
+__device__ __forceinline__ float scale_value(float x, float s, int mode) {
+    if (mode == SA_QUANT_DIV) return __fdiv_rn(x, s);
+    const float t = x * s;
+    return mode == SA_QUANT_MUL_BF16 ? bf16_round(t) : t;
+}
+
+__device__ __forceinline__ uint2 quant8(const float (&f)[8], float s, int mode) {
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = scale_value(f[i], s, mode);
+    uint2 r;
+    r.x = static_cast<uint32_t>(pack_e4m3x2(y[0], y[1])) | (static_cast<uint32_t>(pack_e4m3x2(y[2], y[3])) << 16);
+    r.y = static_cast<uint32_t>(pack_e4m3x2(y[4], y[5])) | (static_cast<uint32_t>(pack_e4m3x2(y[6], y[7])) << 16);
+    return r;
+}
+
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

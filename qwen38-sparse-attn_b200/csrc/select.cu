@@ -182,14 +182,15 @@ __device__ __forceinline__ int ties_needed(double above, float vstar, int ties, 
 
 // Register path: selects within one row of nbc <= 32*NPL blocks; returns the kept flags of this
 // lane's blocks (bit c <-> block lane + 32c).
-template <int NPL>
+// L is a global workspace row (read through the read-only cache) or, with SMEM, a shared-memory row.
+template <int NPL, bool SMEM = false>
 __device__ uint64_t select_row_regs(const float* __restrict__ L, int nbc, float tau_f, int lane) {
     constexpr bool PRE = NPL <= 16;                               // keep float64 copies in registers
     float p[NPL];
 #pragma unroll
     for (int c = 0; c < NPL; ++c) {
         const int j = lane + 32 * c;
-        p[c] = j < nbc ? __ldg(L + j) : -INFINITY;
+        p[c] = j < nbc ? (SMEM ? L[j] : __ldg(L + j)) : -INFINITY;
     }
     float mx = p[0];
 #pragma unroll
@@ -623,6 +624,188 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel_split(const SelArgs
     if (a.counts && half == 1 && lane == 0) a.counts[unit] = total;
 }
 
+// ------------------------------------------------------------------------------------------------
+// (b') fused selection from the query rows: pooling, scores and tau selection in one launch
+// ------------------------------------------------------------------------------------------------
+// One CTA per (unit of QB consecutive query blocks, KV head): QB = 2 for the pair union, else 1; its
+// R = QB * g rows are the unit's query blocks times the g query heads of the KV head.
+//  1. pool: mean of the query rows of each block (rows of the chunk only) for the g heads, 16-byte
+//     loads along head_dim, rows summed in order per thread and the row groups combined in fixed
+//     order; optionally every row read is also written as e4m3 (the FP8 path's q8, fused);
+//  2. score: logits[r][j] = scale * qm[r] . km[j] for the unit's causal key blocks, fp32, into
+//     shared memory (blocks at or past nb_km score 0: the driver's zero padding);
+//  3. select: one warp per row with select_row_regs (the same arithmetic as select_kernel),
+//     diagonal and sink forced per query block, then the union of the mode and the list emission.
+constexpr int FU_THREADS = 256;
+constexpr int FU_MAX_FLOATS = 16384;                              // logits rows x padded blocks
+
+struct FusedArgs {
+    const uint16_t* q;
+    int64_t qrs, qhs;
+    int n, q_start, block, qblk0, MB;
+    const float* km;
+    int64_t khs, kbs;
+    int nb_km, H, Hk, nb_total, nbp;                              // nbp: padded logits row length
+    float scale, tau_f;
+    int32_t* counts;
+    int32_t* lists;
+    int64_t list_stride;
+    uint8_t* masks;
+    uint8_t* q8;
+    int64_t q8rs, q8hs;
+    const float* inv_scale;
+    int iss;
+};
+
+__device__ __forceinline__ void emit_row(const FusedArgs& a, int64_t unit, uint32_t keep, int npl, int lane) {
+    int total = 0;
+    for (int c = 0; c < npl; ++c) {
+        const bool on = (keep >> c) & 1u;
+        const uint32_t word = __ballot_sync(0xffffffffu, on);
+        const int j = 32 * c + lane;
+        if (a.lists && on) a.lists[unit * a.list_stride + total + __popc(word & ((1u << lane) - 1u))] = j;
+        if (a.masks && j < a.nb_total) a.masks[unit * a.nb_total + j] = on ? 1 : 0;
+        total += __popc(word);
+    }
+    if (a.counts && lane == 0) a.counts[unit] = total;
+}
+
+template <int NPL, int MODE>
+__global__ void __launch_bounds__(FU_THREADS, 2) select_fused_kernel(const FusedArgs a) {
+    constexpr int QB = MODE == SA_SELECT_PAIR_UNION ? 2 : 1;
+    extern __shared__ __align__(16) float fu_smem[];
+    const int g = a.H / a.Hk;
+    const int R = QB * g;
+    const int D = 128;
+    float* qm = fu_smem;                                          // [R][D]
+    float* logits = qm + R * D;                                   // [R][nbp]; the pooling partials first
+    uint32_t* keepw = reinterpret_cast<uint32_t*>(logits + R * a.nbp);   // [R][32] (unions)
+    const int hk = blockIdx.y;
+    const int m0 = blockIdx.x * QB;                               // first query block of the unit
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // ---------------------------------------------------------------- 1. pool
+    {
+        const int per_row = g * 16;                               // (head, 16-byte chunk) pairs of a row
+        const int RG = FU_THREADS / per_row;                      // row groups
+        const int ty = tid / per_row, tx = tid - ty * per_row;
+        const int hl = tx >> 4, c = tx & 15;
+        const int h = hk * g + hl;
+        float* partial = logits;                                  // [RG - 1][per_row][8]
+        const float inv = a.q8 ? __ldg(a.inv_scale + h * a.iss) : 0.f;
+        for (int qb = 0; qb < QB; ++qb) {
+            const int b = a.qblk0 + m0 + qb;
+            const int lo = max(a.q_start, b * a.block) - a.q_start;
+            const int hi = min(a.q_start + a.n, (b + 1) * a.block) - a.q_start;
+            float acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+            if (ty < RG) {
+                const uint16_t* src = a.q + static_cast<int64_t>(h) * a.qhs + c * 8;
+                uint8_t* dst = a.q8 ? a.q8 + static_cast<int64_t>(h) * a.q8hs + c * 8 : nullptr;
+                constexpr int BATCH = 8;                          // 8 row loads in flight, summed in order
+                for (int base = lo + ty; base < hi; base += BATCH * RG) {
+                    uint4 v[BATCH];
+#pragma unroll
+                    for (int k = 0; k < BATCH; ++k) {
+                        const int r = base + k * RG;
+                        v[k] = r < hi ? ld_stream(src + static_cast<int64_t>(r) * a.qrs) : make_uint4(0u, 0u, 0u, 0u);
+                    }
+#pragma unroll
+                    for (int k = 0; k < BATCH; ++k) {
+                        const int r = base + k * RG;
+                        if (r >= hi) break;
+                        float f[8];
+                        unpack8(v[k], f);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) acc[i] += f[i];
+                        if (dst)
+                            *reinterpret_cast<uint2*>(dst + static_cast<int64_t>(r) * a.q8rs) =
+                                quant8(f, inv, SA_QUANT_MUL_BF16);
+                    }
+                }
+                if (ty > 0) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) partial[((ty - 1) * per_row + tx) * 8 + i] = acc[i];
+                }
+            }
+            __syncthreads();
+            if (ty == 0) {
+                for (int k = 1; k < RG; ++k) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[i] += partial[((k - 1) * per_row + tx) * 8 + i];
+                }
+                const float cnt = static_cast<float>(max(hi - lo, 1));
+                float* o = qm + (qb * g + hl) * D + c * 8;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = hi > lo ? __fdiv_rn(acc[i], cnt) : 0.f;
+            }
+            __syncthreads();
+        }
+    }
+    // ---------------------------------------------------------------- 2. scores
+    const int nb_max = min(a.qblk0 + m0 + QB, a.nb_total);       // causal blocks of the unit's last q block
+    {
+        const float* kmh = a.km + static_cast<int64_t>(hk) * a.khs;
+        for (int j = tid; j < nb_max; j += FU_THREADS) {
+            const bool real = j < a.nb_km;
+            const float4* kr = reinterpret_cast<const float4*>(kmh + static_cast<int64_t>(real ? j : 0) * a.kbs);
+            for (int r0 = 0; r0 < R; r0 += 8) {
+                float acc[8];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+#pragma unroll 4
+                for (int d4 = 0; d4 < D / 4; ++d4) {
+                    const float4 kv = __ldg(kr + d4);
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) {
+                        if (r0 + r < R) {
+                            const float4 qv = reinterpret_cast<const float4*>(qm + (r0 + r) * D)[d4];
+                            acc[r] = fmaf(qv.x, kv.x, acc[r]);
+                            acc[r] = fmaf(qv.y, kv.y, acc[r]);
+                            acc[r] = fmaf(qv.z, kv.z, acc[r]);
+                            acc[r] = fmaf(qv.w, kv.w, acc[r]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+                    if (r0 + r < R) logits[(r0 + r) * a.nbp + j] = real ? acc[r] * a.scale : 0.f;
+            }
+        }
+    }
+    __syncthreads();
+    // ---------------------------------------------------------------- 3. select
+    const int npl_used = (a.nb_total + 31) >> 5;
+    for (int r = warp; r < R; r += FU_THREADS / 32) {
+        const int qb = r / g, i = r - qb * g;
+        const int m = m0 + qb;
+        const int gi = a.qblk0 + m;
+        const int nbc = min(gi + 1, a.nb_total);
+        uint32_t keep = static_cast<uint32_t>(select_row_regs<NPL, true>(logits + r * a.nbp, nbc, a.tau_f, lane));
+        if (gi < a.nb_total && (gi & 31) == lane) keep |= 1u << (gi >> 5);     // diagonal
+        if (lane == 0) keep |= 1u;                                             // sink
+        if (MODE == SA_SELECT_PER_HEAD)
+            emit_row(a, static_cast<int64_t>(hk * g + i) * a.MB + m, keep, npl_used, lane);
+        else
+            keepw[r * 32 + lane] = keep;
+    }
+    if (MODE == SA_SELECT_PER_HEAD) return;
+    __syncthreads();
+    if (MODE == SA_SELECT_KV_UNION) {                             // one row per (KV head, q block)
+        if (warp == 0) {
+            uint32_t keep = 0;
+            for (int i = 0; i < g; ++i) keep |= keepw[i * 32 + lane];
+            emit_row(a, static_cast<int64_t>(hk) * a.MB + m0, keep, npl_used, lane);
+        }
+    } else {                                                      // one row per (query head, q-block pair)
+        for (int i = warp; i < g; i += FU_THREADS / 32) {
+            const uint32_t keep = keepw[i * 32 + lane] | keepw[(g + i) * 32 + lane];
+            emit_row(a, static_cast<int64_t>(hk * g + i) * (a.MB / 2) + m0 / 2, keep, npl_used, lane);
+        }
+    }
+}
+
 int64_t logits_row_stride(int nb_total) { return (static_cast<int64_t>(nb_total) + 31) / 32 * 32; }
 
 // Scratch of sa_select_static: one buffer per device, part of the module image, so that entry
@@ -707,6 +890,60 @@ extern "C" int sa_select(const float* qm, int64_t qm_block_stride, int64_t qm_he
         select_kernel_long<<<blocks, SEL_THREADS, smem, s>>>(a, units, npl);
     }
     return check_launch("select_kernel");
+}
+
+extern "C" int sa_select_q(const void* q, int64_t q_row_stride, int64_t q_head_stride, int n, int q_start, int block,
+                           int qblk0, int MB, const float* km, int64_t km_head_stride, int64_t km_block_stride,
+                           int nb_km, int num_heads, int num_kv_heads, int head_dim, int nb_total, float scale,
+                           float tau, int mode, int32_t* counts, int32_t* lists, int64_t list_stride, uint8_t* masks,
+                           uint8_t* q8, int64_t q8_row_stride, int64_t q8_head_stride, const float* inv_scale,
+                           int inv_scale_stride, void* stream) {
+    const char* name = "sa_select_q";
+    if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || MB <= 0 || nb_total <= 0 || qblk0 < 0 ||
+        nb_km < 0 || n < 0 || q_start < 0 || block <= 0)
+        return fail(SA_ERR_ARG, "%s: bad sizes", name);
+    if (mode < 0 || mode > 2) return fail(SA_ERR_ARG, "%s: bad mode", name);
+    if (mode == SA_SELECT_PAIR_UNION && (MB % 2)) return fail(SA_ERR_ARG, "%s: pair union needs even MB", name);
+    if (lists && list_stride < nb_total) return fail(SA_ERR_ARG, "%s: list_stride < nb_total", name);
+    if (q_start < qblk0 * block || (n > 0 && q_start + n > (qblk0 + MB) * block))
+        return fail(SA_ERR_ARG, "%s: query rows outside the query blocks", name);
+    const int g = num_heads / num_kv_heads;
+    const int QB = mode == SA_SELECT_PAIR_UNION ? 2 : 1;
+    const int R = QB * g;
+    const int npl = (nb_total + 31) / 32;
+    const int nbp = npl * 32;
+    // shapes the one-pass kernel serves; others take block means + sa_select
+    if (head_dim != 128 || g > 16 || (16 * g) > FU_THREADS || npl > 32 || R * nbp > FU_MAX_FLOATS)
+        return fail(SA_ERR_UNSUPPORTED, "%s: %d heads per KV head, %d key blocks, head_dim %d (use sa_select)", name, g,
+                    nb_total, head_dim);
+    if (!q || (!km && nb_km > 0) || (q8 && !inv_scale)) return fail(SA_ERR_ARG, "%s: null pointer", name);
+    if (!aligned16(q) || q_row_stride % 8 || q_head_stride % 8 || !aligned16(km) || km_block_stride % 4 ||
+        km_head_stride % 4 || (q8 && ((reinterpret_cast<uintptr_t>(q8) & 7) || q8_row_stride % 8 || q8_head_stride % 8)))
+        return fail(SA_ERR_ALIGN, "%s: q and km 16-byte aligned, strides of 8 elements (q8: 8 bytes)", name);
+    const int per_row = 16 * g, RG = FU_THREADS / per_row;
+    const size_t smem = (static_cast<size_t>(R) * 128 + std::max<size_t>(static_cast<size_t>(R) * nbp,
+                         static_cast<size_t>(RG - 1) * per_row * 8) + static_cast<size_t>(R) * 32) * 4;
+    FusedArgs fa{static_cast<const uint16_t*>(q), q_row_stride, q_head_stride, n, q_start, block, qblk0, MB, km,
+                 km_head_stride, km_block_stride, nb_km, num_heads, num_kv_heads, nb_total, nbp, scale,
+                 static_cast<float>(tau), counts, lists, list_stride, masks, q8, q8_row_stride, q8_head_stride,
+                 inv_scale, inv_scale_stride};
+    void (*kern)(const FusedArgs) = nullptr;
+#define SA_FUSED_PICK(NPL_)                                                                            \
+    kern = mode == SA_SELECT_PER_HEAD ? select_fused_kernel<NPL_, SA_SELECT_PER_HEAD>                 \
+         : mode == SA_SELECT_KV_UNION ? select_fused_kernel<NPL_, SA_SELECT_KV_UNION>                 \
+                                      : select_fused_kernel<NPL_, SA_SELECT_PAIR_UNION>;
+    if (npl <= 4) { SA_FUSED_PICK(4) }
+    else if (npl <= 8) { SA_FUSED_PICK(8) }
+    else if (npl <= 16) { SA_FUSED_PICK(16) }
+    else { SA_FUSED_PICK(32) }
+#undef SA_FUSED_PICK
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+    }
+    dim3 grid(MB / QB, num_kv_heads);
+    kern<<<grid, FU_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(fa);
+    return check_launch(name);
 }
 
 // Same selection as sa_select, on the static scratch buffer above instead of a caller workspace.

@@ -29,6 +29,8 @@ SIGNATURES = {
     'sa_select': [_p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _f32, _i32, _p, _p,
                   _i64, _p, _p, _sz, _p],
     'sa_select_workspace_bytes': [_i32, _i32, _i32],
+    'sa_select_q': [_p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _f32,
+                    _f32, _i32, _p, _p, _i64, _p, _p, _i64, _i64, _p, _i32, _p],
     'sa_select_static': [_p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _f32, _i32,
                          _p, _p, _i64, _p, _p],
     'sa_quantize_e4m3': [_p, _i64, _i64, _i32, _i32, _i32, _p, _i32, _i32, _p, _i64, _i64, _i32, _i32, _p],

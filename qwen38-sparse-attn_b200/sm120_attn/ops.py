@@ -106,6 +106,36 @@ def select(qm, km, num_heads: int, num_kv_heads: int, nb_total: int, qblk0: int,
            _stream(qm.device))
 
 
+def select_q_supported(num_heads: int, num_kv_heads: int, head_dim: int, nb_total: int, mode: int) -> bool:
+    """Whether sa_select_q (the one-pass pooling + selection kernel) serves these sizes: head_dim 128,
+    at most 16 query heads per KV head, rows of at most 1024 key blocks, and the unit's logits
+    (query blocks of the unit x heads per KV head x padded key blocks) within 16384 floats."""
+    g = num_heads // num_kv_heads
+    npl = -(-nb_total // 32)
+    rows = (2 if mode == N.SA_SELECT_PAIR_UNION else 1) * g
+    return head_dim == 128 and g <= 16 and npl <= 32 and rows * npl * 32 <= 16384
+
+
+def select_q(q, q_start: int, block: int, qblk0: int, MB: int, km, num_heads: int, num_kv_heads: int,
+             nb_total: int, scale: float, tau: float, mode: int, counts=None, lists=None, masks=None, q8=None,
+             inv_scale=None):
+    """Block selection straight from the query rows (see sa_select_q): q [n, H, D] bf16 at absolute
+    positions q_start.., pooled per `block` rows into query blocks qblk0 .. qblk0+MB-1, scored against
+    km [Hk, NBk, D] fp32; optional fused e4m3 q8 [n, H, D] = e4m3(bf16(q * inv_scale))."""
+    _need_cuda('select_q', q, km, counts, lists, masks, q8, inv_scale)
+    assert q.dtype == torch.bfloat16 and q.stride(2) == 1 and km.dtype == torch.float32 and km.stride(2) == 1
+    n, H, D = q.shape
+    iss = 0
+    if q8 is not None:
+        assert q8.stride(2) == 1 and inv_scale is not None and inv_scale.dtype == torch.float32
+        iss = 0 if inv_scale.numel() == 1 else 1
+    N.call('sa_select_q', _p(q), q.stride(0), q.stride(1), n, q_start, block, qblk0, MB, _p(km), km.stride(0),
+           km.stride(1), km.shape[1], num_heads, num_kv_heads, D, nb_total, float(scale), float(tau), mode,
+           _p(counts), _p(lists), lists.stride(0) if lists is not None else 0, _p(masks), _p(q8),
+           q8.stride(0) if q8 is not None else 0, q8.stride(1) if q8 is not None else 0, _p(inv_scale), iss,
+           _stream(q.device))
+
+
 def quantize(x, scale, mode: int, out, transpose: bool = False, rows_pad: int = 0):
     """e4m3 quantisation of x [rows, heads, D] bf16 into out (uint8 / float8_e4m3fn storage)."""
     _need_cuda('quantize', x, scale, out)

@@ -94,6 +94,19 @@ class SparsePrefill:
             ops.block_means(k[:rows], 0, BLOCK, km, 0, fixed_divisor=BLOCK)
         return km
 
+    def _select(self, q, q_start, qblk0, MB, km, nb_total, mode, counts=None, lists=None, masks=None, q8=None,
+                inv_scale=None):
+        """Selection for the query rows q [n, H, D] at q_start.. over query blocks qblk0.. (MB of them):
+        one pass over q (pool, score, select; sa_select_q) when that kernel serves the sizes, else the
+        pooled means qm and sa_select.  q8 / inv_scale: fused e4m3 copy of q (FP8 path)."""
+        if ops.select_q_supported(self.H, self.Hk, self.D, nb_total, mode):
+            ops.select_q(q, q_start, BLOCK, qblk0, MB, km, self.H, self.Hk, nb_total, self.scale, self.tau, mode,
+                         counts=counts, lists=lists, masks=masks, q8=q8, inv_scale=inv_scale)
+            return
+        qm = self._pool_q(q, q_start, qblk0 * BLOCK, MB, q8=q8, inv_scale=inv_scale)
+        ops.select(qm, km, self.H, self.Hk, nb_total, qblk0, self.scale, self.tau, mode, counts=counts, lists=lists,
+                   masks=masks)
+
     def _pool_q(self, q, q_start, qs, MB, q8=None, inv_scale=None):
         """Pooled query blocks qm [MB, H, D] (block m at aligned position qs + m*BLOCK) of q [n, H, D] at
         q_start; optionally writes e4m3(bf16(q * inv_scale)) into q8 in the same pass."""
@@ -119,13 +132,10 @@ class SparsePrefill:
         if valid is None:
             valid = (0, n)
         v0, nv = int(valid[0]), int(valid[1])
-        qm = torch.zeros(MB, self.H, self.D, dtype=torch.float32, device=q.device)
-        if nv > 0:
-            ops.block_means(q[v0:v0 + nv], q_start + v0, BLOCK, qm.permute(1, 0, 2), q_start // BLOCK)
         rows = (self.Hk if union else self.H) * MB
         masks = torch.empty(rows, NB, dtype=torch.uint8, device=q.device)
-        ops.select(qm, km, self.H, self.Hk, NB, q_start // BLOCK, self.scale, self.tau,
-                   SA_SELECT_KV_UNION if union else SA_SELECT_PER_HEAD, masks=masks)
+        self._select(q[v0:v0 + nv], q_start + v0, q_start // BLOCK, MB, km, NB,
+                     SA_SELECT_KV_UNION if union else SA_SELECT_PER_HEAD, masks=masks)
         return masks.view(self.Hk if union else self.H, MB, NB).bool()
 
     # -------------------------------------------------------------------------------------------
@@ -166,11 +176,9 @@ class SparsePrefill:
         if FP8_EMULATE:
             q, k, v = (_fp8_round(t, FP8_EMULATE, name) for t, name in ((q, 'q'), (k, 'k'), (v, 'v')))
         NB = km.shape[1]
-        qm = self._pool_q(q, q_start, qs, MB)
         counts = torch.empty(self.H * MB, dtype=torch.int32, device=dev)
         lists = torch.empty(self.H * MB, NB, dtype=torch.int32, device=dev)
-        ops.select(qm, km, self.H, self.Hk, NB, qs // B, self.scale, self.tau, SA_SELECT_PER_HEAD,
-                   counts=counts, lists=lists)
+        self._select(q, q_start, qs // B, MB, km, NB, SA_SELECT_PER_HEAD, counts=counts, lists=lists)
         t1 = self._tick()
         o, copy_back = self._out(out, n, dev)
         ev0, ev1 = self._attn_events()
@@ -226,12 +234,11 @@ class SparsePrefill:
         st = _scale_tensor(dev, sq, sk, sv)
         inv, sc = st[0:3], st[3:6]
         q8 = torch.empty(n, self.H, self.D, dtype=torch.uint8, device=dev)
-        qm = self._pool_q(q, q_start, qs, MB, q8=q8, inv_scale=inv[0:1])
         rows = self.H * (M // BM)
         counts = torch.empty(rows, dtype=torch.int32, device=dev)
         lists = torch.empty(rows, nb_need, dtype=torch.int32, device=dev)
-        ops.select(qm, km, self.H, self.Hk, nb_need, qs // B, self.scale, self.tau,
-                   SA_SELECT_PAIR_UNION if B == 64 else SA_SELECT_PER_HEAD, counts=counts, lists=lists)
+        self._select(q, q_start, qs // B, MB, km, nb_need, SA_SELECT_PAIR_UNION if B == 64 else SA_SELECT_PER_HEAD,
+                     counts=counts, lists=lists, q8=q8, inv_scale=inv[0:1])
         if kv8 is not None:
             k8, v8 = kv8
             if k8.shape[0] < kv_len or v8.shape[0] < kv_len:

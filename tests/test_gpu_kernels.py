@@ -157,6 +157,68 @@ def test_select_matches_oracle(case):
         np.testing.assert_array_equal(pm.cpu().numpy().astype(bool).reshape(H, MB // 2, -1), O.pair_union(got))
 
 
+@pytest.mark.parametrize('case', SEL, ids=[f'b{c[0]}_{c[4]}_{c[1]}_{c[5]}' for c in SEL])
+def test_select_q_matches_oracle(case):
+    """The one-pass kernel (sa_select_q: pooling, scores and selection from the query rows) against the
+    oracle, in the three modes; shapes it does not serve are refused with SA_ERR_UNSUPPORTED."""
+    from sm120_attn._native import (SA_ERR_UNSUPPORTED, SA_SELECT_KV_UNION, SA_SELECT_PAIR_UNION,
+                                    SA_SELECT_PER_HEAD, NativeError)
+    ops = _ops()
+    block, kv, q_start, n, strength, H, Hk, hot = case
+    q, k, _, _ = synth.make_qkv(n, kv, H, Hk, 128, block=block, q_start=q_start, seed=kv + n, strength=strength,
+                                hot=hot, with_v=False)
+    qs = q_start - q_start % block
+    _, kmr = O.block_means(f32(k), 0, block)
+    qm = O.q_block_means(f32(q), q_start, block)
+    MB, NB = qm.shape[0], kmr.shape[1]
+    if block == 64 and MB % 2:
+        qm = np.concatenate([qm, np.zeros((1, H, 128), np.float32)])
+        MB += 1
+    nb_total = max(NB, qs // block + MB)
+    qd, km_d = q.to(DEV), torch.from_numpy(kmr).to(DEV)
+    supported = ops.select_q_supported(H, Hk, 128, nb_total, SA_SELECT_PER_HEAD)
+    masks = torch.empty(H * MB, nb_total, dtype=torch.uint8, device=DEV)
+    counts = torch.empty(H * MB, dtype=torch.int32, device=DEV)
+    lists = torch.full((H * MB, nb_total), -1, dtype=torch.int32, device=DEV)
+    if not supported:
+        with pytest.raises(NativeError) as err:
+            ops.select_q(qd, q_start, block, qs // block, MB, km_d, H, Hk, nb_total, 128 ** -0.5, 0.95,
+                         SA_SELECT_PER_HEAD, masks=masks)
+        assert err.value.code == SA_ERR_UNSUPPORTED
+        return
+    # per-head scales that keep |q * inv| below 448 (past it the hardware convert saturates where
+    # torch's cast gives NaN, a documented difference outside the quantiser's range)
+    inv = (400.0 / torch.from_numpy(np.abs(f32(q)).max(axis=(0, 2))).clamp_min(1e-3)).to(DEV)
+    q8 = torch.zeros(n, H, 128, dtype=torch.uint8, device=DEV)
+    ops.select_q(qd, q_start, block, qs // block, MB, km_d, H, Hk, nb_total, 128 ** -0.5, 0.95, SA_SELECT_PER_HEAD,
+                 counts=counts, lists=lists, masks=masks, q8=q8, inv_scale=inv)
+    np.testing.assert_array_equal(q8.cpu().numpy(), O.quantize_glue(f32(q), inv.cpu().numpy()))
+    ref, aux = O.select_masks(qm, kmr, qs, block, H, Hk, 0.95, nb_total=nb_total, return_aux=True)
+    got = masks.cpu().numpy().astype(bool).reshape(H, MB, nb_total)
+    report = {}
+    nbad, unexplained = O.compare_masks(got, ref, aux, 0.95, Hk, report=report)
+    print(f'sa_select_q mask exemptions {case}: {report} of {got.size} mask entries')
+    assert not unexplained, (nbad, unexplained[:8])
+    c, li = counts.cpu().numpy(), lists.cpu().numpy()
+    gm = got.reshape(H * MB, -1)
+    np.testing.assert_array_equal(c, gm.sum(1))
+    for r in range(H * MB):
+        np.testing.assert_array_equal(li[r, :c[r]], np.nonzero(gm[r])[0])
+    um = torch.empty(Hk * MB, nb_total, dtype=torch.uint8, device=DEV)
+    ops.select_q(qd, q_start, block, qs // block, MB, km_d, H, Hk, nb_total, 128 ** -0.5, 0.95, SA_SELECT_KV_UNION,
+                 masks=um)
+    np.testing.assert_array_equal(um.cpu().numpy().astype(bool).reshape(Hk, MB, -1),
+                                  got.reshape(Hk, H // Hk, MB, -1).any(1))
+    if block == 64 and ops.select_q_supported(H, Hk, 128, nb_total, SA_SELECT_PAIR_UNION):
+        pm = torch.empty(H * MB // 2, nb_total, dtype=torch.uint8, device=DEV)
+        pc = torch.empty(H * MB // 2, dtype=torch.int32, device=DEV)
+        ops.select_q(qd, q_start, block, qs // block, MB, km_d, H, Hk, nb_total, 128 ** -0.5, 0.95,
+                     SA_SELECT_PAIR_UNION, counts=pc, masks=pm)
+        pmn = pm.cpu().numpy().astype(bool)
+        np.testing.assert_array_equal(pmn.reshape(H, MB // 2, -1), O.pair_union(got))
+        np.testing.assert_array_equal(pc.cpu().numpy(), pmn.sum(1))
+
+
 # ------------------------------------------------------------------------------------------------
 # kernel (c): attention
 # ------------------------------------------------------------------------------------------------
