@@ -38,6 +38,17 @@ def test_two_rank_kv_head_shards_match_unsharded(tmp_path):
     assert sorted(p.name for p in tmp_path.iterdir()) == [f'ok{r}' for r in range(world)]
 
 
+def test_two_rank_glue_shards_match_unsharded(tmp_path):
+    """The product's host glue (block-mean cache, scale cache, block_masks) run per KV-head shard on two
+    gloo ranks reproduces the unsharded run."""
+    import torch.multiprocessing as mp
+    import multirank_worker
+    world = 2
+    mp.start_processes(multirank_worker.run_glue, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method='spawn', join=True)
+    assert sorted(p.name for p in tmp_path.iterdir()) == [f'ok{r}' for r in range(world)]
+
+
 def test_two_rank_tp_decoder_matches_unsharded(tmp_path):
     """The C5 decoder's tensor-parallel split (KV-head / intermediate / vocabulary slices, all-reduce
     after the row-parallel projections) reproduces the unsharded model on two gloo ranks."""
