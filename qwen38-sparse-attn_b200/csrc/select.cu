@@ -144,6 +144,7 @@ __global__ void __launch_bounds__(SC_THREADS, 2) score_kernel(
 // (b2) selection
 // ------------------------------------------------------------------------------------------------
 constexpr int SEL_WARPS = 8;
+constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr int SEL_THREADS = SEL_WARPS * 32;
 constexpr int SEL_MAX_NPL = 64;   // rows up to 2048 blocks in registers (one warp up to 1024, a warp pair above)
 
@@ -634,10 +635,113 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel_split(const SelArgs
 //     order; optionally every row read is also written as e4m3 (the FP8 path's q8, fused);
 //  2. score: logits[r][j] = scale * qm[r] . km[j] for the unit's causal key blocks, fp32, into
 //     shared memory (blocks at or past nb_km score 0: the driver's zero padding);
-//  3. select: one warp per row with select_row_regs (the same arithmetic as select_kernel),
-//     diagonal and sink forced per query block, then the union of the mode and the list emission.
+//  3. select: one warp per row with select_row_lean (the decision rule of select_kernel), the
+//     diagonal and the sink forced per query block, then the union of the mode and the list emission.
 constexpr int FU_THREADS = 256;
 constexpr int FU_MAX_FLOATS = 16384;                              // logits rows x padded blocks
+
+// Selection of one row held in shared memory, for the one-pass kernel: the same decision rule as
+// select_row_regs with cheaper fp32 arithmetic around it - exponentials as ex2.approx of the
+// log2e-scaled difference, one rounded reciprocal instead of a division per block, and the bisection
+// sums as multiply-adds by 0/1 - then the float64 check of the boundary and the float64 search where
+// it disagrees, which fix the decision exactly for the probabilities computed here.  Those differ
+// from torch's softmax by a few ulp, which moves a decision only for blocks whose cumulative mass is
+// within ~1e-6 of tau (inside the 1e-4 band of the parity bar).  Bit c of the result <-> block
+// lane + 32c.
+template <int NPL>
+__device__ uint32_t select_row_lean(const float* L, int nbc, float tau_f, int lane) {
+    float p[NPL];
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const int j = lane + 32 * c;
+        p[c] = j < nbc ? L[j] : -INFINITY;
+    }
+    float mx = p[0];
+#pragma unroll
+    for (int c = 1; c < NPL; ++c) mx = fmaxf(mx, p[c]);
+    mx = warp_max_f(mx);
+    const float off = -mx * LOG2E_F;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        p[c] = (lane + 32 * c < nbc) ? ex2_approx(fmaf(p[c], LOG2E_F, off)) : 0.f;
+        if (c & 1) s1 += p[c]; else s0 += p[c];
+    }
+    const float rs = __frcp_rn(warp_sum_f(s0 + s1));
+    double t0 = 0.0, t1 = 0.0;
+    float pmax = 0.f;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const bool valid = lane + 32 * c < nbc;
+        p[c] = valid ? p[c] * rs : -1.f;                          // -1: not a block of this row
+        const double d = valid ? static_cast<double>(p[c]) : 0.0;
+        if (c & 1) t1 += d; else t0 += d;
+        pmax = fmaxf(pmax, p[c]);
+    }
+    uint32_t keep = 0;
+    if (!(static_cast<float>(warp_sum_d(t0 + t1)) >= tau_f)) {   // tau never reached: every causal block
+#pragma unroll
+        for (int c = 0; c < NPL; ++c)
+            if (lane + 32 * c < nbc) keep |= 1u << c;
+        return keep;
+    }
+    auto mass32 = [&](float v) -> float {
+        float m0 = 0.f, m1 = 0.f, m2 = 0.f, m3 = 0.f;
+#pragma unroll
+        for (int c = 0; c < NPL; c += 4) {
+            m0 = fmaf(p[c] >= v ? 1.f : 0.f, p[c], m0);
+            if (c + 1 < NPL) m1 = fmaf(p[c + 1] >= v ? 1.f : 0.f, p[c + 1], m1);
+            if (c + 2 < NPL) m2 = fmaf(p[c + 2] >= v ? 1.f : 0.f, p[c + 2], m2);
+            if (c + 3 < NPL) m3 = fmaf(p[c + 3] >= v ? 1.f : 0.f, p[c + 3], m3);
+        }
+        return warp_sum_f((m0 + m1) + (m2 + m3));
+    };
+    auto pred64 = [&](uint32_t bits) -> bool {
+        const float v = __uint_as_float(bits);
+        double m0 = 0.0, m1 = 0.0;
+#pragma unroll
+        for (int c = 0; c < NPL; ++c) {
+            const double d = (p[c] >= v) ? static_cast<double>(p[c]) : 0.0;
+            if (c & 1) m1 += d; else m0 += d;
+        }
+        return static_cast<float>(warp_sum_d(m0 + m1)) >= tau_f;
+    };
+    const uint32_t top = __float_as_uint(warp_max_f(pmax)) + 1u;
+    uint32_t lo = 0u, hi = top;
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + ((hi - lo) >> 1);
+        if (mass32(__uint_as_float(mid)) >= tau_f) lo = mid; else hi = mid;
+    }
+    if (!(pred64(lo) && (hi == top || !pred64(hi)))) {
+        lo = 0u;
+        hi = top;
+        while (hi - lo > 1u) {
+            const uint32_t mid = lo + ((hi - lo) >> 1);
+            if (pred64(mid)) lo = mid; else hi = mid;
+        }
+    }
+    const float vstar = __uint_as_float(lo);
+    double above = 0.0;
+    int ties = 0;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        above += p[c] > vstar ? static_cast<double>(p[c]) : 0.0;
+        ties += (p[c] == vstar);
+    }
+    above = warp_sum_d(above);
+    ties = warp_sum_i(ties);
+    const int kt = ties_needed(above, vstar, ties, tau_f);
+    int seen = 0;
+#pragma unroll
+    for (int c = 0; c < NPL; ++c) {
+        const bool tie = p[c] == vstar;
+        const uint32_t tb = __ballot_sync(0xffffffffu, tie);
+        const int rank = seen + __popc(tb & ((1u << lane) - 1u));
+        if (p[c] > vstar || (tie && rank < kt)) keep |= 1u << c;
+        seen += __popc(tb);
+    }
+    return keep;
+}
 
 struct FusedArgs {
     const uint16_t* q;
@@ -671,20 +775,21 @@ __device__ __forceinline__ void emit_row(const FusedArgs& a, int64_t unit, uint3
 }
 
 template <int NPL, int MODE>
-__global__ void __launch_bounds__(FU_THREADS, 2) select_fused_kernel(const FusedArgs a) {
+__global__ void __launch_bounds__(FU_THREADS, NPL >= 32 ? 2 : 3) select_fused_kernel(const FusedArgs a) {
     constexpr int QB = MODE == SA_SELECT_PAIR_UNION ? 2 : 1;
     extern __shared__ __align__(16) float fu_smem[];
     const int g = a.H / a.Hk;
     const int R = QB * g;
     const int D = 128;
-    float* qm = fu_smem;                                          // [R][D]
-    float* logits = qm + R * D;                                   // [R][nbp]; the pooling partials first
+    float* qm = fu_smem;                                          // [R rounded up to 8][D]
+    float* logits = qm + ((R + 7) & ~7) * D;                      // [R][nbp]; the pooling partials first
     uint32_t* keepw = reinterpret_cast<uint32_t*>(logits + R * a.nbp);   // [R][32] (unions)
     const int hk = blockIdx.y;
     const int m0 = blockIdx.x * QB;                               // first query block of the unit
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     // ---------------------------------------------------------------- 1. pool
+    for (int i = R * D + tid; i < ((R + 7) & ~7) * D; i += FU_THREADS) qm[i] = 0.f;   // zero pad rows
     {
         const int per_row = g * 16;                               // (head, 16-byte chunk) pairs of a row
         const int RG = FU_THREADS / per_row;                      // row groups
@@ -744,33 +849,50 @@ __global__ void __launch_bounds__(FU_THREADS, 2) select_fused_kernel(const Fused
         }
     }
     // ---------------------------------------------------------------- 2. scores
+    // Lanes split head_dim: lane l holds columns 4l..4l+3 of 8 query rows in registers and reads the
+    // same columns of each key-means row (one coalesced 512-byte row per warp load).  Every 4 key
+    // blocks the 32 partial sums per lane (4 blocks x 8 rows) are reduced across the warp by a
+    // transposing butterfly (31 shuffles), after which lane l holds the score of block l >> 3, row
+    // l & 7.  Rows go in groups of 8 (qm is zero-padded to a multiple of 8 rows).
     const int nb_max = min(a.qblk0 + m0 + QB, a.nb_total);       // causal blocks of the unit's last q block
     {
+        const int R8 = (R + 7) & ~7;
         const float* kmh = a.km + static_cast<int64_t>(hk) * a.khs;
-        for (int j = tid; j < nb_max; j += FU_THREADS) {
-            const bool real = j < a.nb_km;
-            const float4* kr = reinterpret_cast<const float4*>(kmh + static_cast<int64_t>(real ? j : 0) * a.kbs);
-            for (int r0 = 0; r0 < R; r0 += 8) {
-                float acc[8];
+        const int nwarp = FU_THREADS / 32;
+        const int groups = (nb_max + 3) >> 2;                     // 4-block groups
+        for (int r0 = 0; r0 < R8; r0 += 8) {
+            float4 qv[8];
 #pragma unroll
-                for (int r = 0; r < 8; ++r) acc[r] = 0.f;
-#pragma unroll 4
-                for (int d4 = 0; d4 < D / 4; ++d4) {
-                    const float4 kv = __ldg(kr + d4);
+            for (int r = 0; r < 8; ++r) qv[r] = reinterpret_cast<const float4*>(qm + (r0 + r) * D)[lane];
+            for (int grp = warp; grp < groups; grp += nwarp) {
+                float v[32];                                      // v[b * 8 + r]: block 4grp+b, row r
 #pragma unroll
-                    for (int r = 0; r < 8; ++r) {
-                        if (r0 + r < R) {
-                            const float4 qv = reinterpret_cast<const float4*>(qm + (r0 + r) * D)[d4];
-                            acc[r] = fmaf(qv.x, kv.x, acc[r]);
-                            acc[r] = fmaf(qv.y, kv.y, acc[r]);
-                            acc[r] = fmaf(qv.z, kv.z, acc[r]);
-                            acc[r] = fmaf(qv.w, kv.w, acc[r]);
-                        }
+                for (int b = 0; b < 4; ++b) {
+                    const int j = 4 * grp + b;
+                    const bool real = j < nb_max && j < a.nb_km;
+                    const float4 kv = real ? __ldg(reinterpret_cast<const float4*>(kmh + static_cast<int64_t>(j) * a.kbs) + lane)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int r = 0; r < 8; ++r)
+                        v[b * 8 + r] = fmaf(qv[r].x, kv.x, fmaf(qv[r].y, kv.y, fmaf(qv[r].z, kv.z, qv[r].w * kv.w)));
+                }
+                // transposing butterfly: at step w (16, 8, 4, 2, 1) lanes exchange the half of their
+                // values selected by their lane bit w and keep the sum of the other half
+#pragma unroll
+                for (int w = 16; w >= 1; w >>= 1) {
+                    const bool upper = (lane & w) != 0;
+#pragma unroll
+                    for (int i = 0; i < w; ++i) {
+                        const float send = upper ? v[i] : v[i + w];
+                        const float keep = upper ? v[i + w] : v[i];
+                        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
                     }
                 }
-#pragma unroll
-                for (int r = 0; r < 8; ++r)
-                    if (r0 + r < R) logits[(r0 + r) * a.nbp + j] = real ? acc[r] * a.scale : 0.f;
+                // lane l now holds value index l (block l >> 3, row l & 7) in v[0]
+                const int b = lane >> 3, r = lane & 7;
+                const int j = 4 * grp + b;
+                if (j < nb_max && r0 + r < R)
+                    logits[(r0 + r) * a.nbp + j] = (j < a.nb_km) ? v[0] * a.scale : 0.f;
             }
         }
     }
@@ -782,7 +904,7 @@ __global__ void __launch_bounds__(FU_THREADS, 2) select_fused_kernel(const Fused
         const int m = m0 + qb;
         const int gi = a.qblk0 + m;
         const int nbc = min(gi + 1, a.nb_total);
-        uint32_t keep = static_cast<uint32_t>(select_row_regs<NPL, true>(logits + r * a.nbp, nbc, a.tau_f, lane));
+        uint32_t keep = select_row_lean<NPL>(logits + r * a.nbp, nbc, a.tau_f, lane);
         if (gi < a.nb_total && (gi & 31) == lane) keep |= 1u << (gi >> 5);     // diagonal
         if (lane == 0) keep |= 1u;                                             // sink
         if (MODE == SA_SELECT_PER_HEAD)
@@ -921,7 +1043,7 @@ extern "C" int sa_select_q(const void* q, int64_t q_row_stride, int64_t q_head_s
         km_head_stride % 4 || (q8 && ((reinterpret_cast<uintptr_t>(q8) & 7) || q8_row_stride % 8 || q8_head_stride % 8)))
         return fail(SA_ERR_ALIGN, "%s: q and km 16-byte aligned, strides of 8 elements (q8: 8 bytes)", name);
     const int per_row = 16 * g, RG = FU_THREADS / per_row;
-    const size_t smem = (static_cast<size_t>(R) * 128 + std::max<size_t>(static_cast<size_t>(R) * nbp,
+    const size_t smem = (static_cast<size_t>((R + 7) & ~7) * 128 + std::max<size_t>(static_cast<size_t>(R) * nbp,
                          static_cast<size_t>(RG - 1) * per_row * 8) + static_cast<size_t>(R) * 32) * 4;
     FusedArgs fa{static_cast<const uint16_t*>(q), q_row_stride, q_head_stride, n, q_start, block, qblk0, MB, km,
                  km_head_stride, km_block_stride, nb_km, num_heads, num_kv_heads, nb_total, nbp, scale,
