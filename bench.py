@@ -388,10 +388,7 @@ def run_b200(args):
         'dtype': 'fp8-e4m3 (fp32 accumulate, bf16 in/out)',
         'data': 'synthetic (seeded N(0,1) q/k/v with sink + 6 hot blocks per KV head)',
         'config': {
-            'workload': f'sparse FP8 prefill chunk (configs[1] shape): q {N_Q} @ {Q_START} vs {KV} keys, '
-                        f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection',
-            'global_batch': 1, 'seq_len': KV, 'chunk': N_Q,
-            'parallelism': f'kv-head shards x{world} ({args.scaling}), no collective on the data path',
+            **chunk_config(args, world),
             'gpus_active': world, 'kv_heads_per_gpu': hk,
             'ms_per_step_fastest_rank': round(-neg_min / args.steps, 4),
             'kept_fraction': round(kept, 4),
@@ -415,6 +412,13 @@ def run_b200(args):
         'clocks': clk,
     }
     line['check'] = check
+    if args.ttft_tokens > 0 and not n_failed:
+        # second half of the metric: prefill TTFT of the config-5 decoder, measured on the same ranks
+        # after the chunk workload (its tensors released first)
+        del q, k, v, out, bufs, q_h, k_h, v_h
+        ksp._KMEAN_CACHE.clear()
+        torch.cuda.empty_cache()
+        line['config']['ttft'] = measure_ttft(args.ttft_tokens, dev, rank, world, local)
     if n_failed:
         if rank == 0:
             print(f'bench: output check failed on {int(n_failed)} rank(s): {check}; no result line', file=sys.stderr,
@@ -591,9 +595,7 @@ def _selection(args, h, hk, dev, rank):
             'kernel_ms': sel_ms, 'kernel_work': sel_bytes, 'bound': 'hbm',
             'h2d': q_h.numel() * 2 + k_h.numel() * 2, 'd2h': c_h.numel() * 4 + l_h.numel() * 4,
             'launches': 2 if fused else 3,
-            'config': {'workload': f'selection path (configs[1] shape): K-chunk means into the cache, Q pooling, '
-                                   f'per-head selection to CSR; q {N_Q} @ {Q_START} vs {KV} keys, H {h}/Hk {hk}/D {D}, '
-                                   f'block {BLOCK}, tau {TAU}, {args.strength} injection',
+            'config': {**selection_config(args, h, hk),
                        'bytes_per_step': nbytes, 'nnz': nnz,
                        'note': 'value = algorithmic bytes (q + k chunk read, km read/append, CSR write) / time; '
                                'roofline on the query-side selection launch alone (q, km read, CSR write)'}}
@@ -772,6 +774,46 @@ def _decoder_kernels(args, h, hk, dev, rank):
                        'per_kernel': {k: {'us': round(t * 1000, 1), 'MB': round(b / 1e6, 1),
                                           'GB/s': round(b / (t * 1e-3) / 1e9, 1)} for k, (t, b) in per.items()},
                        'value_definition': 'algorithmic bytes of the three kernels / their time'}}
+
+
+def measure_ttft(tokens, dev, rank, world, local):
+    """Prefill TTFT (s) of the config-5 decoder for one prompt of `tokens` random ids, tensor parallel
+    over the ranks of the current process group (the headline line's secondary figure): model built
+    from random N(0, 0.02) weights, one untimed 8192-token prefill to warm up, then one timed prefill
+    on the device (max over ranks) and one end to end (ids from pinned host memory, first token read
+    back)."""
+    import torch
+    from sm120_attn.decoder import DecoderConfig, TPDecoder
+    from sm120_attn.shard import reduce_over_ranks
+    cfg = DecoderConfig()
+    t_init = time.perf_counter()
+    model = TPDecoder(cfg, dev, rank=rank, world=world, group=None, seed=0, tau=TAU, kernel='sm120fp8',
+                      fp8_kv_cache=False, max_tokens=tokens, chunk=8192, min_kv=8192, comm_blocks=2)
+    torch.cuda.synchronize(dev)
+    t_init = time.perf_counter() - t_init
+    g = torch.Generator()
+    g.manual_seed(0)
+    ids_host = torch.randint(0, cfg.vocab, (tokens,), generator=g).pin_memory()
+    ids_dev = ids_host.to(dev)
+    model.prefill(ids_dev[:min(tokens, 8192)])
+    toks = []
+    ms = _timed(lambda: toks.append(model.prefill(ids_dev)), 1, dev, world)
+    tok_host = torch.empty(1, dtype=torch.int64).pin_memory()
+
+    def e2e():
+        tok_host.copy_(model.prefill(ids_host.to(dev, non_blocking=True)).reshape(1), non_blocking=True)
+    e2e_ms = _timed(e2e, 1, dev, world)
+    kept = float(model.sp.kept_fraction() or 0.0)
+    (ms, e2e_ms), _ = reduce_over_ranks([ms, e2e_ms], [0.0], device=dev)
+    model.release_caches()
+    del model
+    torch.cuda.empty_cache()
+    return {'tokens': tokens, 'ttft_s': round(ms / 1000.0, 4), 'e2e_ttft_s': round(e2e_ms / 1000.0, 4),
+            'first_token': int(toks[-1].item()), 'kept_fraction': round(kept, 4), 'model_init_s': round(t_init, 1),
+            'model': f'random-init GQA decoder {cfg.layers} layers, hidden {cfg.hidden}, {cfg.heads}/{cfg.kv_heads} '
+                     f'heads, SwiGLU {cfg.inter}, vocab {cfg.vocab}, bf16; 8192-token chunks, sparse FP8 attention '
+                     f'tau {TAU}; tensor parallel over {world} GPU(s)',
+            'timing': 'device time of one prefill, max over ranks, after one warm-up prefill'}
 
 
 def run_ttft(args):
@@ -1018,27 +1060,44 @@ def run_reference(args):
         return
     sample = cpu_sample if args.workload == 'chunk' else (lambda st, seconds_budget=0: cpu_selection_sample(st))
     unit = 'TFLOPS' if args.workload == 'chunk' else 'GB/s'
+    # every one of the K timed steps is a bounded sample of the workload, sized so that the whole
+    # run (W + K samples) stays within about 150 s of host time
+    budget = max(1.0, min(10.0, 150.0 / max(1, args.steps + args.warmup)))
     vals = []
     desc, threads = '', 0
-    for _ in range(max(0, args.warmup)):                       # short untimed samples (BLAS threads, caches)
-        sample(args.strength, seconds_budget=2.0)
-    for _ in range(max(1, min(args.steps, 2))):
-        v, desc, threads = sample(args.strength, seconds_budget=10.0)
+    for _ in range(max(0, args.warmup)):                       # untimed samples (BLAS threads, caches)
+        sample(args.strength, seconds_budget=min(budget, 2.0))
+    for _ in range(max(1, args.steps)):
+        v, desc, threads = sample(args.strength, seconds_budget=budget)
         vals.append(v)
     value = sum(vals) / len(vals)
+    base = chunk_config(args, world) if args.workload == 'chunk' else selection_config(args, H_FULL, HK_FULL)
     line = {
         'metric': METRIC, 'value': round(value, 6), 'unit': unit, 'impl': 'reference', 'n_gpus': world,
         'steps': len(vals), 'warmup': max(0, args.warmup), 'higher_is_better': True, 'scaling': args.scaling,
         'vs_baseline': None, 'dtype': 'fp32', 'data': 'synthetic (seeded, same workload as the b200 arm)',
-        'config': {'workload': f'{"sparse prefill chunk" if args.workload == "chunk" else "selection path"} '
-                               f'(configs[1] shape): q {N_Q} @ {Q_START} vs {KV} keys, '
-                               f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection',
-                   'global_batch': 1, 'seq_len': KV, 'parallelism': 'host cores of rank 0'},
+        'config': base,
         'cpu_baseline': {'value': round(value, 6), 'unit': unit, 'cores': os.cpu_count(), 'threads': threads,
-                         'kind': 'port', 'sample': desc},
+                         'kind': 'port', 'sample': desc,
+                         'arm': 'host cores of rank 0 (the other ranks exit); the reference algorithm restated in '
+                                'numpy (oracle/), the reference checkout itself does not travel to the GPU host'},
         'e2e': {'value': round(value, 6), 'unit': unit, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def chunk_config(args, world):
+    """`config` of the default (chunk) workload, shared by both arms."""
+    return {'workload': f'sparse FP8 prefill chunk (configs[1] shape): q {N_Q} @ {Q_START} vs {KV} keys, '
+                        f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection',
+            'global_batch': 1, 'seq_len': KV, 'chunk': N_Q,
+            'parallelism': f'kv-head shards x{world} ({args.scaling}), no collective on the data path'}
+
+
+def selection_config(args, h, hk):
+    return {'workload': f'selection path (configs[1] shape): K-chunk means into the cache, Q pooling, '
+                        f'per-head selection to CSR; q {N_Q} @ {Q_START} vs {KV} keys, H {h}/Hk {hk}/D {D}, '
+                        f'block {BLOCK}, tau {TAU}, {args.strength} injection'}
 
 
 def main():
@@ -1059,6 +1118,9 @@ def main():
                     help='ttft workload: row blocks whose all-reduces overlap the next block\'s GEMMs (1: none)')
     ap.add_argument('--contexts', default='65536,131072,262144',
                     help='ttft workload: prompt lengths (the 131072 one is the reported value)')
+    ap.add_argument('--ttft-tokens', type=int, default=65536,
+                    help='default workload: also time the prefill TTFT of the config-5 decoder for a prompt of '
+                         'this many tokens (config.ttft; 0 skips it)')
     ap.add_argument('--fp8-kv-cache', action='store_true',
                     help='chunked / hook workloads: keep e4m3 K/V across chunks (SM120_SPARSE_FP8_KV_CACHE)')
     args = ap.parse_args()
