@@ -16,6 +16,9 @@ __global__ void __launch_bounds__(512, 2) block_means_kernel(const uint16_t* __r
                                    int64_t ohs, int64_t obs, int out_block0, uint8_t* __restrict__ q8,
                                    int64_t q8rs, int64_t q8hs, const float* __restrict__ inv_scale, int iss,
                                    int fixed_divisor) {
+    // a one-pass selection launched next may start its query pooling now (it waits for this kernel's
+    // block means before it reads them)
+    grid_dependents_launch();
     extern __shared__ float partial[];          // [RG-1][blockDim.x][8]
     const int cols = D >> 3;
     const int tx = threadIdx.x, ty = threadIdx.y, RG = blockDim.y;

@@ -198,6 +198,17 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 }
 
 // ------------------------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with the programmatic-serialization attribute
+// may start once every CTA of the kernel before it in the stream has executed
+// grid_dependents_launch (or exited); grid_dependency_wait then blocks until that kernel has
+// completed and its memory writes are visible.  Both are no-ops for kernels launched normally.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void grid_dependents_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ------------------------------------------------------------------------------------------
 // mbarrier
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {

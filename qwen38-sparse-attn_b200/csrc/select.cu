@@ -848,6 +848,8 @@ __global__ void __launch_bounds__(FU_THREADS, NPL >= 32 ? 2 : 3) select_fused_ke
             __syncthreads();
         }
     }
+    // the key means may come from the kernel launched just before (programmatic dependent launch)
+    grid_dependency_wait();
     // ---------------------------------------------------------------- 2. scores
     // Lanes split head_dim: lane l holds columns 4l..4l+3 of 8 query rows in registers and reads the
     // same columns of each key-means row (one coalesced 512-byte row per warp load).  Every 4 key
@@ -1063,8 +1065,21 @@ extern "C" int sa_select_q(const void* q, int64_t q_row_stride, int64_t q_head_s
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
     }
-    dim3 grid(MB / QB, num_kv_heads);
-    kern<<<grid, FU_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(fa);
+    // launched as a programmatic dependent of the previous kernel in the stream: the pooling of q
+    // (written by earlier kernels) may overlap that kernel, whose outputs (the key means) are read
+    // only after grid_dependency_wait
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(MB / QB, num_kv_heads);
+    cfg.blockDim = dim3(FU_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, fa);
+    if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
     return check_launch(name);
 }
 

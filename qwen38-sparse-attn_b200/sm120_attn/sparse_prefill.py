@@ -199,8 +199,9 @@ class SparsePrefill:
     def forward_sm120fp8(self, q, k, v, q_start, out=None, km=None, scales=None, kv8=None, k_rows=None):
         """FP8 (e4m3) kernel over 128-row query blocks; k, v NHD [T, Hk, D] bf16, quantised here.
 
-        scales: the request's (sq, sk, sv) as Python floats (the hook caches them per layer and
-        request); when absent they are taken from this call's amax (three device syncs).  kv8: optional (k8, v8) uint8
+        scales: the request's (sq, sk, sv), each a Python float (per tensor, the reference's scales) or
+        a sequence of per-head floats (H for q, Hk for k and v); the hook caches them per layer and
+        request.  When absent they are taken from this call's per-tensor amax (three device syncs).  kv8: optional (k8, v8) uint8
         [kv_len, Hk, D] already quantised with these scales (`_cached_kv8`); then k and v are not
         read here and may be None (with km and scales given), k_rows then standing for k.shape[0]
         (the selection covers ceil(k_rows / BLOCK) key blocks, as with the key tensor itself).
@@ -230,30 +231,28 @@ class SparsePrefill:
             amax = torch.cat([ops.absmax(t if t.stride(-1) == 1 else t.contiguous(), per_head=False)
                               for t in (q, k, v)]).clamp_min_(1e-6).tolist()
             scales = tuple(a / 448.0 for a in amax)
-        sq, sk, sv = scales
-        st = _scale_tensor(dev, sq, sk, sv)
-        inv, sc = st[0:3], st[3:6]
+        inv_q, inv_k, inv_v, s_q, s_k, s_v = _scale_views(dev, scales)
         q8 = torch.empty(n, self.H, self.D, dtype=torch.uint8, device=dev)
         rows = self.H * (M // BM)
         counts = torch.empty(rows, dtype=torch.int32, device=dev)
         lists = torch.empty(rows, nb_need, dtype=torch.int32, device=dev)
         self._select(q, q_start, qs // B, MB, km, nb_need, SA_SELECT_PAIR_UNION if B == 64 else SA_SELECT_PER_HEAD,
-                     counts=counts, lists=lists, q8=q8, inv_scale=inv[0:1])
+                     counts=counts, lists=lists, q8=q8, inv_scale=inv_q)
         if kv8 is not None:
             k8, v8 = kv8
             if k8.shape[0] < kv_len or v8.shape[0] < kv_len:
                 raise ValueError('kv8 holds fewer rows than q_start + n')
         else:
             k8 = torch.empty(kv_len, self.Hk, self.D, dtype=torch.uint8, device=dev)
-            ops.quantize(k[:kv_len], inv[1:2], SA_QUANT_MUL_BF16, k8)
+            ops.quantize(k[:kv_len], inv_k, SA_QUANT_MUL_BF16, k8)
             v8 = torch.empty(kv_len, self.Hk, self.D, dtype=torch.uint8, device=dev)
-            ops.quantize(v[:kv_len], inv[2:3], SA_QUANT_MUL_BF16, v8)
+            ops.quantize(v[:kv_len], inv_v, SA_QUANT_MUL_BF16, v8)
         t1 = self._tick()
         o, copy_back = self._out(out, n, dev)
         ev0, ev1 = self._attn_events()
         if ev0 is not None:
             ev0.record()
-        ops.attn_fp8(q8, k8, v8, o, kv_len, front, qs, counts, lists, B, sc[0:1], sc[1:2], sc[2:3], self.scale)
+        ops.attn_fp8(q8, k8, v8, o, kv_len, front, qs, counts, lists, B, s_q, s_k, s_v, self.scale)
         if ev1 is not None:
             ev1.record()
         self.last_counts, self.last_lists = counts, lists
@@ -344,6 +343,7 @@ _KNOBS = (
     _Knob('kernel', 'SM120_SPARSE_KERNEL', 'sm120fp8', str),
     _Knob('fp8_pipeline', 'SM120_SPARSE_FP8_PIPELINE', 'tma', str),
     _Knob('fp8_kv_cache', 'SM120_SPARSE_FP8_KV_CACHE', 0, _flag_or_empty),   # keep e4m3 K/V per request
+    _Knob('fp8_scales', 'SM120_SPARSE_FP8_SCALES', 'tensor', str),            # 'tensor' | 'head' e4m3 scales
 )
 
 
@@ -465,24 +465,40 @@ def _cached_block_means(layer_key, first_page, key_chunk, q_start, kv_len, key_a
 _SCALE_TENSORS: dict = {}
 
 
-def _scale_tensor(dev, sq, sk, sv):
-    """Device fp32 [1/sq, 1/sk, 1/sv, sq, sk, sv] for one scale triple, kept per (device, triple).
+def _scale_list(x) -> tuple:
+    """A scale as a tuple of floats: one for a per-tensor scale, one per head otherwise."""
+    return tuple(float(a) for a in x) if isinstance(x, (tuple, list)) else (float(x),)
+
+
+def _scale_views(dev, scales):
+    """Device fp32 views (1/sq, 1/sk, 1/sv, sq, sk, sv) of one scale triple, each of one element
+    (per-tensor scale) or one per head, kept per (device, triple).
 
     A host tensor copied from pageable memory makes the copy wait for the whole stream (a device
     sync every chunk); the triple is fixed per request and layer, so it is staged once through
     pinned memory and reused."""
+    parts = [_scale_list(x) for x in scales]
+    flat = [1.0 / a for p in parts for a in p] + [a for p in parts for a in p]
     dev = torch.device(dev)
     if dev.type != 'cuda':                                      # host-side tests with fake ops
-        return torch.tensor([1.0 / sq, 1.0 / sk, 1.0 / sv, sq, sk, sv], dtype=torch.float32, device=dev)
-    key = (dev.index if dev.index is not None else torch.cuda.current_device(), float(sq), float(sk), float(sv))
-    hit = _SCALE_TENSORS.get(key)
-    if hit is None:
-        if len(_SCALE_TENSORS) >= 4 * _KMEAN_MAX_ENTRIES:
-            _SCALE_TENSORS.pop(next(iter(_SCALE_TENSORS)))
-        host = torch.tensor([1.0 / sq, 1.0 / sk, 1.0 / sv, sq, sk, sv], dtype=torch.float32).pin_memory()
-        hit = (host.to(dev, non_blocking=True), host)          # the pinned source lives as long as the entry
-        _SCALE_TENSORS[key] = hit
-    return hit[0]
+        t = torch.tensor(flat, dtype=torch.float32, device=dev)
+    else:
+        key = (dev.index if dev.index is not None else torch.cuda.current_device(), tuple(parts))
+        hit = _SCALE_TENSORS.get(key)
+        if hit is None:
+            if len(_SCALE_TENSORS) >= 4 * _KMEAN_MAX_ENTRIES:
+                _SCALE_TENSORS.pop(next(iter(_SCALE_TENSORS)))
+            host = torch.tensor(flat, dtype=torch.float32).pin_memory()
+            hit = (host.to(dev, non_blocking=True), host)      # the pinned source lives as long as the entry
+            _SCALE_TENSORS[key] = hit
+        t = hit[0]
+    sizes = [len(p) for p in parts] * 2
+    return tuple(torch.split(t, sizes))
+
+
+def _kv_scale_key(scales) -> tuple:
+    """The part of a scale triple the e4m3 K/V bytes depend on (k and v scales)."""
+    return _scale_list(scales[1]), _scale_list(scales[2])
 
 
 _KV8_CACHE: dict = {}
@@ -515,13 +531,13 @@ def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
     k and v hold sequence rows k_row0 .. k_row0 + len (k_row0 > 0 only for a contiguous entry: a
     rebuild needs every row from 0).  The bytes are the same as re-quantising the history.
     """
-    sk, sv = float(scales[1]), float(scales[2])
+    kv_key = _kv_scale_key(scales)
     key = (layer_key, first_page)
     Hk, D = k.shape[1], k.shape[2]
     dev = k.device
 
     def continues(e):
-        return e['rows'] == q_start and e['scales'] == (sk, sv)
+        return e['rows'] == q_start and e['scales'] == kv_key
     prior = _KV8_CACHE.get(key)
     if k_row0 and not (prior is not None and q_start > 0 and continues(prior)):
         raise RuntimeError('stale FP8 KV cache entry and no key/value rows before %d to rebuild it' % k_row0)
@@ -529,8 +545,8 @@ def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
     def fresh():
         rows = max(kv_len, 8192)
         return {'k8': torch.empty(rows, Hk, D, dtype=torch.uint8, device=dev),
-                'v8': torch.empty(rows, Hk, D, dtype=torch.uint8, device=dev), 'rows': 0, 'scales': (sk, sv),
-                'inv': _scale_tensor(dev, scales[0], sk, sv)[1:3]}
+                'v8': torch.empty(rows, Hk, D, dtype=torch.uint8, device=dev), 'rows': 0, 'scales': kv_key,
+                'inv': _scale_views(dev, scales)[1:3]}
     entry, _ = _request_entry(_KV8_CACHE, key, q_start, continues, fresh)
     lo = entry['rows']
     if entry['k8'].shape[0] < kv_len:
@@ -543,8 +559,8 @@ def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
     if kv_len > lo:
         if k.shape[0] < kv_len - k_row0 or v.shape[0] < kv_len - k_row0 or lo < k_row0:
             raise ValueError('_cached_kv8: k/v do not hold rows %d..%d' % (lo, kv_len))
-        ops.quantize(k[lo - k_row0:kv_len - k_row0], entry['inv'][0:1], SA_QUANT_MUL_BF16, entry['k8'][lo:kv_len])
-        ops.quantize(v[lo - k_row0:kv_len - k_row0], entry['inv'][1:2], SA_QUANT_MUL_BF16, entry['v8'][lo:kv_len])
+        ops.quantize(k[lo - k_row0:kv_len - k_row0], entry['inv'][0], SA_QUANT_MUL_BF16, entry['k8'][lo:kv_len])
+        ops.quantize(v[lo - k_row0:kv_len - k_row0], entry['inv'][1], SA_QUANT_MUL_BF16, entry['v8'][lo:kv_len])
     entry['rows'] = kv_len
     return entry['k8'][:kv_len], entry['v8'][:kv_len]
 
@@ -556,21 +572,31 @@ def _fp8_warm(layer_key, first_page, q_start) -> bool:
     km, sc, kv = _KMEAN_CACHE.get(key), _SCALE_CACHE.get(key), _KV8_CACHE.get(key)
     return (q_start > 0 and km is not None and km.get('last_kv') == q_start and km['nb'] >= q_start // BLOCK
             and sc is not None and sc['last_kv'] == q_start and kv is not None and kv['rows'] == q_start
-            and kv['scales'] == (float(sc['scales'][1]), float(sc['scales'][2])))
+            and kv['scales'] == _kv_scale_key(sc['scales']))
 
 
 _SCALE_CACHE: dict = {}
 SCALE_MARGIN = 1.5
 
 
-def _cached_scales(layer_key, first_page, q, k, v, q_start):
+def _cached_scales(layer_key, first_page, q, k, v, q_start, per_head: bool = False):
     """e4m3 scales (sq, sk, sv) of a request, fixed at its first sparse chunk: amax of that chunk's q and
     of k, v (the history so far) / 448, times SCALE_MARGIN for the rows still to come
-    (sparse_prefill.py:450-469).  One host sync when an entry is made."""
+    (sparse_prefill.py:450-469).  per_head (SM120_SPARSE_FP8_SCALES=head): each of the three is a
+    tuple with one scale per head (H for q, Hk for k and v) instead of one per tensor.  One host sync
+    when an entry is made."""
     def fresh():
-        peaks = torch.cat([ops.absmax(t if t.stride(-1) == 1 else t.contiguous(), per_head=False)
-                           for t in (q, k, v)]).clamp_min(1e-6).tolist()
-        return {'scales': tuple(a * SCALE_MARGIN / 448.0 for a in peaks), 'last_kv': 0}
+        peaks = [ops.absmax(t if t.stride(-1) == 1 else t.contiguous(), per_head=per_head).clamp_min(1e-6)
+                 for t in (q, k, v)]
+        if not per_head:
+            return {'scales': tuple(a * SCALE_MARGIN / 448.0 for a in torch.cat(peaks).tolist()), 'last_kv': 0}
+        sizes = [int(p.numel()) for p in peaks]
+        host = torch.cat(peaks).tolist()
+        parts, i = [], 0
+        for n in sizes:
+            parts.append(tuple(a * SCALE_MARGIN / 448.0 for a in host[i:i + n]))
+            i += n
+        return {'scales': tuple(parts), 'last_kv': 0}
     entry, _ = _request_entry(_SCALE_CACHE, (layer_key, first_page), q_start,
                               lambda e: e['last_kv'] == q_start, fresh)
     entry['last_kv'] = q_start + q.shape[0]
@@ -678,7 +704,7 @@ def _sparse_request(sp, cfg, layer, rq, q_r, key_r, key_cache, value_cache, o_r,
         own = pages_row[p0:npages].long()
         k_new, v_new = key_cache[own].reshape(-1, Hk, D), value_cache[own].reshape(-1, Hk, D)
         km = _cached_block_means(layer, rq.first_page, key_r, q_start, rq.kv_len)
-        scales = _cached_scales(layer, rq.first_page, q_r, None, None, q_start)
+        scales = _cached_scales(layer, rq.first_page, q_r, None, None, q_start, per_head=cfg.get('fp8_scales') == 'head')
         kv8 = _cached_kv8(layer, rq.first_page, k_new, v_new, q_start, rq.kv_len, scales, k_row0=p0 * page)
         sp.forward_sm120fp8(q_r, None, None, q_start, out=o_r, km=km, scales=scales, kv8=kv8, k_rows=npages * page)
         return
@@ -689,7 +715,8 @@ def _sparse_request(sp, cfg, layer, rq, q_r, key_r, key_cache, value_cache, o_r,
     if not fp8:
         sp.forward_sm120(q_r, k_all, v_all, q_start, out=o_r, km=km)
         return
-    scales = _cached_scales(layer, rq.first_page, q_r, k_all[:rq.kv_len], v_all[:rq.kv_len], q_start)
+    scales = _cached_scales(layer, rq.first_page, q_r, k_all[:rq.kv_len], v_all[:rq.kv_len], q_start,
+                            per_head=cfg.get('fp8_scales') == 'head')
     kv8 = _cached_kv8(layer, rq.first_page, k_all, v_all, q_start, rq.kv_len, scales) if cfg['fp8_kv_cache'] else None
     sp.forward_sm120fp8(q_r, k_all, v_all, q_start, out=o_r, km=km, scales=scales, kv8=kv8)
 

@@ -202,6 +202,53 @@ def test_fp8_kv_cache_chunks_bit_identical(ksp):
     ksp._KV8_CACHE.clear()
 
 
+def test_fp8_per_head_scales_and_kv_cache(ksp):
+    """Per-head e4m3 scales (SM120_SPARSE_FP8_SCALES=head): output within the FP8 bars of the fp32
+    reference and of the P-rounding model on per-head dequantised operands, and the FP8 KV cache
+    with per-head scales bit-identical to re-quantising the history."""
+    from kmodel import fp8_model_kwargs
+    ksp.BLOCK = 128
+    ksp._KV8_CACHE.clear()
+    H, Hk, D, n = 16, 2, 128, 1024
+    kv_total = 2 * n + 256
+    q, k, v, _ = synth.make_qkv(kv_total, kv_total, H, Hk, D, block=128, q_start=0, seed=23, strength='strong')
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    sp = ksp.SparsePrefill(H, Hk, D, DEV, tau=0.95, min_kv=0, min_q=0, kernel='sm120fp8')
+    for q_start in (0, n + 256):
+        kv_len = q_start + n
+        qc = qd[q_start:kv_len]
+        km = ksp._cached_block_means('ph', 3, kd[q_start:kv_len], q_start, kv_len, key_all=kd)
+        scales = ksp._cached_scales('ph', 3, qc, kd[:kv_len], vd[:kv_len], q_start, per_head=True)
+        assert len(scales[0]) == H and len(scales[1]) == Hk
+        o_plain = sp.forward_sm120fp8(qc, kd[:kv_len], vd[:kv_len], q_start, km=km, scales=scales)
+        kv8 = ksp._cached_kv8('ph', 3, kd, vd, q_start, kv_len, scales)
+        o_cache = sp.forward_sm120fp8(qc, kd[:kv_len], vd[:kv_len], q_start, km=km, scales=scales, kv8=kv8)
+        torch.cuda.synchronize()
+        from sm120_attn import ops
+        ops.check_status(DEV)
+        assert torch.equal(o_plain, o_cache), q_start
+    # oracle on the last chunk: per-head quantised operands, the kernel's lists
+    sq, sk, sv = (np.asarray(x, np.float32) for x in scales)
+    qf, kf, vf = f32(q)[q_start:kv_len], f32(k)[:kv_len], f32(v)[:kv_len]
+    q8 = O.quantize_glue(qf, (1.0 / sq).astype(np.float32))
+    k8 = O.quantize_glue(kf, (1.0 / sk).astype(np.float32))
+    v8 = O.quantize_glue(vf, (1.0 / sv).astype(np.float32))
+    deq = [O.e4m3_decode(b) * s[None, :, None] for b, s in ((q8, sq), (k8, sk), (v8, sv))]
+    counts, lists = sp.last_counts.cpu().numpy(), sp.last_lists.cpu().numpy()
+    n_tiles = n // 128
+    masks = np.zeros((H * n_tiles, lists.shape[1]), dtype=bool)
+    for r in range(H * n_tiles):
+        masks[r, lists[r, :counts[r]]] = True
+    masks = masks.reshape(H, n_tiles, -1)
+    got = f32(o_plain)
+    ref = O.attention_ref(*deq, q_start, masks, q_block=128, kv_block=128)
+    model = O.attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_start, counts, lists, q_block=128, kv_block=128,
+                                         **fp8_model_kwargs(H, Hk, n_tiles))
+    assert rel_l2(got, model) < 1e-2, rel_l2(got, model)
+    assert rel_l2(got, ref) < 3e-2, rel_l2(got, ref)
+    ksp._KV8_CACHE.clear()
+
+
 def test_stale_first_page(ksp):
     """tests/test_sparse_prefill.py:65-92: a recycled first page never supplies stale means or scales."""
     ksp.BLOCK = 64
@@ -285,14 +332,15 @@ def test_dropin_kernels_match_reference_semantics():
     assert rel_l2(f32(o8d), O.attention_ref(*deq, kv - n)) < 3e-2
 
 
-@pytest.mark.parametrize('kv_cache', [False, True])
-def test_try_sparse_forward_paged(ksp, monkeypatch, kv_cache):
+@pytest.mark.parametrize('kv_cache,scale_mode', [(False, 'tensor'), (True, 'tensor'), (True, 'head')])
+def test_try_sparse_forward_paged(ksp, monkeypatch, kv_cache, scale_mode):
     """The vLLM hook with a paged KV cache and fake metadata: eligible requests go through the sparse path
-    and match a direct forward_sm120fp8 call (with and without the FP8 KV cache); the ineligible one is
-    handed to _dense_request."""
+    and match a direct forward_sm120fp8 call (with and without the FP8 KV cache, per-tensor or per-head
+    e4m3 scales); the ineligible one is handed to _dense_request."""
     ksp.BLOCK = 64
     monkeypatch.setattr(ksp, '_CONFIG', {'enabled': True, 'tau': 0.95, 'min_kv': 2048, 'min_q': 512,
-                                         'kernel': 'sm120fp8', 'fp8_pipeline': 'tma', 'fp8_kv_cache': kv_cache})
+                                         'kernel': 'sm120fp8', 'fp8_pipeline': 'tma', 'fp8_kv_cache': kv_cache,
+                                         'fp8_scales': scale_mode})
     ksp._STATE.clear()
     dense_calls = []
     monkeypatch.setattr(ksp, '_dense_request', lambda *a: dense_calls.append(a[-2:]))
@@ -331,7 +379,12 @@ def test_try_sparse_forward_paged(ksp, monkeypatch, kv_cache):
         kfull = key_cache[bt[r, :npages[r]].long()].reshape(-1, Hk, D)
         vfull = value_cache[bt[r, :npages[r]].long()].reshape(-1, Hk, D)
         q_r = query[qsl[r]:qsl[r + 1]]
-        scales = tuple(float(t.float().abs().amax()) * ksp.SCALE_MARGIN / 448.0 for t in (q_r, kfull[:kv], vfull[:kv]))
+        if scale_mode == 'head':
+            scales = tuple(tuple(float(a) * ksp.SCALE_MARGIN / 448.0 for a in t.float().abs().amax(dim=(0, 2)).tolist())
+                           for t in (q_r, kfull[:kv], vfull[:kv]))
+        else:
+            scales = tuple(float(t.float().abs().amax()) * ksp.SCALE_MARGIN / 448.0
+                           for t in (q_r, kfull[:kv], vfull[:kv]))
         full = kv // 64
         km = torch.zeros(Hk, -(-kv // 64), D, device=DEV)
         km[:, :full] = kfull[:full * 64].float().view(full, 64, Hk, D).mean(1).transpose(0, 1)

@@ -61,7 +61,7 @@ def test_config_env_and_json(monkeypatch, tmp_path, capsys):
     monkeypatch.setattr(m, '_CONFIG', None)
     c = m.config()
     assert c == {'enabled': False, 'tau': 0.85, 'min_kv': 4096, 'min_q': 1024, 'kernel': 'sm120', 'fp8_pipeline': 'tma',
-                 'fp8_kv_cache': False}
+                 'fp8_kv_cache': False, 'fp8_scales': 'tensor'}
     assert 'config' in capsys.readouterr().out
     assert m.config() is c                                           # cached
     monkeypatch.setattr(m, '_CONFIG', None)
@@ -163,6 +163,23 @@ def test_cached_scales_bookkeeping(ksp):
     np.testing.assert_allclose(np.array([s0, s1, s2]), np.array([r0, r1, r2]), rtol=1e-12)
     assert s0 == s1 and s2 != s1
     assert ksp._SCALE_CACHE[('L', 3)]['last_kv'] == 1000 + 512
+
+
+def test_cached_scales_per_head(ksp):
+    """SM120_SPARSE_FP8_SCALES=head: one scale per query head and per KV head, fixed at the request's
+    first chunk like the per-tensor ones; the FP8 KV cache keys on them."""
+    q, k, v, _ = synth.make_qkv(512, 2048, 8, 2, 128, seed=6, strength='strong')
+    sq, sk, sv = ksp._cached_scales('H', 1, q, k[:1536], v[:1536], 1024, per_head=True)
+    margin = ksp.SCALE_MARGIN / 448.0
+    np.testing.assert_allclose(sq, np.abs(q.float().numpy()).max(axis=(0, 2)) * margin, rtol=1e-6)
+    np.testing.assert_allclose(sk, np.abs(k[:1536].float().numpy()).max(axis=(0, 2)) * margin, rtol=1e-6)
+    assert len(sq) == 8 and len(sk) == len(sv) == 2
+    assert ksp._cached_scales('H', 1, q, None, None, 1536, per_head=True) == (sq, sk, sv)   # continued
+    views = ksp._scale_views('cpu', (sq, sk, sv))
+    assert [t.numel() for t in views] == [8, 2, 2, 8, 2, 2]
+    np.testing.assert_allclose(views[4].numpy(), sk, rtol=1e-6)
+    assert ksp._kv_scale_key((sq, sk, sv)) == (tuple(sk), tuple(sv))
+    assert ksp._kv_scale_key((0.1, 0.2, 0.3)) == ((0.2,), (0.3,))
 
 
 def test_cached_kv8_quantises_each_row_once(ksp, monkeypatch):
