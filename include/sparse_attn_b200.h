@@ -44,6 +44,7 @@ extern "C" {
 #define SA_DEV_WAIT_P 0x8        /* a wait for the probability (P) tile expired           */
 #define SA_DEV_WAIT_O 0x10       /* a wait for the output accumulator expired             */
 #define SA_DEV_BAD_LIST 0x20     /* a block index in a list was out of range              */
+#define SA_DEV_BAD_PAGE 0x40     /* a page id in a page table was out of range (read as 0) */
 
 /* selection modes for sa_select */
 #define SA_SELECT_PER_HEAD 0     /* one row per (query head, q block): union=False         */
@@ -78,6 +79,33 @@ SA_API int sa_block_means_bf16(const void* x, int64_t x_row_stride, int64_t x_he
                         int64_t out_block_stride, int out_block0, uint8_t* q8, int64_t q8_row_stride,
                         int64_t q8_head_stride, const float* inv_scale, int inv_scale_stride, int fixed_divisor,
                         void* stream);
+
+/*
+ * Paged KV caches.  The reference gathers a request's whole key/value history out of vLLM's paged
+ * cache on every chunk (sm120_attn/sparse_prefill.py:521-522, `key_cache[pages].reshape(...)`);
+ * these entries read the pages in place instead.  cache: bf16 [num_pages, page_size, heads,
+ * head_dim] viewed through element strides page_stride / row_stride / head_stride (vLLM's
+ * key_cache or value_cache, page_stride % 8 == 0); the row at logical position l of the request is
+ * slot l % page_size of page page_table[l / page_size] (the request's row of vLLM's block table,
+ * int32).  page_table must hold an entry for every page the call reads.
+ */
+/* sa_block_means_bf16 (no fixed divisor, no q8) over the keys at positions pos0 .. pos0+n-1 of a
+ * paged cache; the same launch shape and summation order as sa_block_means_bf16 over the gathered
+ * rows, so the two give the same bits. */
+SA_API int sa_block_means_paged_bf16(const void* cache, int64_t page_stride, int64_t row_stride, int64_t head_stride,
+                                     const int32_t* page_table, int page_size, int n, int heads, int head_dim,
+                                     int pos0, int block, float* out, int64_t out_head_stride,
+                                     int64_t out_block_stride, int out_block0, void* stream);
+/* sa_absmax_bf16 over the rows at positions row0 .. row0+rows-1 of a paged cache. */
+SA_API int sa_absmax_paged_bf16(const void* cache, int64_t page_stride, int64_t row_stride, int64_t head_stride,
+                                const int32_t* page_table, int page_size, int row0, int rows, int heads, int head_dim,
+                                int per_head, float* out, void* stream);
+/* sa_quantize_e4m3 (row-major output) of the rows at positions row0 .. row0+rows-1 of a paged cache:
+ * out row r holds position row0 + r. */
+SA_API int sa_quantize_paged_e4m3(const void* cache, int64_t page_stride, int64_t row_stride, int64_t head_stride,
+                                  const int32_t* page_table, int page_size, int row0, int rows, int heads,
+                                  int head_dim, const float* scale, int scale_stride, int mode, uint8_t* out,
+                                  int64_t out_row_stride, int64_t out_head_stride, void* stream);
 
 /*
  * (b) Block selection.  Replaces `SparsePrefill.block_masks` (sm120_attn/sparse_prefill.py:41-85)
@@ -211,6 +239,24 @@ SA_API int sa_attn_fwd_bf16(const void* q, int64_t q_row_stride, int64_t q_head_
                      float softmax_scale, int32_t* status, void* stream);
 
 /*
+ * sa_attn_fwd_bf16 reading K and V from paged caches in place (the reference gathers the request's
+ * history into contiguous tensors first, sm120_attn/sparse_prefill.py:521-522).  k_cache, v_cache:
+ * bf16 [num_pages, page_size, num_kv_heads, head_dim] with the same element strides page_stride /
+ * row_stride / head_stride (multiples of 8); the key at position j is slot j % page_size of page
+ * page_table[j / page_size], for j < kv_len (page_table holds ceil(kv_len / page_size) ids in
+ * [0, num_pages)).  page_size 8, 16, 32 or a multiple of 64.  Keys past kv_len read as zero, as in
+ * sa_attn_fwd_bf16; a page id out of range sets SA_DEV_BAD_PAGE in status and reads as zeros.
+ * Every other argument as sa_attn_fwd_bf16.
+ */
+SA_API int sa_attn_fwd_bf16_paged(const void* q, int64_t q_row_stride, int64_t q_head_stride, const void* k_cache,
+                                  const void* v_cache, int64_t page_stride, int64_t row_stride, int64_t head_stride,
+                                  const int32_t* page_table, int page_size, int num_pages, void* out,
+                                  int64_t o_row_stride, int64_t o_head_stride, int n_q, int num_heads, int num_kv_heads,
+                                  int head_dim, int kv_len, int q_front, int q_offset, const int32_t* counts,
+                                  const int32_t* lists, int64_t list_stride, int q_block, int kv_block,
+                                  float softmax_scale, int32_t* status, void* stream);
+
+/*
  * Elementwise kernels of the end-to-end prefill harness (benchmark configuration 5: a random-init dense
  * GQA decoder whose TTFT the reference measures through vLLM, scripts/bench_ttft.py:1-12).  The
  * reference has no entry points of its own here: these compute what vLLM 0.22's model layers do
@@ -231,6 +277,17 @@ SA_API int sa_add_rmsnorm_bf16(const void* delta, int64_t delta_row_stride, void
 SA_API int sa_rope_qkv_bf16(const void* qkv, int64_t qkv_row_stride, int rows, int num_heads, int num_kv_heads,
                             int head_dim, const float* cos_sin, int pos0, int max_pos, void* q_out, void* k_out,
                             int64_t k_row_stride, void* v_out, int64_t v_row_stride, void* stream);
+
+/* sa_rope_qkv_bf16 that also writes the fp32 block means of the rotated k rows it stores (the key
+ * block summary of sm120_attn/sparse_prefill.py:437-446 taken at KV-write time, with no second pass
+ * over the keys): for every block b in [pos0/block, ceil((pos0+rows)/block)) and KV head h,
+ *   km[h*km_head_stride + (b - km_block0)*km_block_stride + d] = mean of k_out rows of block b
+ * (the rows this call writes).  Bit for bit what sa_block_means_bf16(k_out, ..., pos0, block, km,
+ * ..., km_block0) computes afterwards. */
+SA_API int sa_rope_qkv_means_bf16(const void* qkv, int64_t qkv_row_stride, int rows, int num_heads, int num_kv_heads,
+                                  int head_dim, const float* cos_sin, int pos0, int max_pos, void* q_out, void* k_out,
+                                  int64_t k_row_stride, void* v_out, int64_t v_row_stride, int block, float* km,
+                                  int64_t km_head_stride, int64_t km_block_stride, int km_block0, void* stream);
 
 /* out[r, j] = silu(gate_up[r, j]) * gate_up[r, inter + j], j < inter (inter % 8 == 0). */
 SA_API int sa_silu_mul_bf16(const void* gate_up, int64_t gate_up_row_stride, int rows, int inter, void* out,

@@ -23,6 +23,15 @@ struct Params {
     int qss, kss, vss;
     float softmax_scale;
     int32_t* status;
+    // Paged K/V (BF16 kernel; pages == nullptr: contiguous K/V): key j of the request is slot j % page
+    // of cache page pages[j / page].  The tensor maps are then 4D {head_dim, Hk, page, num_pages}
+    // with box_rows-row boxes (box_rows = min(page, 64)); kc / vc and the element strides serve the
+    // plain loads of the one box that holds the last key when kv_len ends inside it.
+    const int32_t* pages;
+    int page, box_rows, num_pages;
+    const uint16_t* kc;
+    const uint16_t* vc;
+    int64_t kv_ps, kv_rs, kv_hs;
 };
 
 // Paired-tile attention kernel (attn_pair.cu, FP8 only): two 128-row query tiles per CTA sharing
@@ -157,6 +166,26 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
             fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
     });
     return fn;
+}
+
+inline int encode_nd(CUtensorMap* map, bool fp8, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle sw, const char* what) {
+    auto fn = encode_fn();
+    if (!fn) return fail(SA_ERR_TMA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t d[5];
+    cuuint64_t st[4];
+    cuuint32_t b[5], e[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        b[i] = box[i];
+        e[i] = 1;
+        if (i + 1 < rank) st[i] = strides_bytes[i];
+    }
+    CUresult r = fn(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank,
+                    const_cast<void*>(base), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(SA_ERR_TMA, "tensor map for %s: error %d", what, (int)r);
+    return SA_OK;
 }
 
 inline int encode3d(CUtensorMap* map, bool fp8, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,

@@ -73,6 +73,87 @@ struct Cfg {
 #endif
 constexpr int TILE_EXP_POLY = SA_TILE_EXP_POLY;
 
+// Paged K/V (BF16 kernel).  Page id of box `lane` of the 64-key tile at kb (0 for lanes past the
+// tile's boxes or boxes past the last key; an id outside [0, num_pages) sets SA_DEV_BAD_PAGE and
+// reads as zeros, through TMA's bounds or the guarded plain loads).
+__device__ __forceinline__ int box_page(const Params& p, int kb, int lane) {
+    const int key0 = kb + lane * p.box_rows;
+    if (lane >= 64 / p.box_rows || key0 >= p.kv_len) return 0;
+    return __ldg(p.pages + key0 / p.page);
+}
+
+// One K/V stage of a paged cache: box i of the tile (keys kb + i * box_rows ..) is a 4D TMA load
+// from page pages[key / page] at slot key % page, or an out-of-range page coordinate (zero fill)
+// when the box starts at or past kv_len.  The box that holds the last key when kv_len ends inside
+// it is read by the warp's lanes with plain loads instead (rows past kv_len written as zeros, as
+// TMA's bounds would give a contiguous K/V), stored at the 128-byte-swizzled places TMA would use
+// (16-byte chunk c of tile row R at chunk c ^ (R % 8) of the row), then fenced for the tensor
+// cores before the stage barrier is armed with the remaining bytes.
+template <class C>
+__device__ __forceinline__ void load_paged_stage(const Params& p, uint8_t* dst, uint32_t full, const CUtensorMap* tmK,
+                                                 const CUtensorMap* tmV, int kb, int hk, int lane, int my_page,
+                                                 volatile int* kb_slot) {
+    static_assert(C::E == 2, "paged stages are bf16");
+    const int br = p.box_rows;
+    const int nbox = 64 / br;
+    const bool bad = static_cast<unsigned>(my_page) >= static_cast<unsigned>(p.num_pages);
+    if (__any_sync(0xffffffffu, bad) && lane == 0 && p.status) atomicOr(p.status, SA_DEV_BAD_PAGE);
+    if (bad) my_page = p.num_pages;                          // TMA: out of range, zero fill
+    int pg[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pg[i] = __shfl_sync(0xffffffffu, my_page, i);
+    const int last0 = ((p.kv_len - 1) / br) * br;           // first key of the box holding the last key
+    const int tail = (p.kv_len % br != 0 && last0 >= kb && last0 < kb + 64) ? (last0 - kb) / br : -1;
+    uint32_t tail_bytes = 0;
+    if (tail >= 0) {
+        int tp = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) if (i == tail) tp = pg[i];
+        const bool tp_ok = tp < p.num_pages;
+        const int valid = p.kv_len - last0;
+        const int slot0 = last0 % p.page;
+        const int chunks = br * 16;                          // 16-byte chunks of the box's K rows (and V rows)
+        for (int i = lane; i < 2 * chunks; i += 32) {
+            const bool isv = i >= chunks;
+            const int ii = isv ? i - chunks : i;
+            const int rr = ii >> 4, c = ii & 15;
+            const int R = tail * br + rr;                    // row of the 64-key tile
+            uint4 val = make_uint4(0u, 0u, 0u, 0u);
+            if (rr < valid && tp_ok) {
+                const uint16_t* base = isv ? p.vc : p.kc;
+                val = *reinterpret_cast<const uint4*>(base + static_cast<int64_t>(tp) * p.kv_ps +
+                                                      static_cast<int64_t>(slot0 + rr) * p.kv_rs +
+                                                      static_cast<int64_t>(hk) * p.kv_hs + c * 8);
+            }
+            const int reg = c >> 3, cc = c & 7;
+            uint8_t* d = dst + (isv ? C::K_BYTES + reg * C::V_REG : reg * C::K_REG) + R * 128 + ((cc ^ (R & 7)) << 4);
+            *reinterpret_cast<uint4*>(d) = val;
+        }
+        fence_proxy_async_smem();
+        tail_bytes = static_cast<uint32_t>(2 * br * 256);
+    }
+    __syncwarp();
+    if (elect_one()) {
+        *kb_slot = kb;
+        mbar_arrive_expect_tx(full, C::STAGE - tail_bytes);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (i >= nbox) break;
+            if (i == tail) continue;
+            const int key0 = kb + i * br;
+            const bool past = key0 >= p.kv_len;
+            const int page = past ? p.num_pages : pg[i];
+            const int slot = past ? 0 : key0 % p.page;
+            for (int r = 0; r < C::NREG; ++r) {
+                tma_load_4d(smem_u32(dst + r * C::K_REG + i * br * 128), tmK, full, r * C::REG_ELEMS, hk, slot, page);
+                tma_load_4d(smem_u32(dst + C::K_BYTES + r * C::V_REG + i * br * 128), tmV, full, r * C::REG_ELEMS, hk,
+                            slot, page);
+            }
+        }
+    }
+    __syncwarp();
+}
+
 template <bool FP8>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                           const __grid_constant__ CUtensorMap tmK,
@@ -148,8 +229,13 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                     tma_load_3d(smem_u32(sQ + r * C::Q_REG), &tmQ, smem_u32(bQ), r * C::REG_ELEMS, h, qrow0);
             }
             __syncwarp();
+            bool paged = false;
+            if constexpr (!FP8) paged = p.pages != nullptr;
             for (int t = 0;; ++t, have = w.next(kb, rm)) {
                 const int st = t % C::NST;
+                // paged K/V: lane i fetches the page id of the tile's box i while the stage drains
+                int my_page = 0;
+                if (paged && have) my_page = box_page(p, kb, lane);
                 if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bEmpty + st), ((t / C::NST) & 1) ^ 1, abort_flag,
                                                         p.status, SA_DEV_WAIT_KV)))
                     break;
@@ -162,6 +248,15 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                     break;
                 }
                 uint8_t* dst = sKV + st * C::STAGE;
+                if constexpr (!FP8) {
+                    if (paged) {
+                        load_paged_stage<C>(p, dst, smem_u32(bFull + st), &tmK, &tmV, kb, hk, lane, my_page,
+                                            tile_kb + st);
+                        par[st] = (t / C::NST) & 1;
+                        used[st] = true;
+                        continue;
+                    }
+                }
                 if (elect_one()) {
                     tile_kb[st] = kb;
                     mbar_arrive_expect_tx(smem_u32(bFull + st), C::STAGE);
@@ -453,14 +548,22 @@ bool use_pair_kernel() {
     return pair;
 }
 
+// A paged K/V cache (BF16 kernel): k and v are the cache bases, krs/khs (= vrs/vhs) the slot and
+// head strides, page_stride the element stride between pages.
+struct PagedKV {
+    const int32_t* pages;
+    int page, num_pages;
+    int64_t page_stride;
+};
+
 template <bool FP8>
 int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t krs, int64_t khs, const void* v,
                 int64_t vrs, int64_t vhs, void* out, int64_t ors, int64_t ohs, int n_q, int H, int Hk, int D, int kv_len,
                 int q_front, int q_offset, const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block,
                 int kv_block, const float* qsc, int qss, const float* ksc, int kss, const float* vsc, int vss,
-                float softmax_scale, int32_t* status, cudaStream_t stream) {
+                float softmax_scale, int32_t* status, cudaStream_t stream, const PagedKV* paged = nullptr) {
     using C = Cfg<FP8>;
-    const char* name = FP8 ? "sa_attn_fwd_fp8" : "sa_attn_fwd_bf16";
+    const char* name = paged ? "sa_attn_fwd_bf16_paged" : FP8 ? "sa_attn_fwd_fp8" : "sa_attn_fwd_bf16";
     if (D != 128) return fail(SA_ERR_UNSUPPORTED, "%s: head_dim %d (only 128)", name, D);
     if (n_q < 0 || H <= 0 || Hk <= 0 || H % Hk || kv_len <= 0 || q_front < 0 || q_front >= 128 || q_offset < 0)
         return fail(SA_ERR_ARG, "%s: bad sizes", name);
@@ -476,15 +579,46 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     if (!a16(q) || !a16(k) || !a16(v) || !a16(out) || (qrs * E) % 16 || (qhs * E) % 16 || (krs * E) % 16 ||
         (khs * E) % 16 || (vrs * E) % 16 || (vhs * E) % 16 || (ors * 2) % 16 || (ohs * 2) % 16)
         return fail(SA_ERR_ALIGN, "%s: pointers must be 16-byte aligned and strides multiples of 16 bytes", name);
+    int box_rows = 0;
+    if (paged) {
+        if (FP8) return fail(SA_ERR_UNSUPPORTED, "%s: paged K/V is bf16 only", name);
+        if (!paged->pages || paged->num_pages <= 0) return fail(SA_ERR_ARG, "%s: page table and num_pages > 0 required", name);
+        if (paged->page <= 0 || !(paged->page % 64 == 0 || paged->page == 8 || paged->page == 16 || paged->page == 32))
+            return fail(SA_ERR_UNSUPPORTED, "%s: page_size %d (8, 16, 32 or a multiple of 64)", name, paged->page);
+        if ((paged->page_stride * E) % 16 || krs != vrs || khs != vhs)
+            return fail(SA_ERR_ALIGN, "%s: page stride multiple of 16 bytes, K and V with the same strides", name);
+        box_rows = std::min(paged->page, 64);
+    }
     if (n_q == 0) return SA_OK;
     const int n_tiles = (q_front + n_q + 127) / 128;
     CUtensorMap tmQ, tmK, tmV;
     int rc;
     const CUtensorMapSwizzle sw128 = CU_TENSOR_MAP_SWIZZLE_128B;
     if ((rc = encode3d(&tmQ, FP8, q, D, H, n_q > 0 ? n_q : 1, qhs * E, qrs * E, C::REG_ELEMS, 1, 128, sw128, "q"))) return rc;
-    if ((rc = encode3d(&tmK, FP8, k, D, Hk, kv_len, khs * E, krs * E, C::REG_ELEMS, 1, C::BN, sw128, "k"))) return rc;
-    if ((rc = encode3d(&tmV, FP8, v, D, Hk, kv_len, vhs * E, vrs * E, C::REG_ELEMS, 1, C::BN, sw128, "v"))) return rc;
-    Params p;
+    if (paged) {
+        const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Hk), static_cast<uint64_t>(paged->page),
+                                  static_cast<uint64_t>(paged->num_pages)};
+        const uint64_t strides[3] = {static_cast<uint64_t>(khs * E), static_cast<uint64_t>(krs * E),
+                                     static_cast<uint64_t>(paged->page_stride * E)};
+        const uint32_t box[4] = {static_cast<uint32_t>(C::REG_ELEMS), 1u, static_cast<uint32_t>(box_rows), 1u};
+        if ((rc = encode_nd(&tmK, FP8, k, 4, dims, strides, box, sw128, "k pages"))) return rc;
+        if ((rc = encode_nd(&tmV, FP8, v, 4, dims, strides, box, sw128, "v pages"))) return rc;
+    } else {
+        if ((rc = encode3d(&tmK, FP8, k, D, Hk, kv_len, khs * E, krs * E, C::REG_ELEMS, 1, C::BN, sw128, "k"))) return rc;
+        if ((rc = encode3d(&tmV, FP8, v, D, Hk, kv_len, vhs * E, vrs * E, C::REG_ELEMS, 1, C::BN, sw128, "v"))) return rc;
+    }
+    Params p{};
+    if (paged) {
+        p.pages = paged->pages;
+        p.page = paged->page;
+        p.box_rows = box_rows;
+        p.num_pages = paged->num_pages;
+        p.kc = static_cast<const uint16_t*>(k);
+        p.vc = static_cast<const uint16_t*>(v);
+        p.kv_ps = paged->page_stride;
+        p.kv_rs = krs;
+        p.kv_hs = khs;
+    }
     p.counts = counts;
     p.lists = lists;
     p.list_stride = list_stride;
@@ -546,6 +680,20 @@ extern "C" int sa_attn_fwd_fp8(const uint8_t* q, int64_t q_row_stride, int64_t q
                                  kv_len, q_front, q_offset, counts, lists, list_stride, q_block, kv_block, q_scale,
                                  q_scale_stride, k_scale, k_scale_stride, v_scale, v_scale_stride, softmax_scale, status,
                                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sa_attn_fwd_bf16_paged(const void* q, int64_t q_row_stride, int64_t q_head_stride, const void* k_cache,
+                                      const void* v_cache, int64_t page_stride, int64_t row_stride, int64_t head_stride,
+                                      const int32_t* page_table, int page_size, int num_pages, void* out,
+                                      int64_t o_row_stride, int64_t o_head_stride, int n_q, int num_heads,
+                                      int num_kv_heads, int head_dim, int kv_len, int q_front, int q_offset,
+                                      const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block,
+                                      int kv_block, float softmax_scale, int32_t* status, void* stream) {
+    const sa::PagedKV pg{page_table, page_size, num_pages, page_stride};
+    return sa::launch_attn<false>(q, q_row_stride, q_head_stride, k_cache, row_stride, head_stride, v_cache, row_stride,
+                                  head_stride, out, o_row_stride, o_head_stride, n_q, num_heads, num_kv_heads, head_dim,
+                                  kv_len, q_front, q_offset, counts, lists, list_stride, q_block, kv_block, nullptr, 0,
+                                  nullptr, 0, nullptr, 0, softmax_scale, status, static_cast<cudaStream_t>(stream), &pg);
 }
 
 extern "C" int sa_attn_fwd_bf16(const void* q, int64_t q_row_stride, int64_t q_head_stride, const void* k,

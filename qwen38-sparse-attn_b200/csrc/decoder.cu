@@ -80,55 +80,155 @@ __global__ void __launch_bounds__(128) add_rmsnorm_kernel(const uint16_t* __rest
     }
 }
 
-// Neox-style rotary embedding: element i < D/2 pairs with i + D/2 at angle pos * theta^(-2i/D);
-// cos_sin[pos] holds cos of the D/2 angles then their sin (fp32).  One thread per 8 pairs of one
-// head of one row; q heads go to q_out [rows, Hq, D], k heads (rotated) and v heads (copied) to the
-// cache rows.
-__global__ void __launch_bounds__(256) rope_qkv_kernel(const uint16_t* __restrict__ qkv, int64_t qkv_stride, int rows,
-                                                       int hq, int hk, int D, const float* __restrict__ cos_sin,
-                                                       int pos0, uint16_t* __restrict__ q_out,
-                                                       uint16_t* __restrict__ k_out, int64_t k_stride,
-                                                       uint16_t* __restrict__ v_out, int64_t v_stride) {
-    const int jn = D / 16;                                        // 8-pair groups per head
-    const int heads = hq + 2 * hk;
-    const int64_t total = static_cast<int64_t>(rows) * heads * jn;
-    const int half = D / 2;
-    for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+// Neox-style rotary embedding of 8 pairs: elements 8j..8j+7 (a) pair with half+8j.. (b) at the
+// angles of position row cs (cos_sin[pos] holds cos of the D/2 angles then their sin, fp32).
+__device__ __forceinline__ void rope8(const uint4 a, const uint4 b, const float* __restrict__ cs, int j, int half,
+                                      uint4& oa, uint4& ob) {
+    const float4 c0 = __ldg(reinterpret_cast<const float4*>(cs + 8 * j));
+    const float4 c1 = __ldg(reinterpret_cast<const float4*>(cs + 8 * j + 4));
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(cs + half + 8 * j));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(cs + half + 8 * j + 4));
+    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float x1[8], x2[8], y1[8], y2[8];
+    bf16x8_to_f32(a, x1);
+    bf16x8_to_f32(b, x2);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        y1[e] = x1[e] * c[e] - x2[e] * s[e];
+        y2[e] = x2[e] * c[e] + x1[e] * s[e];
+    }
+    oa = f32_to_bf16x8(y1);
+    ob = f32_to_bf16x8(y2);
+}
+
+struct RopeArgs {
+    const uint16_t* qkv;
+    int64_t qkv_stride;
+    int rows, hq, hk, D, pos0;
+    const float* cos_sin;
+    uint16_t* q_out;
+    uint16_t* k_out;
+    int64_t k_stride;
+    uint16_t* v_out;
+    int64_t v_stride;
+    // key block means of the rotated k rows (kctas > 0): CTAs [0, kctas) = nblk key blocks x nhg
+    // groups of hpc KV heads, rg row groups (block_means_shape); km[h, b - km_block0, :]
+    int kctas, nhg, hpc, rg, block, b0;
+    float* km;
+    int64_t km_hs, km_bs;
+    int km_block0;
+};
+
+// One launch: rotary embedding of the q and k heads of qkv rows (positions pos0 + row), q to q_out
+// [rows, Hq, D], rotated k and copied v to the cache rows.  With kctas > 0 the k heads are done by
+// CTAs [0, kctas) that also write the key block means: CTA (b, head group) owns the rows of block b
+// within [pos0, pos0 + rows); thread (head, pair group j, row group g) rotates rows lo+g, lo+g+rg, ...
+// and sums the bf16 results in that order; the rg partial sums are then added in group order and
+// divided by the row count.  That is block_means_kernel's order for the same launch shape, so the
+// means equal sa_block_means_bf16's over the written k rows bit for bit.  The remaining CTAs rotate
+// the q heads (and the k heads when kctas == 0) and copy the v heads, grid-strided, one thread per
+// 8 pairs of one head of one row.
+__global__ void __launch_bounds__(256) rope_qkv_kernel(const RopeArgs a) {
+    const int D = a.D, half = D / 2, jn = D / 16;
+    if (static_cast<int>(blockIdx.x) < a.kctas) {
+        extern __shared__ float partial[];                       // [rg - 1][threads in use][16]
+        const int txp = a.hpc * jn;
+        const int tid = threadIdx.x, tx = tid % txp, ty = tid / txp;
+        const int used = txp * a.rg;
+        const int hl = tx / jn, j = tx - hl * jn;
+        const int b = a.b0 + static_cast<int>(blockIdx.x) / a.nhg;
+        const int h = (static_cast<int>(blockIdx.x) % a.nhg) * a.hpc + hl;
+        const bool active = tid < used && h < a.hk;
+        const int lo = max(a.pos0, b * a.block) - a.pos0;
+        const int hi = min(a.pos0 + a.rows, (b + 1) * a.block) - a.pos0;
+        float acc[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+        if (active) {
+            const uint16_t* src = a.qkv + static_cast<int64_t>(a.hq + h) * D;
+            uint16_t* dst = a.k_out + static_cast<int64_t>(h) * D;
+            constexpr int BATCH = 4;
+            for (int base = lo + ty; base < hi; base += BATCH * a.rg) {
+                uint4 va[BATCH], vb[BATCH];
+#pragma unroll
+                for (int k = 0; k < BATCH; ++k) {
+                    const int r = base + k * a.rg;
+                    if (r < hi) {
+                        const uint16_t* row = src + static_cast<int64_t>(r) * a.qkv_stride;
+                        va[k] = *reinterpret_cast<const uint4*>(row + 8 * j);
+                        vb[k] = *reinterpret_cast<const uint4*>(row + half + 8 * j);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < BATCH; ++k) {
+                    const int r = base + k * a.rg;
+                    if (r >= hi) break;
+                    uint4 oa, ob;
+                    rope8(va[k], vb[k], a.cos_sin + static_cast<int64_t>(a.pos0 + r) * D, j, half, oa, ob);
+                    uint16_t* drow = dst + static_cast<int64_t>(r) * a.k_stride;
+                    *reinterpret_cast<uint4*>(drow + 8 * j) = oa;
+                    *reinterpret_cast<uint4*>(drow + half + 8 * j) = ob;
+                    float f[8];
+                    bf16x8_to_f32(oa, f);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[i] += f[i];
+                    bf16x8_to_f32(ob, f);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[8 + i] += f[i];
+                }
+            }
+        }
+        if (a.rg > 1) {
+            if (active && ty > 0) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) partial[((ty - 1) * txp + tx) * 16 + i] = acc[i];
+            }
+            __syncthreads();
+            if (ty != 0) return;
+            for (int g = 1; g < a.rg; ++g) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) acc[i] += partial[((g - 1) * txp + tx) * 16 + i];
+            }
+        }
+        if (!active) return;
+        const float cnt = static_cast<float>(max(hi - lo, 1));
+        float* o = a.km + static_cast<int64_t>(h) * a.km_hs + static_cast<int64_t>(b - a.km_block0) * a.km_bs;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            o[8 * j + i] = __fdiv_rn(acc[i], cnt);
+            o[half + 8 * j + i] = __fdiv_rn(acc[8 + i], cnt);
+        }
+        return;
+    }
+    const int nk = a.kctas ? 0 : a.hk;                           // k heads rotated here
+    const int heads = a.hq + nk + a.hk;
+    const int64_t total = static_cast<int64_t>(a.rows) * heads * jn;
+    const int64_t first = (static_cast<int64_t>(blockIdx.x) - a.kctas) * blockDim.x + threadIdx.x;
+    const int64_t stride = static_cast<int64_t>(gridDim.x - a.kctas) * blockDim.x;
+    for (int64_t idx = first; idx < total; idx += stride) {
         const int j = static_cast<int>(idx % jn);
         const int64_t rest = idx / jn;
         const int hh = static_cast<int>(rest % heads);
         const int row = static_cast<int>(rest / heads);
-        const uint16_t* src = qkv + static_cast<int64_t>(row) * qkv_stride + static_cast<int64_t>(hh) * D;
-        const uint4 a = *reinterpret_cast<const uint4*>(src + 8 * j);
-        const uint4 b = *reinterpret_cast<const uint4*>(src + half + 8 * j);
-        uint4 oa = a, ob = b;
-        if (hh < hq + hk) {
-            const float* cs = cos_sin + static_cast<int64_t>(pos0 + row) * D;
-            const float4 c0 = __ldg(reinterpret_cast<const float4*>(cs + 8 * j));
-            const float4 c1 = __ldg(reinterpret_cast<const float4*>(cs + 8 * j + 4));
-            const float4 s0 = __ldg(reinterpret_cast<const float4*>(cs + half + 8 * j));
-            const float4 s1 = __ldg(reinterpret_cast<const float4*>(cs + half + 8 * j + 4));
-            const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-            const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-            float x1[8], x2[8], y1[8], y2[8];
-            bf16x8_to_f32(a, x1);
-            bf16x8_to_f32(b, x2);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                y1[e] = x1[e] * c[e] - x2[e] * s[e];
-                y2[e] = x2[e] * c[e] + x1[e] * s[e];
-            }
-            oa = f32_to_bf16x8(y1);
-            ob = f32_to_bf16x8(y2);
-        }
         uint16_t* dst;
-        if (hh < hq)
-            dst = q_out + (static_cast<int64_t>(row) * hq + hh) * D;
-        else if (hh < hq + hk)
-            dst = k_out + static_cast<int64_t>(row) * k_stride + static_cast<int64_t>(hh - hq) * D;
-        else
-            dst = v_out + static_cast<int64_t>(row) * v_stride + static_cast<int64_t>(hh - hq - hk) * D;
+        int src_head;
+        if (hh < a.hq) {
+            dst = a.q_out + (static_cast<int64_t>(row) * a.hq + hh) * D;
+            src_head = hh;
+        } else if (hh < a.hq + nk) {
+            dst = a.k_out + static_cast<int64_t>(row) * a.k_stride + static_cast<int64_t>(hh - a.hq) * D;
+            src_head = hh;
+        } else {
+            const int hv = hh - a.hq - nk;
+            dst = a.v_out + static_cast<int64_t>(row) * a.v_stride + static_cast<int64_t>(hv) * D;
+            src_head = a.hq + a.hk + hv;
+        }
+        const uint16_t* src = a.qkv + static_cast<int64_t>(row) * a.qkv_stride + static_cast<int64_t>(src_head) * D;
+        const uint4 va = *reinterpret_cast<const uint4*>(src + 8 * j);
+        const uint4 vb = *reinterpret_cast<const uint4*>(src + half + 8 * j);
+        uint4 oa = va, ob = vb;
+        if (hh < a.hq + nk) rope8(va, vb, a.cos_sin + static_cast<int64_t>(a.pos0 + row) * D, j, half, oa, ob);
         *reinterpret_cast<uint4*>(dst + 8 * j) = oa;
         *reinterpret_cast<uint4*>(dst + half + 8 * j) = ob;
     }
@@ -193,23 +293,79 @@ extern "C" int sa_add_rmsnorm_bf16(const void* delta, int64_t delta_row_stride, 
     return check_launch("add_rmsnorm_kernel");
 }
 
+namespace sa {
+namespace {
+
+int rope_qkv(const char* who, const void* qkv, int64_t qkv_row_stride, int rows, int num_heads, int num_kv_heads,
+             int head_dim, const float* cos_sin, int pos0, int max_pos, void* q_out, void* k_out, int64_t k_row_stride,
+             void* v_out, int64_t v_row_stride, int block, float* km, int64_t km_head_stride, int64_t km_block_stride,
+             int km_block0, void* stream) {
+    if (rows < 0 || num_heads <= 0 || num_kv_heads <= 0 || pos0 < 0) return fail(SA_ERR_ARG, "%s: bad sizes", who);
+    if (head_dim % 16 || head_dim > 8 * 256)
+        return fail(SA_ERR_UNSUPPORTED, "%s: head_dim %d not a multiple of 16 (<= 2048)", who, head_dim);
+    if (pos0 + rows > max_pos) return fail(SA_ERR_ARG, "%s: positions %d.. beyond the table (%d)", who, pos0, max_pos);
+    if (!qkv || !cos_sin || !q_out || !k_out || !v_out) return fail(SA_ERR_ARG, "%s: null pointer", who);
+    if (!aligned16(qkv) || !aligned16(cos_sin) || !aligned16(q_out) || !aligned16(k_out) || !aligned16(v_out) ||
+        qkv_row_stride % 8 || k_row_stride % 8 || v_row_stride % 8)
+        return fail(SA_ERR_ALIGN, "%s: tensors must be 16-byte aligned with row strides %% 8 == 0", who);
+    RopeArgs a{};
+    a.qkv = static_cast<const uint16_t*>(qkv);
+    a.qkv_stride = qkv_row_stride;
+    a.rows = rows;
+    a.hq = num_heads;
+    a.hk = num_kv_heads;
+    a.D = head_dim;
+    a.pos0 = pos0;
+    a.cos_sin = cos_sin;
+    a.q_out = static_cast<uint16_t*>(q_out);
+    a.k_out = static_cast<uint16_t*>(k_out);
+    a.k_stride = k_row_stride;
+    a.v_out = static_cast<uint16_t*>(v_out);
+    a.v_stride = v_row_stride;
+    size_t smem = 0;
+    if (km) {
+        if (block <= 0) return fail(SA_ERR_ARG, "%s: block %d", who, block);
+        const int b0 = pos0 / block, b1 = (pos0 + rows + block - 1) / block;
+        if (b0 < km_block0) return fail(SA_ERR_ARG, "%s: first block %d < km_block0 %d", who, b0, km_block0);
+        if (rows > 0) {
+            block_means_shape(b1 - b0, num_kv_heads, head_dim, block, &a.hpc, &a.rg);
+            a.nhg = (num_kv_heads + a.hpc - 1) / a.hpc;
+            a.kctas = (b1 - b0) * a.nhg;
+            a.block = block;
+            a.b0 = b0;
+            a.km = km;
+            a.km_hs = km_head_stride;
+            a.km_bs = km_block_stride;
+            a.km_block0 = km_block0;
+            smem = static_cast<size_t>(a.rg - 1) * a.hpc * (head_dim / 16) * 16 * sizeof(float);   // <= 15.5 KB
+        }
+    }
+    if (rows == 0) return SA_OK;
+    const int64_t work = static_cast<int64_t>(rows) * (num_heads + (a.kctas ? 0 : num_kv_heads) + num_kv_heads) *
+                         (head_dim / 16);
+    rope_qkv_kernel<<<a.kctas + grid_for(work, 256), 256, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    return check_launch("rope_qkv_kernel");
+}
+
+}  // namespace
+}  // namespace sa
+
 extern "C" int sa_rope_qkv_bf16(const void* qkv, int64_t qkv_row_stride, int rows, int num_heads, int num_kv_heads,
                                 int head_dim, const float* cos_sin, int pos0, int max_pos, void* q_out, void* k_out,
                                 int64_t k_row_stride, void* v_out, int64_t v_row_stride, void* stream) {
-    if (rows < 0 || num_heads <= 0 || num_kv_heads <= 0 || pos0 < 0) return fail(SA_ERR_ARG, "sa_rope_qkv_bf16: bad sizes");
-    if (head_dim % 16) return fail(SA_ERR_UNSUPPORTED, "sa_rope_qkv_bf16: head_dim %d not a multiple of 16", head_dim);
-    if (pos0 + rows > max_pos) return fail(SA_ERR_ARG, "sa_rope_qkv_bf16: positions %d.. beyond the table (%d)", pos0, max_pos);
-    if (!qkv || !cos_sin || !q_out || !k_out || !v_out) return fail(SA_ERR_ARG, "sa_rope_qkv_bf16: null pointer");
-    if (!aligned16(qkv) || !aligned16(cos_sin) || !aligned16(q_out) || !aligned16(k_out) || !aligned16(v_out) ||
-        qkv_row_stride % 8 || k_row_stride % 8 || v_row_stride % 8)
-        return fail(SA_ERR_ALIGN, "sa_rope_qkv_bf16: tensors must be 16-byte aligned with row strides %% 8 == 0");
-    if (rows == 0) return SA_OK;
-    const int64_t work = static_cast<int64_t>(rows) * (num_heads + 2 * num_kv_heads) * (head_dim / 16);
-    rope_qkv_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint16_t*>(qkv), qkv_row_stride, rows, num_heads, num_kv_heads, head_dim, cos_sin, pos0,
-        static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_out), k_row_stride, static_cast<uint16_t*>(v_out),
-        v_row_stride);
-    return check_launch("rope_qkv_kernel");
+    return rope_qkv("sa_rope_qkv_bf16", qkv, qkv_row_stride, rows, num_heads, num_kv_heads, head_dim, cos_sin, pos0,
+                    max_pos, q_out, k_out, k_row_stride, v_out, v_row_stride, 0, nullptr, 0, 0, 0, stream);
+}
+
+extern "C" int sa_rope_qkv_means_bf16(const void* qkv, int64_t qkv_row_stride, int rows, int num_heads,
+                                      int num_kv_heads, int head_dim, const float* cos_sin, int pos0, int max_pos,
+                                      void* q_out, void* k_out, int64_t k_row_stride, void* v_out,
+                                      int64_t v_row_stride, int block, float* km, int64_t km_head_stride,
+                                      int64_t km_block_stride, int km_block0, void* stream) {
+    if (!km) return fail(SA_ERR_ARG, "sa_rope_qkv_means_bf16: null km");
+    return rope_qkv("sa_rope_qkv_means_bf16", qkv, qkv_row_stride, rows, num_heads, num_kv_heads, head_dim, cos_sin,
+                    pos0, max_pos, q_out, k_out, k_row_stride, v_out, v_row_stride, block, km, km_head_stride,
+                    km_block_stride, km_block0, stream);
 }
 
 extern "C" int sa_silu_mul_bf16(const void* gate_up, int64_t gate_up_row_stride, int rows, int inter, void* out,

@@ -11,7 +11,8 @@ namespace {
 // One CTA per (block b, group of heads).  threadIdx.x -> (head in group, 16-byte column chunk),
 // threadIdx.y -> row group: rows lo+ty, lo+ty+RG, ... are summed in order by each thread and the
 // RG partial sums are added in row-group order (RG = 1 gives a strictly sequential row sum).
-__global__ void __launch_bounds__(512, 2) block_means_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64_t xhs, int n, int heads,
+// Row r of x is at rm.offset(r, xrs) (contiguous, or a paged cache with rm.row0 = pos0).
+__global__ void __launch_bounds__(512, 2) block_means_kernel(const uint16_t* __restrict__ x, RowMap rm, int64_t xrs, int64_t xhs, int n, int heads,
                                    int D, int pos0, int block, int b0, int heads_per_cta, float* __restrict__ out,
                                    int64_t ohs, int64_t obs, int out_block0, uint8_t* __restrict__ q8,
                                    int64_t q8rs, int64_t q8hs, const float* __restrict__ inv_scale, int iss,
@@ -43,7 +44,7 @@ __global__ void __launch_bounds__(512, 2) block_means_kernel(const uint16_t* __r
 #pragma unroll
             for (int k = 0; k < BATCH; ++k) {
                 const int r = base + k * RG;
-                v[k] = r < hi ? ld_stream(src + static_cast<int64_t>(r) * xrs) : make_uint4(0u, 0u, 0u, 0u);
+                v[k] = r < hi ? ld_stream(src + rm.offset(r, xrs)) : make_uint4(0u, 0u, 0u, 0u);
             }
 #pragma unroll
             for (int k = 0; k < BATCH; ++k) {
@@ -84,8 +85,9 @@ __global__ void __launch_bounds__(512, 2) block_means_kernel(const uint16_t* __r
 
 // Elementwise e4m3 quantisation, row-major output.  threadIdx.x (with blockIdx.y) picks a 16-byte
 // column chunk hc = (head, 8 elements) of the row, fixed for the thread; rows are walked in
-// batches of 8 blockDim.y apart, all 8 loads issued before the first is used.
-__global__ void __launch_bounds__(256) quant_rows_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64_t xhs,
+// batches of 8 blockDim.y apart, all 8 loads issued before the first is used.  Row r of x is at
+// rm.offset(r, xrs) (contiguous or paged).
+__global__ void __launch_bounds__(256) quant_rows_kernel(const uint16_t* __restrict__ x, RowMap rm, int64_t xrs, int64_t xhs,
                                                          int rows, int heads, int D, const float* __restrict__ scale,
                                                          int iss, int mode, uint8_t* __restrict__ out, int64_t ors,
                                                          int64_t ohs) {
@@ -103,7 +105,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const uint16_t* __restr
 #pragma unroll
             for (int k = 0; k < BATCH; ++k) {
                 const int r = r0 + k * static_cast<int>(blockDim.y);
-                v[k] = r < rows ? ld_stream(src + static_cast<int64_t>(r) * xrs) : make_uint4(0u, 0u, 0u, 0u);
+                v[k] = r < rows ? ld_stream(src + rm.offset(r, xrs)) : make_uint4(0u, 0u, 0u, 0u);
             }
 #pragma unroll
             for (int k = 0; k < BATCH; ++k) {
@@ -161,8 +163,8 @@ __global__ void transpose_kernel(const uint16_t* __restrict__ x, int64_t xrs, in
     }
 }
 
-__global__ void absmax_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64_t xhs, int rows, int heads, int D,
-                              int per_head, float* __restrict__ out) {
+__global__ void absmax_kernel(const uint16_t* __restrict__ x, RowMap rm, int64_t xrs, int64_t xhs, int rows, int heads,
+                              int D, int per_head, float* __restrict__ out) {
     // grid.y = head; grid.x strides over rows
     const int h = blockIdx.y;
     const int cols = D >> 3;
@@ -171,7 +173,7 @@ __global__ void absmax_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t r = i / cols;
         const int c = static_cast<int>(i - r * cols);
-        const uint4 v = ld_stream(x + r * xrs + static_cast<int64_t>(h) * xhs + c * 8);
+        const uint4 v = ld_stream(x + rm.offset(static_cast<int>(r), xrs) + static_cast<int64_t>(h) * xhs + c * 8);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -187,6 +189,81 @@ __global__ void absmax_kernel(const uint16_t* __restrict__ x, int64_t xrs, int64
 }  // namespace
 }  // namespace sa
 
+namespace sa {
+namespace {
+
+int check_pages(const char* who, const int32_t* pages, int page, int64_t page_stride) {
+    if (!pages || page <= 0) return fail(SA_ERR_ARG, "%s: page table and page_size > 0 required", who);
+    if (page_stride % 8) return fail(SA_ERR_ALIGN, "%s: page_stride %% 8 != 0", who);
+    return SA_OK;
+}
+
+int block_means(const char* who, const void* x, RowMap rm, int64_t x_row_stride, int64_t x_head_stride, int n,
+                int heads, int head_dim, int pos0, int block, float* out, int64_t out_head_stride,
+                int64_t out_block_stride, int out_block0, uint8_t* q8, int64_t q8_row_stride, int64_t q8_head_stride,
+                const float* inv_scale, int inv_scale_stride, int fixed_divisor, void* stream) {
+    if (n < 0 || heads <= 0 || block <= 0 || pos0 < 0) return fail(SA_ERR_ARG, "%s: bad sizes", who);
+    if (head_dim % 8 || head_dim > 8 * 256) return fail(SA_ERR_UNSUPPORTED, "%s: head_dim %d", who, head_dim);
+    if (!x || !out) return fail(SA_ERR_ARG, "%s: null pointer", who);
+    if (!aligned16(x) || x_row_stride % 8 || x_head_stride % 8)
+        return fail(SA_ERR_ALIGN, "%s: x must be 16-byte aligned with strides %% 8 == 0", who);
+    if (q8 && (!inv_scale || (reinterpret_cast<uintptr_t>(q8) & 7) || q8_row_stride % 8 || q8_head_stride % 8))
+        return fail(SA_ERR_ALIGN, "%s: q8 needs inv_scale, 8-byte alignment, strides %% 8 == 0", who);
+    if (n == 0) return SA_OK;
+    const int b0 = pos0 / block;
+    const int b1 = (pos0 + n + block - 1) / block;
+    if (b0 < out_block0) return fail(SA_ERR_ARG, "%s: first block %d < out_block0 %d", who, b0, out_block0);
+    const int nblk = b1 - b0;
+    int hpc, rg;
+    block_means_shape(nblk, heads, head_dim, block, &hpc, &rg);
+    const int tx = hpc * (head_dim / 8);
+    const int nhg = (heads + hpc - 1) / hpc;
+    dim3 grid(nblk, nhg), blk(tx, rg);
+    const size_t smem = rg > 1 ? static_cast<size_t>(rg - 1) * tx * 8 * sizeof(float) : 0;   // <= 15.5 KB
+    block_means_kernel<<<grid, blk, smem, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(x), rm, x_row_stride, x_head_stride, n, heads, head_dim, pos0, block, b0, hpc,
+        out, out_head_stride, out_block_stride, out_block0, q8, q8_row_stride, q8_head_stride, inv_scale,
+        inv_scale_stride, fixed_divisor);
+    return check_launch("block_means_kernel");
+}
+
+int quantize_rows(const char* who, const void* x, RowMap rm, int64_t x_row_stride, int64_t x_head_stride, int rows,
+                  int heads, int head_dim, const float* scale, int scale_stride, int mode, uint8_t* out,
+                  int64_t out_row_stride, int64_t out_head_stride, cudaStream_t s) {
+    if ((reinterpret_cast<uintptr_t>(out) & 7) || out_row_stride % 8 || out_head_stride % 8)
+        return fail(SA_ERR_ALIGN, "%s: out must be 8-byte aligned with strides %% 8 == 0", who);
+    if (rows == 0) return SA_OK;
+    const int HC = heads * (head_dim / 8);
+    const int bx = std::min(HC, 128);
+    const dim3 blk(bx, 256 / bx);
+    const int gy = (HC + bx - 1) / bx;
+    const int per_cta = static_cast<int>(blk.y) * 8;
+    const int gx = std::max(1, std::min((rows + per_cta - 1) / per_cta, (8 * num_sms() + gy - 1) / gy));
+    quant_rows_kernel<<<dim3(gx, gy), blk, 0, s>>>(static_cast<const uint16_t*>(x), rm, x_row_stride, x_head_stride,
+                                                   rows, heads, head_dim, scale, scale_stride, mode, out,
+                                                   out_row_stride, out_head_stride);
+    return check_launch("quant_rows_kernel");
+}
+
+int absmax(const char* who, const void* x, RowMap rm, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads,
+           int head_dim, int per_head, float* out, void* stream) {
+    if (rows < 0 || heads <= 0 || head_dim % 8) return fail(SA_ERR_ARG, "%s: bad sizes", who);
+    if (!x || !out) return fail(SA_ERR_ARG, "%s: null pointer", who);
+    if (!aligned16(x) || x_row_stride % 8 || x_head_stride % 8) return fail(SA_ERR_ALIGN, "%s: alignment", who);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(out, 0, sizeof(float) * (per_head ? heads : 1), s);
+    if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", who, cudaGetErrorString(e));
+    if (rows == 0) return SA_OK;
+    const int64_t per = static_cast<int64_t>(rows) * (head_dim / 8);
+    const int bx = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((per + 255) / 256, (8ll * num_sms()) / heads + 1)));
+    absmax_kernel<<<dim3(bx, heads), 256, 0, s>>>(static_cast<const uint16_t*>(x), rm, x_row_stride, x_head_stride,
+                                                 rows, heads, head_dim, per_head, out);
+    return check_launch("absmax_kernel");
+}
+
+}  // namespace
+}  // namespace sa
+
 using namespace sa;
 
 extern "C" int sa_block_means_bf16(const void* x, int64_t x_row_stride, int64_t x_head_stride, int n, int heads,
@@ -194,37 +271,21 @@ extern "C" int sa_block_means_bf16(const void* x, int64_t x_row_stride, int64_t 
                                    int64_t out_block_stride, int out_block0, uint8_t* q8, int64_t q8_row_stride,
                                    int64_t q8_head_stride, const float* inv_scale, int inv_scale_stride,
                                    int fixed_divisor, void* stream) {
-    if (n < 0 || heads <= 0 || block <= 0 || pos0 < 0) return fail(SA_ERR_ARG, "sa_block_means_bf16: bad sizes");
-    if (head_dim % 8 || head_dim > 8 * 256) return fail(SA_ERR_UNSUPPORTED, "sa_block_means_bf16: head_dim %d", head_dim);
-    if (!x || !out) return fail(SA_ERR_ARG, "sa_block_means_bf16: null pointer");
-    if (!aligned16(x) || x_row_stride % 8 || x_head_stride % 8)
-        return fail(SA_ERR_ALIGN, "sa_block_means_bf16: x must be 16-byte aligned with strides % 8 == 0");
-    if (q8 && (!inv_scale || (reinterpret_cast<uintptr_t>(q8) & 7) || q8_row_stride % 8 || q8_head_stride % 8))
-        return fail(SA_ERR_ALIGN, "sa_block_means_bf16: q8 needs inv_scale, 8-byte alignment, strides % 8 == 0");
-    if (n == 0) return SA_OK;
-    const int b0 = pos0 / block;
-    const int b1 = (pos0 + n + block - 1) / block;
-    if (b0 < out_block0) return fail(SA_ERR_ARG, "sa_block_means_bf16: first block %d < out_block0 %d", b0, out_block0);
-    // Launch shape: enough CTAs for >= 4 per SM and ~2048 threads per SM of independent 16-byte row
-    // streams.  Fewer heads per CTA first (more CTAs), then row groups (more loads in flight per block).
-    const int cols = head_dim / 8;
-    const int nblk = b1 - b0;
-    int hpc = std::min(std::max(1, 256 / cols), heads);
-    while (hpc > 1 && static_cast<long long>(nblk) * ((heads + hpc - 1) / hpc) < 4ll * num_sms()) hpc = (hpc + 1) / 2;
-    const int tx = hpc * cols;
-    const int nhg = (heads + hpc - 1) / hpc;
-    const long long ctas = static_cast<long long>(nblk) * nhg;
-    const long long target = 2048ll * num_sms();
-    int rg = 1;
-    while (rg < 16 && (ctas * tx * rg < target || tx * rg < 128) && tx * rg * 2 <= 512 && rg * 2 <= block / 4) rg *= 2;
-    dim3 grid(b1 - b0, nhg), blk(tx, rg);
-    const size_t smem = rg > 1 ? static_cast<size_t>(rg - 1) * tx * 8 * sizeof(float) : 0;
-    if (smem > 48 * 1024) cudaFuncSetAttribute(block_means_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    block_means_kernel<<<grid, blk, smem, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint16_t*>(x), x_row_stride, x_head_stride, n, heads, head_dim, pos0, block, b0, hpc, out,
-        out_head_stride, out_block_stride, out_block0, q8, q8_row_stride, q8_head_stride, inv_scale, inv_scale_stride,
-        fixed_divisor);
-    return check_launch("block_means_kernel");
+    return block_means("sa_block_means_bf16", x, contiguous_rows(), x_row_stride, x_head_stride, n, heads, head_dim,
+                       pos0, block, out, out_head_stride, out_block_stride, out_block0, q8, q8_row_stride,
+                       q8_head_stride, inv_scale, inv_scale_stride, fixed_divisor, stream);
+}
+
+extern "C" int sa_block_means_paged_bf16(const void* cache, int64_t page_stride, int64_t row_stride,
+                                         int64_t head_stride, const int32_t* page_table, int page_size, int n,
+                                         int heads, int head_dim, int pos0, int block, float* out,
+                                         int64_t out_head_stride, int64_t out_block_stride, int out_block0,
+                                         void* stream) {
+    const char* who = "sa_block_means_paged_bf16";
+    if (int rc = check_pages(who, page_table, page_size, page_stride)) return rc;
+    const RowMap rm{page_table, page_stride, page_size, pos0};
+    return block_means(who, cache, rm, row_stride, head_stride, n, heads, head_dim, pos0, block, out, out_head_stride,
+                       out_block_stride, out_block0, nullptr, 0, 0, nullptr, 0, 0, stream);
 }
 
 extern "C" int sa_quantize_e4m3(const void* x, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads,
@@ -237,21 +298,9 @@ extern "C" int sa_quantize_e4m3(const void* x, int64_t x_row_stride, int64_t x_h
     if (!aligned16(x) || x_row_stride % 8 || x_head_stride % 8)
         return fail(SA_ERR_ALIGN, "sa_quantize_e4m3: x must be 16-byte aligned with strides % 8 == 0");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (!transpose) {
-        if ((reinterpret_cast<uintptr_t>(out) & 7) || out_row_stride % 8 || out_head_stride % 8)
-            return fail(SA_ERR_ALIGN, "sa_quantize_e4m3: out must be 8-byte aligned with strides % 8 == 0");
-        if (rows == 0) return SA_OK;
-        const int HC = heads * (head_dim / 8);
-        const int bx = std::min(HC, 128);
-        const dim3 blk(bx, 256 / bx);
-        const int gy = (HC + bx - 1) / bx;
-        const int per_cta = static_cast<int>(blk.y) * 8;
-        const int gx = std::max(1, std::min((rows + per_cta - 1) / per_cta, (8 * num_sms() + gy - 1) / gy));
-        quant_rows_kernel<<<dim3(gx, gy), blk, 0, s>>>(static_cast<const uint16_t*>(x), x_row_stride, x_head_stride, rows,
-                                                 heads, head_dim, scale, scale_stride, mode, out,
-                                                 out_row_stride, out_head_stride);
-        return check_launch("quant_rows_kernel");
-    }
+    if (!transpose)
+        return quantize_rows("sa_quantize_e4m3", x, contiguous_rows(), x_row_stride, x_head_stride, rows, heads,
+                             head_dim, scale, scale_stride, mode, out, out_row_stride, out_head_stride, s);
     if (rows_pad < rows || rows_pad % 64 || !aligned16(out) || out_row_stride % 16 || out_head_stride % 16)
         return fail(SA_ERR_ALIGN, "sa_quantize_e4m3: transposed output needs rows_pad %% 64 == 0, 16-byte alignment");
     if (rows_pad == 0) return SA_OK;
@@ -263,18 +312,34 @@ extern "C" int sa_quantize_e4m3(const void* x, int64_t x_row_stride, int64_t x_h
     return check_launch("transpose_kernel<e4m3>");
 }
 
+extern "C" int sa_quantize_paged_e4m3(const void* cache, int64_t page_stride, int64_t row_stride, int64_t head_stride,
+                                      const int32_t* page_table, int page_size, int row0, int rows, int heads,
+                                      int head_dim, const float* scale, int scale_stride, int mode, uint8_t* out,
+                                      int64_t out_row_stride, int64_t out_head_stride, void* stream) {
+    const char* who = "sa_quantize_paged_e4m3";
+    if (rows < 0 || row0 < 0 || heads <= 0 || head_dim % 8) return fail(SA_ERR_ARG, "%s: bad sizes", who);
+    if (!cache || !out || !scale) return fail(SA_ERR_ARG, "%s: null pointer", who);
+    if (mode < SA_QUANT_MUL || mode > SA_QUANT_DIV) return fail(SA_ERR_ARG, "%s: bad mode %d", who, mode);
+    if (int rc = check_pages(who, page_table, page_size, page_stride)) return rc;
+    if (!aligned16(cache) || row_stride % 8 || head_stride % 8)
+        return fail(SA_ERR_ALIGN, "%s: cache must be 16-byte aligned with strides %% 8 == 0", who);
+    const RowMap rm{page_table, page_stride, page_size, row0};
+    return quantize_rows(who, cache, rm, row_stride, head_stride, rows, heads, head_dim, scale, scale_stride, mode, out,
+                         out_row_stride, out_head_stride, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int sa_absmax_bf16(const void* x, int64_t x_row_stride, int64_t x_head_stride, int rows, int heads,
                               int head_dim, int per_head, float* out, void* stream) {
-    if (rows < 0 || heads <= 0 || head_dim % 8) return fail(SA_ERR_ARG, "sa_absmax_bf16: bad sizes");
-    if (!x || !out) return fail(SA_ERR_ARG, "sa_absmax_bf16: null pointer");
-    if (!aligned16(x) || x_row_stride % 8 || x_head_stride % 8) return fail(SA_ERR_ALIGN, "sa_absmax_bf16: alignment");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemsetAsync(out, 0, sizeof(float) * (per_head ? heads : 1), s);
-    if (e != cudaSuccess) return fail(SA_ERR_CUDA, "sa_absmax_bf16: %s", cudaGetErrorString(e));
-    if (rows == 0) return SA_OK;
-    const int64_t per = static_cast<int64_t>(rows) * (head_dim / 8);
-    const int bx = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((per + 255) / 256, (8ll * num_sms()) / heads + 1)));
-    absmax_kernel<<<dim3(bx, heads), 256, 0, s>>>(static_cast<const uint16_t*>(x), x_row_stride, x_head_stride, rows,
-                                                 heads, head_dim, per_head, out);
-    return check_launch("absmax_kernel");
+    return absmax("sa_absmax_bf16", x, contiguous_rows(), x_row_stride, x_head_stride, rows, heads, head_dim, per_head,
+                  out, stream);
+}
+
+extern "C" int sa_absmax_paged_bf16(const void* cache, int64_t page_stride, int64_t row_stride, int64_t head_stride,
+                                    const int32_t* page_table, int page_size, int row0, int rows, int heads,
+                                    int head_dim, int per_head, float* out, void* stream) {
+    const char* who = "sa_absmax_paged_bf16";
+    if (row0 < 0) return fail(SA_ERR_ARG, "%s: row0 < 0", who);
+    if (int rc = check_pages(who, page_table, page_size, page_stride)) return rc;
+    const RowMap rm{page_table, page_stride, page_size, row0};
+    return absmax(who, cache, rm, row_stride, head_stride, rows, heads, head_dim, per_head, out, stream);
 }

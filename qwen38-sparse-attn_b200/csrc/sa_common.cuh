@@ -164,6 +164,44 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
     return v;
 }
 
+// Row addressing of a [rows, heads, head_dim] operand that is either contiguous (pages == nullptr:
+// row r at r * row_stride) or held in fixed-size pages, like a vLLM KV cache [num_pages, page,
+// heads, head_dim]: row r is logical row l = row0 + r, which sits in slot l % page of page
+// pages[l / page] (page_stride elements between pages, row_stride between the slots of a page).
+struct RowMap {
+    const int32_t* pages;
+    int64_t page_stride;
+    int page, row0;
+    __device__ __forceinline__ int64_t offset(int r, int64_t row_stride) const {
+        if (!pages) return static_cast<int64_t>(r) * row_stride;
+        const int l = row0 + r;
+        const int pg = l / page;
+        return static_cast<int64_t>(__ldg(pages + pg)) * page_stride + static_cast<int64_t>(l - pg * page) * row_stride;
+    }
+};
+inline RowMap contiguous_rows() { return RowMap{nullptr, 0, 1, 0}; }
+
+// Launch shape of a block-means reduction over nblk key blocks of `block` rows and `heads` heads of
+// head_dim: heads per CTA (hpc, each with head_dim / 8 column threads) and row groups (rg).  The
+// row groups fix the order in which a block's rows are added (group g sums rows lo+g, lo+g+rg, ...
+// in order; the groups' sums are then added in group order), so kernels that produce block means
+// for the same (nblk, heads, head_dim, block) through this shape produce the same bits.  Aims at
+// >= 4 CTAs per SM and ~2048 threads per SM of independent 16-byte row streams: fewer heads per CTA
+// first (more CTAs), then row groups (more loads in flight per block); hpc * head_dim / 8 * rg <= 512.
+inline void block_means_shape(int nblk, int heads, int head_dim, int block, int* hpc_out, int* rg_out) {
+    const int cols = head_dim / 8;
+    int hpc = heads < 256 / cols ? heads : 256 / cols;
+    if (hpc < 1) hpc = 1;
+    while (hpc > 1 && static_cast<long long>(nblk) * ((heads + hpc - 1) / hpc) < 4ll * num_sms()) hpc = (hpc + 1) / 2;
+    const int tx = hpc * cols;
+    const long long ctas = static_cast<long long>(nblk) * ((heads + hpc - 1) / hpc);
+    const long long target = 2048ll * num_sms();
+    int rg = 1;
+    while (rg < 16 && (ctas * tx * rg < target || tx * rg < 128) && tx * rg * 2 <= 512 && rg * 2 <= block / 4) rg *= 2;
+    *hpc_out = hpc;
+    *rg_out = rg;
+}
+
 // eight bf16 values -> fp32
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -322,6 +360,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
         "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%3, %4, %5}], [%2];"
         :: "r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1, int c2,
+                                            int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];"
+        :: "r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
 

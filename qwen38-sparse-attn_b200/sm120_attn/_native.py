@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / '_lib' / 'libsa_b200.so'
 SA_OK = 0
 SA_ERR_ARG, SA_ERR_ALIGN, SA_ERR_UNSUPPORTED, SA_ERR_CUDA, SA_ERR_TMA, SA_ERR_DEVICE = -1, -2, -3, -4, -5, -6
 SA_DEV_WAIT_Q, SA_DEV_WAIT_KV, SA_DEV_WAIT_S, SA_DEV_WAIT_P, SA_DEV_WAIT_O, SA_DEV_BAD_LIST = 1, 2, 4, 8, 16, 32
+SA_DEV_BAD_PAGE = 64
 SA_SELECT_PER_HEAD, SA_SELECT_KV_UNION, SA_SELECT_PAIR_UNION = 0, 1, 2
 SA_QUANT_MUL, SA_QUANT_MUL_BF16, SA_QUANT_DIV = 0, 1, 2
 
@@ -42,6 +43,15 @@ SIGNATURES = {
     'sa_add_rmsnorm_bf16': [_p, _i64, _p, _i64, _p, _p, _i64, _i32, _i32, _f32, _p],
     'sa_rope_qkv_bf16': [_p, _i64, _i32, _i32, _i32, _i32, _p, _i32, _i32, _p, _p, _i64, _p, _i64, _p],
     'sa_silu_mul_bf16': [_p, _i64, _i32, _i32, _p, _i64, _p],
+    'sa_rope_qkv_means_bf16': [_p, _i64, _i32, _i32, _i32, _i32, _p, _i32, _i32, _p, _p, _i64, _p, _i64, _i32, _p,
+                               _i64, _i64, _i32, _p],
+    'sa_block_means_paged_bf16': [_p, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p, _i64, _i64, _i32,
+                                  _p],
+    'sa_absmax_paged_bf16': [_p, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p],
+    'sa_quantize_paged_e4m3': [_p, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _p, _i32, _i32, _p, _i64, _i64,
+                               _p],
+    'sa_attn_fwd_bf16_paged': [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i32, _i32, _p, _i64, _i64, _i32, _i32,
+                               _i32, _i32, _i32, _i32, _i32, _p, _p, _i64, _i32, _i32, _f32, _p, _p],
 }
 
 

@@ -166,11 +166,21 @@ class TPDecoder:
         if self.world > 1:
             torch.distributed.all_reduce(t, group=self.group)
 
-    def _attention(self, L: int, q, c0: int, n: int, out):
+    def _rope(self, L: int, qkv, q, c0: int, n: int) -> bool:
+        """RoPE of the chunk's q and k into q and the layer's K/V cache rows, with the key block means
+        written into the layer's block-mean cache in the same pass when that entry continues at c0.
+        Returns whether it did (else _attention computes them from the cache rows)."""
+        D = self.cfg.head_dim
+        km = ksp.km_slot((self._key, L), 0, c0, c0 + n, self.hk, D, self.device)
+        ops.rope_qkv(qkv, self.hq, self.hk, D, self.cos_sin, c0, q, self.k_cache[L][c0:c0 + n],
+                     self.v_cache[L][c0:c0 + n], km=km, block=ksp.BLOCK)
+        return km is not None
+
+    def _attention(self, L: int, q, c0: int, n: int, out, means_written: bool = False):
         kv_len = c0 + n
         kc, vc = self.k_cache[L], self.v_cache[L]
         key = (self._key, L)
-        km = ksp._cached_block_means(key, 0, kc[c0:kv_len], c0, kv_len, key_all=kc)
+        km = ksp._cached_block_means(key, 0, kc[c0:kv_len], c0, kv_len, key_all=kc, written=means_written)
         if self.sp.kernel == 'sm120fp8':
             scales = ksp._cached_scales(key, 0, q, kc[:kv_len], vc[:kv_len], c0)
             kv8 = ksp._cached_kv8(key, 0, kc, vc, c0, kv_len, scales) if self.fp8_kv_cache else None
@@ -195,9 +205,8 @@ class TPDecoder:
             for L, W in enumerate(self.layers):
                 ops.add_rmsnorm(h, W['ln1'], x, cfg.eps, delta=d if L > 0 else None)
                 torch.matmul(x, W['qkv'].t(), out=qkv)
-                ops.rope_qkv(qkv, self.hq, self.hk, D, self.cos_sin, c0, q, self.k_cache[L][c0:c0 + n],
-                             self.v_cache[L][c0:c0 + n])
-                self._attention(L, q, c0, n, attn)
+                written = self._rope(L, qkv, q, c0, n)
+                self._attention(L, q, c0, n, attn, means_written=written)
                 if self.comm_blocks > 1:
                     self._mlp_overlapped(W, attn.view(n, self.hq * D), h, x, o, gu, a, d, n)
                     continue

@@ -150,6 +150,49 @@ def quantize(x, scale, mode: int, out, transpose: bool = False, rows_pad: int = 
                out.stride(0), out.stride(1), 0, 0, _stream(x.device))
 
 
+def _paged(name, cache, table):
+    """Strides of a paged cache [num_pages, page, heads, D] bf16 and its int32 page table row."""
+    if cache.dtype != torch.bfloat16 or cache.dim() != 4 or cache.stride(3) != 1:
+        raise ValueError(f'{name}: cache must be bf16 [num_pages, page, heads, head_dim] with unit last stride')
+    if table.dtype != torch.int32 or table.dim() != 1 or table.stride(0) != 1:
+        raise ValueError(f'{name}: page table must be a contiguous int32 vector')
+    return cache.stride(0), cache.stride(1), cache.stride(2)
+
+
+def block_means_paged(cache, table, pos0: int, n: int, block: int, out, out_block0: int):
+    """Block means of the keys at positions pos0 .. pos0+n-1 of a paged cache (page table row
+    `table`) into out [heads, blocks, D] fp32; see sa_block_means_paged_bf16."""
+    _need_cuda('block_means_paged', cache, table, out)
+    ps, rs, hs = _paged('block_means_paged', cache, table)
+    heads, D = cache.shape[2], cache.shape[3]
+    assert out.dtype == torch.float32 and out.dim() == 3 and out.stride(2) == 1
+    N.call('sa_block_means_paged_bf16', _p(cache), ps, rs, hs, _p(table), cache.shape[1], n, heads, D, pos0, block,
+           _p(out), out.stride(0), out.stride(1), out_block0, _stream(cache.device))
+
+
+def absmax_paged(cache, table, row0: int, rows: int, per_head: bool, out=None):
+    """absmax over positions row0 .. row0+rows-1 of a paged cache; see sa_absmax_paged_bf16."""
+    _need_cuda('absmax_paged', cache, table, out)
+    ps, rs, hs = _paged('absmax_paged', cache, table)
+    heads, D = cache.shape[2], cache.shape[3]
+    if out is None:
+        out = torch.empty(heads if per_head else 1, dtype=torch.float32, device=cache.device)
+    N.call('sa_absmax_paged_bf16', _p(cache), ps, rs, hs, _p(table), cache.shape[1], row0, rows, heads, D,
+           1 if per_head else 0, _p(out), _stream(cache.device))
+    return out
+
+
+def quantize_paged(cache, table, row0: int, scale, mode: int, out):
+    """e4m3 of positions row0 .. row0+len(out)-1 of a paged cache into out [rows, heads, D] (row r =
+    position row0 + r); see sa_quantize_paged_e4m3."""
+    _need_cuda('quantize_paged', cache, table, scale, out)
+    ps, rs, hs = _paged('quantize_paged', cache, table)
+    heads, D = cache.shape[2], cache.shape[3]
+    ss = 0 if scale.numel() == 1 else 1
+    N.call('sa_quantize_paged_e4m3', _p(cache), ps, rs, hs, _p(table), cache.shape[1], row0, out.shape[0], heads, D,
+           _p(scale), ss, mode, _p(out), out.stride(0), out.stride(1), _stream(cache.device))
+
+
 def absmax(x, per_head: bool, out=None):
     _need_cuda('absmax', x, out)
     rows, heads, D = x.shape
@@ -191,6 +234,28 @@ def attn_bf16(q, k, v, out, kv_len: int, q_front: int, q_offset: int, counts, li
            float(softmax_scale), _p(st), _stream(q.device))
 
 
+def attn_bf16_paged(q, k_cache, v_cache, table, out, kv_len: int, q_front: int, q_offset: int, counts, lists,
+                    kv_block: int, softmax_scale: float, q_block: int = 128):
+    """attn_bf16 with K and V read in place from paged caches [num_pages, page, Hk, D] through the
+    request's page table row (int32); see sa_attn_fwd_bf16_paged."""
+    _need_cuda('attn_bf16_paged', q, k_cache, v_cache, table, out, counts, lists)
+    ps, rs, hs = _paged('attn_bf16_paged', k_cache, table)
+    if v_cache.stride() != k_cache.stride() or v_cache.shape != k_cache.shape:
+        raise ValueError('attn_bf16_paged: k_cache and v_cache must have the same shape and strides')
+    n, H, D = q.shape
+    num_pages, page, Hk = k_cache.shape[0], k_cache.shape[1], k_cache.shape[2]
+    st = status_word(q.device)
+    N.call('sa_attn_fwd_bf16_paged', _p(q), q.stride(0), q.stride(1), _p(k_cache), _p(v_cache), ps, rs, hs, _p(table),
+           page, num_pages, _p(out), out.stride(0), out.stride(1), n, H, Hk, D, kv_len, q_front, q_offset, _p(counts),
+           _p(lists), lists.stride(0) if lists is not None else 0, q_block, kv_block, float(softmax_scale), _p(st),
+           _stream(q.device))
+
+
+def paged_attention_supported(page: int) -> bool:
+    """Page sizes sa_attn_fwd_bf16_paged reads in place."""
+    return page in (8, 16, 32) or (page > 0 and page % 64 == 0)
+
+
 # ---------------------------------------------------------------- end-to-end prefill harness kernels
 
 def _rows2d(name, t):
@@ -210,9 +275,12 @@ def add_rmsnorm(h, weight, x_out, eps: float, delta=None):
            _p(weight), _p(x_out), x_out.stride(0), rows, hidden, ctypes.c_float(eps), _stream(h.device))
 
 
-def rope_qkv(qkv, num_heads: int, num_kv_heads: int, head_dim: int, cos_sin, pos0: int, q_out, k_out, v_out):
+def rope_qkv(qkv, num_heads: int, num_kv_heads: int, head_dim: int, cos_sin, pos0: int, q_out, k_out, v_out,
+             km=None, block: int = 0, km_block0: int = 0):
     """Rotary embedding of the q and k heads of qkv [rows, (H + 2 Hk) D] at positions pos0..; q to
-    q_out [rows, H, D], k and v to k_out / v_out [rows, Hk, D] (e.g. cache rows); see sa_rope_qkv_bf16."""
+    q_out [rows, H, D], k and v to k_out / v_out [rows, Hk, D] (e.g. cache rows); see sa_rope_qkv_bf16.
+    With km ([Hk, blocks, D] fp32) the block means of the rotated keys (blocks of `block` rows, block
+    b at km[:, b - km_block0]) are written in the same pass (sa_rope_qkv_means_bf16)."""
     _need_cuda('rope_qkv', qkv, cos_sin, q_out, k_out, v_out)
     _rows2d('rope_qkv qkv', qkv)
     rows = qkv.shape[0]
@@ -226,8 +294,20 @@ def rope_qkv(qkv, num_heads: int, num_kv_heads: int, head_dim: int, cos_sin, pos
         raise ValueError('rope_qkv: q_out must be contiguous')
     if cos_sin.dtype != torch.float32 or cos_sin.dim() != 2 or cos_sin.shape[1] != head_dim or not cos_sin.is_contiguous():
         raise ValueError('rope_qkv: cos_sin must be a contiguous fp32 [max_pos, head_dim] table')
-    N.call('sa_rope_qkv_bf16', _p(qkv), qkv.stride(0), rows, num_heads, num_kv_heads, head_dim, _p(cos_sin), pos0,
-           cos_sin.shape[0], _p(q_out), _p(k_out), k_out.stride(0), _p(v_out), v_out.stride(0), _stream(qkv.device))
+    if km is None:
+        N.call('sa_rope_qkv_bf16', _p(qkv), qkv.stride(0), rows, num_heads, num_kv_heads, head_dim, _p(cos_sin), pos0,
+               cos_sin.shape[0], _p(q_out), _p(k_out), k_out.stride(0), _p(v_out), v_out.stride(0),
+               _stream(qkv.device))
+        return
+    _need_cuda('rope_qkv', km)
+    if km.dtype != torch.float32 or km.dim() != 3 or km.shape[0] != num_kv_heads or km.shape[2] != head_dim or \
+            km.stride(2) != 1:
+        raise ValueError('rope_qkv: km must be fp32 [num_kv_heads, blocks, head_dim]')
+    if block <= 0 or -(-(pos0 + rows) // block) - km_block0 > km.shape[1]:
+        raise ValueError('rope_qkv: km holds too few blocks')
+    N.call('sa_rope_qkv_means_bf16', _p(qkv), qkv.stride(0), rows, num_heads, num_kv_heads, head_dim, _p(cos_sin),
+           pos0, cos_sin.shape[0], _p(q_out), _p(k_out), k_out.stride(0), _p(v_out), v_out.stride(0), block, _p(km),
+           km.stride(0), km.stride(1), km_block0, _stream(qkv.device))
 
 
 def silu_mul(gate_up, out):

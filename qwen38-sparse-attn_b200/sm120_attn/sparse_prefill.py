@@ -156,13 +156,21 @@ class SparsePrefill:
         return torch.empty(n, self.H, self.D, dtype=torch.bfloat16, device=dev), out is not None
 
     @torch.no_grad()
-    def forward_sm120(self, q, k, v, q_start, out=None, km=None):
+    def forward_sm120(self, q, k, v, q_start, out=None, km=None, kv_pages=None):
         """BF16 kernel, one block list per query head and BLOCK-row query block.  k and v are NHD
         [T, Hk, D]; rows T > q_start + n are not read.  km: the request's cached fp32 block means
-        [Hk, ceil((q_start + n) / BLOCK), D], else they are pooled here from k.  Makes no host sync."""
+        [Hk, ceil((q_start + n) / BLOCK), D], else they are pooled here from k.  Makes no host sync.
+        kv_pages: (key_cache, value_cache, table) read in place by the kernel instead of k and v (which
+        may then be None; km is required): vLLM's paged caches [num_pages, page, Hk, D] and the
+        request's int32 page-table row, holding at least q_start + n keys."""
         n = q.shape[0]
         kv_len = q_start + n
-        if k.shape[0] < kv_len:
+        if kv_pages is not None:
+            if km is None:
+                raise ValueError('forward_sm120: kv_pages needs km')
+            if kv_pages[2].shape[0] * kv_pages[0].shape[1] < kv_len:
+                raise AssertionError('the page table holds fewer keys than q_start + n')
+        elif k.shape[0] < kv_len:
             raise AssertionError('k holds fewer rows than q_start + n')
         B = BLOCK
         front = q_start % B
@@ -174,6 +182,8 @@ class SparsePrefill:
         if km is None:
             km = self._km_from_keys(k, _cdiv(kv_len, B))
         if FP8_EMULATE:
+            if kv_pages is not None:
+                raise ValueError('forward_sm120: FP8 emulation reads gathered k and v, not kv_pages')
             q, k, v = (_fp8_round(t, FP8_EMULATE, name) for t, name in ((q, 'q'), (k, 'k'), (v, 'v')))
         NB = km.shape[1]
         counts = torch.empty(self.H * MB, dtype=torch.int32, device=dev)
@@ -184,7 +194,11 @@ class SparsePrefill:
         ev0, ev1 = self._attn_events()
         if ev0 is not None:
             ev0.record()
-        ops.attn_bf16(q, k[:kv_len], v[:kv_len], o, kv_len, front, qs, counts, lists, B, self.scale, q_block=B)
+        if kv_pages is not None:
+            ops.attn_bf16_paged(q, kv_pages[0], kv_pages[1], kv_pages[2], o, kv_len, front, qs, counts, lists, B,
+                                self.scale, q_block=B)
+        else:
+            ops.attn_bf16(q, k[:kv_len], v[:kv_len], o, kv_len, front, qs, counts, lists, B, self.scale, q_block=B)
         if ev1 is not None:
             ev1.record()
         self.last_counts, self.last_lists = counts, lists
@@ -422,42 +436,92 @@ _KMEAN_CACHE: dict = {}
 _KMEAN_MAX_ENTRIES = 128
 
 
-def _cached_block_means(layer_key, first_page, key_chunk, q_start, kv_len, key_all=None):
+class _PagedRows(NamedTuple):
+    """Rows 0 .. rows-1 of a request in one of vLLM's paged caches [num_pages, page, Hk, D]: position
+    l is slot l % page of page table[l // page] (the request's int32 block-table row).  Stands for
+    the gathered history `cache[table].reshape(-1, Hk, D)[:rows]` and is read in place."""
+    cache: torch.Tensor
+    table: torch.Tensor
+    rows: int
+
+    @property
+    def shape(self):
+        return (self.rows, self.cache.shape[2], self.cache.shape[3])
+
+
+def _km_continues(q_start):
+    return lambda e: e['nb'] >= q_start // BLOCK and e.get('last_kv') == q_start
+
+
+def _km_entry(layer_key, first_page, q_start, end_block, Hk, D, dev):
+    """(entry, rebuilt): the block-mean entry of (layer, request) for a chunk at q_start, its km grown
+    (capacity doubling, at least to end_block blocks)."""
+    def fresh():
+        return {'km': torch.zeros(Hk, max(4096, end_block), D, dtype=torch.float32, device=dev), 'nb': 0,
+                'last_kv': 0}
+    entry, rebuilt = _request_entry(_KMEAN_CACHE, (layer_key, first_page), q_start, _km_continues(q_start), fresh)
+    held = entry['km'].shape[1]
+    if held < end_block:
+        grown = entry['km'].new_zeros(Hk, max(end_block, 2 * held), D)
+        grown[:, :held] = entry['km']
+        entry['km'] = grown
+    return entry, rebuilt
+
+
+def km_slot(layer_key, first_page, q_start, kv_len, Hk, D, dev):
+    """The km tensor [Hk, capacity, D] of a request's block-mean entry prepared for the chunk of keys
+    q_start .. kv_len, for the producer of those keys to write their block means into at KV-write time
+    (ops.rope_qkv(..., km=)); _cached_block_means(..., written=True) then only records them.  None
+    when the entry does not continue at q_start (it is rebuilt from the key history instead)."""
+    entry = _KMEAN_CACHE.get((layer_key, first_page))
+    if q_start > 0 and (entry is None or not _km_continues(q_start)(entry)):
+        return None
+    entry, _ = _km_entry(layer_key, first_page, q_start, -(-kv_len // BLOCK), Hk, D, dev)
+    entry['slot'] = (q_start, kv_len)
+    return entry['km']
+
+
+def _cached_block_means(layer_key, first_page, key_chunk, q_start, kv_len, key_all=None, written=False, q8=None,
+                        inv_scale=None):
     """fp32 block means [Hk, NB, D] of a request's keys, NB = ceil((q_start + n) / BLOCK), kept per
     (layer, request) and extended by each chunk (sparse_prefill.py:398-447).
 
     key_chunk [n, Hk, D] holds the keys at positions q_start..; the entry grows by the chunk's blocks.
     A request whose cached entry does not end at q_start (new request, recycled first page, skipped
-    chunks) is rebuilt from key_all [>= q_start, Hk, D], its history.  As in the reference, a chunk
-    that starts inside a block replaces that block's mean by the mean of its own rows there; only a
-    rebuild averages the block's history rows and chunk rows together.
+    chunks) is rebuilt from key_all, its history: a tensor [>= q_start, Hk, D], or _PagedRows read in
+    place (then covering the chunk too, positions 0 .. kv_len).  As in the reference, a chunk that
+    starts inside a block replaces that block's mean by the mean of its own rows there; only a rebuild
+    averages the block's history rows and chunk rows together.
+    written: the chunk's means were written into the km_slot of this chunk by the keys' producer.
+    q8 / inv_scale: e4m3 copy of the chunk's keys written in the same pass (continuing entries only).
     """
     B = BLOCK
     n, Hk, D = key_chunk.shape
     end_block = -(-(q_start + n) // B)
-    dev = key_chunk.device
-
-    def fresh():
-        return {'km': torch.zeros(Hk, max(4096, end_block), D, dtype=torch.float32, device=dev), 'nb': 0,
-                'last_kv': 0}
-    entry, rebuilt = _request_entry(_KMEAN_CACHE, (layer_key, first_page), q_start,
-                                    lambda e: e['nb'] >= q_start // B and e.get('last_kv') == q_start, fresh)
+    if written:
+        entry = _KMEAN_CACHE.get((layer_key, first_page))
+        if entry is None or entry.pop('slot', None) != (q_start, kv_len):
+            raise RuntimeError('block means marked written without a km_slot for this chunk')
+        entry['nb'], entry['last_kv'] = end_block, kv_len
+        return entry['km'][:, :end_block]
+    entry, rebuilt = _km_entry(layer_key, first_page, q_start, end_block, Hk, D, key_chunk.device)
     rows, pos0 = key_chunk, q_start                  # rows whose block means are (re)computed below
     if rebuilt and q_start > 0:
         if key_all is None:
             raise RuntimeError('stale block-mean cache entry and no key history to rebuild it')
-        whole = q_start - q_start % B                # history rows that fill complete blocks
-        if whole:
-            ops.block_means(key_all[:whole], 0, B, entry['km'], 0)
-        if whole < q_start:                          # the block the chunk continues: history + chunk rows
-            rows, pos0 = torch.cat([key_all[whole:q_start], key_chunk], 0), whole
-    held = entry['km'].shape[1]
-    if held < end_block:                             # capacity doubles (at least to end_block)
-        grown = entry['km'].new_zeros(Hk, max(end_block, 2 * held), D)
-        grown[:, :held] = entry['km']
-        entry['km'] = grown
+        if q8 is not None:
+            raise RuntimeError('a fused e4m3 key copy needs a continuing block-mean entry')
+        if isinstance(key_all, _PagedRows):
+            ops.block_means_paged(key_all.cache, key_all.table, 0, q_start + n, B, entry['km'], 0)
+            rows = key_chunk[:0]
+        else:
+            whole = q_start - q_start % B            # history rows that fill complete blocks
+            if whole:
+                ops.block_means(key_all[:whole], 0, B, entry['km'], 0)
+            if whole < q_start:                      # the block the chunk continues: history + chunk rows
+                rows, pos0 = torch.cat([key_all[whole:q_start], key_chunk], 0), whole
     if rows.shape[0]:
-        ops.block_means(rows, pos0, B, entry['km'], 0)
+        ops.block_means(rows, pos0, B, entry['km'], 0, q8=q8, inv_scale=inv_scale)
     entry['nb'], entry['last_kv'] = end_block, kv_len
     return entry['km'][:, :end_block]
 
@@ -521,33 +585,31 @@ def _kv8_evict(keep_key):
             total -= _kv8_bytes(_KV8_CACHE.pop(key))
 
 
-def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
-    """Per-(layer, request) e4m3 K and V [kv_len, Hk, D] (uint8 views), each row quantised once.
+def _quantize_into(src, lo, hi, row0, inv, out8):
+    """e4m3 (MUL_BF16) of key/value positions lo .. hi-1 into out8[lo:hi]; src is a tensor holding
+    positions row0 .. or _PagedRows (read in place)."""
+    if hi <= lo:
+        return
+    if isinstance(src, _PagedRows):
+        ops.quantize_paged(src.cache, src.table, lo, inv, SA_QUANT_MUL_BF16, out8[lo:hi])
+    else:
+        ops.quantize(src[lo - row0:hi - row0], inv, SA_QUANT_MUL_BF16, out8[lo:hi])
 
-    The FP8 path quantises the whole key/value history with the request's scales on every chunk
-    (sparse_prefill.py:230-233); the scales are cached per request, so rows quantised for an earlier
-    chunk never change.  An entry contiguous with this chunk (its last row is q_start) and made with
-    the same scales only quantises rows q_start..kv_len; otherwise it is rebuilt from k, v (NHD).
-    k and v hold sequence rows k_row0 .. k_row0 + len (k_row0 > 0 only for a contiguous entry: a
-    rebuild needs every row from 0).  The bytes are the same as re-quantising the history.
-    """
+
+def _kv8_entry(layer_key, first_page, q_start, kv_len, scales, Hk, D, dev):
+    """(entry, lo): the FP8 KV cache entry of (layer, request) for a chunk ending at kv_len, grown to
+    hold kv_len rows, with rows lo .. kv_len still to be quantised (lo = q_start for an entry that
+    continues at q_start with the same scales, else 0: a fresh entry)."""
     kv_key = _kv_scale_key(scales)
     key = (layer_key, first_page)
-    Hk, D = k.shape[1], k.shape[2]
-    dev = k.device
-
-    def continues(e):
-        return e['rows'] == q_start and e['scales'] == kv_key
-    prior = _KV8_CACHE.get(key)
-    if k_row0 and not (prior is not None and q_start > 0 and continues(prior)):
-        raise RuntimeError('stale FP8 KV cache entry and no key/value rows before %d to rebuild it' % k_row0)
 
     def fresh():
         rows = max(kv_len, 8192)
         return {'k8': torch.empty(rows, Hk, D, dtype=torch.uint8, device=dev),
                 'v8': torch.empty(rows, Hk, D, dtype=torch.uint8, device=dev), 'rows': 0, 'scales': kv_key,
                 'inv': _scale_views(dev, scales)[1:3]}
-    entry, _ = _request_entry(_KV8_CACHE, key, q_start, continues, fresh)
+    entry, _ = _request_entry(_KV8_CACHE, key, q_start,
+                              lambda e: e['rows'] == q_start and e['scales'] == kv_key, fresh)
     lo = entry['rows']
     if entry['k8'].shape[0] < kv_len:
         cap = max(kv_len, 2 * entry['k8'].shape[0])
@@ -556,13 +618,46 @@ def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
             grown[:lo] = entry[name][:lo]
             entry[name] = grown
     _kv8_evict(key)
+    return entry, lo
+
+
+def _cached_kv8(layer_key, first_page, k, v, q_start, kv_len, scales, k_row0=0):
+    """Per-(layer, request) e4m3 K and V [kv_len, Hk, D] (uint8 views), each row quantised once.
+
+    The FP8 path quantises the whole key/value history with the request's scales on every chunk
+    (sparse_prefill.py:230-233); the scales are cached per request, so rows quantised for an earlier
+    chunk never change.  An entry contiguous with this chunk (its last row is q_start) and made with
+    the same scales only quantises rows q_start..kv_len; otherwise it is rebuilt from k, v.  k and v
+    are NHD tensors holding sequence rows k_row0 .. k_row0 + len (k_row0 > 0 only for a contiguous
+    entry: a rebuild needs every row from 0), or _PagedRows read in place.  The bytes are the same as
+    re-quantising the history.
+    """
+    kv_key = _kv_scale_key(scales)
+    prior = _KV8_CACHE.get((layer_key, first_page))
+    if k_row0 and not (prior is not None and q_start > 0 and prior['rows'] == q_start and prior['scales'] == kv_key):
+        raise RuntimeError('stale FP8 KV cache entry and no key/value rows before %d to rebuild it' % k_row0)
+    entry, lo = _kv8_entry(layer_key, first_page, q_start, kv_len, scales, k.shape[1], k.shape[2],
+                           (k.cache if isinstance(k, _PagedRows) else k).device)
     if kv_len > lo:
-        if k.shape[0] < kv_len - k_row0 or v.shape[0] < kv_len - k_row0 or lo < k_row0:
-            raise ValueError('_cached_kv8: k/v do not hold rows %d..%d' % (lo, kv_len))
-        ops.quantize(k[lo - k_row0:kv_len - k_row0], entry['inv'][0], SA_QUANT_MUL_BF16, entry['k8'][lo:kv_len])
-        ops.quantize(v[lo - k_row0:kv_len - k_row0], entry['inv'][1], SA_QUANT_MUL_BF16, entry['v8'][lo:kv_len])
+        for src in (k, v):
+            if not isinstance(src, _PagedRows) and (src.shape[0] < kv_len - k_row0 or lo < k_row0):
+                raise ValueError('_cached_kv8: k/v do not hold rows %d..%d' % (lo, kv_len))
+        _quantize_into(k, lo, kv_len, k_row0, entry['inv'][0], entry['k8'])
+        _quantize_into(v, lo, kv_len, k_row0, entry['inv'][1], entry['v8'])
     entry['rows'] = kv_len
     return entry['k8'][:kv_len], entry['v8'][:kv_len]
+
+
+def _kv8_scratch(k, v, kv_len, scales, dev):
+    """e4m3 K and V of positions 0 .. kv_len-1 for one chunk (no FP8 KV cache: the whole history is
+    quantised every chunk, as in the reference), read in place from the pages."""
+    inv_k, inv_v = _scale_views(dev, scales)[1:3]
+    out = []
+    for src, inv in ((k, inv_k), (v, inv_v)):
+        t = torch.empty(kv_len, src.shape[1], src.shape[2], dtype=torch.uint8, device=dev)
+        _quantize_into(src, 0, kv_len, 0, inv, t)
+        out.append(t)
+    return tuple(out)
 
 
 def _fp8_warm(layer_key, first_page, q_start) -> bool:
@@ -586,7 +681,8 @@ def _cached_scales(layer_key, first_page, q, k, v, q_start, per_head: bool = Fal
     tuple with one scale per head (H for q, Hk for k and v) instead of one per tensor.  One host sync
     when an entry is made."""
     def fresh():
-        peaks = [ops.absmax(t if t.stride(-1) == 1 else t.contiguous(), per_head=per_head).clamp_min(1e-6)
+        peaks = [(ops.absmax_paged(t.cache, t.table, 0, t.rows, per_head) if isinstance(t, _PagedRows) else
+                  ops.absmax(t if t.stride(-1) == 1 else t.contiguous(), per_head=per_head)).clamp_min(1e-6)
                  for t in (q, k, v)]
         if not per_head:
             return {'scales': tuple(a * SCALE_MARGIN / 448.0 for a in torch.cat(peaks).tolist()), 'last_kv': 0}
@@ -692,33 +788,49 @@ def try_sparse_forward(impl, query, key, key_cache, value_cache, output, attn_me
 
 def _sparse_request(sp, cfg, layer, rq, q_r, key_r, key_cache, value_cache, o_r, pages_row):
     """One long prefill chunk through the block-sparse path.  The caches of (layer, first page) carry
-    the request's block means, e4m3 scales and (with fp8_kv_cache) e4m3 K/V from chunk to chunk."""
-    page, Hk, D = key_cache.shape[1], key_cache.shape[2], key_cache.shape[3]
+    the request's block means, e4m3 scales and (with fp8_kv_cache) e4m3 K/V from chunk to chunk.
+    The key/value history is read in place from the pages (the reference gathers it into contiguous
+    tensors on every chunk, sparse_prefill.py:521-522): by the paged block-mean, absmax and e4m3
+    kernels, and by the BF16 attention kernel itself."""
+    page = key_cache.shape[1]
     npages = -(-rq.kv_len // page)
-    q_start = rq.q_start
-    fp8 = sp.kernel == 'sm120fp8'
-    if fp8 and cfg['fp8_kv_cache'] and _fp8_warm(layer, rq.first_page, q_start):
-        # block means, scales and the e4m3 history all continue at this chunk: read only the pages
-        # the chunk wrote (the reference gathers the whole history every chunk, sparse_prefill.py:521)
-        p0 = q_start // page
-        own = pages_row[p0:npages].long()
-        k_new, v_new = key_cache[own].reshape(-1, Hk, D), value_cache[own].reshape(-1, Hk, D)
-        km = _cached_block_means(layer, rq.first_page, key_r, q_start, rq.kv_len)
-        scales = _cached_scales(layer, rq.first_page, q_r, None, None, q_start, per_head=cfg.get('fp8_scales') == 'head')
-        kv8 = _cached_kv8(layer, rq.first_page, k_new, v_new, q_start, rq.kv_len, scales, k_row0=p0 * page)
-        sp.forward_sm120fp8(q_r, None, None, q_start, out=o_r, km=km, scales=scales, kv8=kv8, k_rows=npages * page)
+    q_start, kv_len = rq.q_start, rq.kv_len
+    table = pages_row[:npages]
+    if table.dtype != torch.int32 or not table.is_contiguous():
+        table = table.to(torch.int32).contiguous()
+    k_src, v_src = _PagedRows(key_cache, table, kv_len), _PagedRows(value_cache, table, kv_len)
+    per_head = cfg.get('fp8_scales') == 'head'
+    if sp.kernel != 'sm120fp8':
+        km = _cached_block_means(layer, rq.first_page, key_r, q_start, kv_len, key_all=k_src)
+        if ops.paged_attention_supported(page) and not FP8_EMULATE:
+            sp.forward_sm120(q_r, None, None, q_start, out=o_r, km=km, kv_pages=(key_cache, value_cache, table))
+        else:                                  # page sizes the kernel does not read in place: gather
+            pages = table.long()
+            Hk, D = key_cache.shape[2], key_cache.shape[3]
+            sp.forward_sm120(q_r, key_cache[pages].reshape(-1, Hk, D), value_cache[pages].reshape(-1, Hk, D), q_start,
+                             out=o_r, km=km)
         return
-    pages = pages_row[:npages].long()
-    k_all = key_cache[pages].reshape(npages * page, Hk, D)      # the request's keys and values, NHD
-    v_all = value_cache[pages].reshape(npages * page, Hk, D)
-    km = _cached_block_means(layer, rq.first_page, key_r, q_start, rq.kv_len, key_all=k_all)
-    if not fp8:
-        sp.forward_sm120(q_r, k_all, v_all, q_start, out=o_r, km=km)
-        return
-    scales = _cached_scales(layer, rq.first_page, q_r, k_all[:rq.kv_len], v_all[:rq.kv_len], q_start,
-                            per_head=cfg.get('fp8_scales') == 'head')
-    kv8 = _cached_kv8(layer, rq.first_page, k_all, v_all, q_start, rq.kv_len, scales) if cfg['fp8_kv_cache'] else None
-    sp.forward_sm120fp8(q_r, k_all, v_all, q_start, out=o_r, km=km, scales=scales, kv8=kv8)
+    if cfg['fp8_kv_cache'] and _fp8_warm(layer, rq.first_page, q_start):
+        # block means, scales and the e4m3 history all continue at this chunk: only the chunk's own
+        # rows are read, its keys once for both their block means and their e4m3 copy
+        scales = _cached_scales(layer, rq.first_page, q_r, None, None, q_start, per_head=per_head)
+        entry, lo = _kv8_entry(layer, rq.first_page, q_start, kv_len, scales, key_r.shape[1], key_r.shape[2],
+                               q_r.device)
+        if lo != q_start:
+            raise RuntimeError('FP8 KV cache entry does not continue at the chunk')
+        km = _cached_block_means(layer, rq.first_page, key_r, q_start, kv_len, q8=entry['k8'][q_start:kv_len],
+                                 inv_scale=entry['inv'][0])
+        _quantize_into(v_src, q_start, kv_len, 0, entry['inv'][1], entry['v8'])
+        entry['rows'] = kv_len
+        kv8 = (entry['k8'][:kv_len], entry['v8'][:kv_len])
+    else:
+        km = _cached_block_means(layer, rq.first_page, key_r, q_start, kv_len, key_all=k_src)
+        scales = _cached_scales(layer, rq.first_page, q_r, k_src, v_src, q_start, per_head=per_head)
+        if cfg['fp8_kv_cache']:
+            kv8 = _cached_kv8(layer, rq.first_page, k_src, v_src, q_start, kv_len, scales)
+        else:
+            kv8 = _kv8_scratch(k_src, v_src, kv_len, scales, q_r.device)
+    sp.forward_sm120fp8(q_r, None, None, q_start, out=o_r, km=km, scales=scales, kv8=kv8, k_rows=npages * page)
 
 
 def _dense_request(impl, query, key_cache, value_cache, output, bt_row, n, kv_len):

@@ -332,19 +332,25 @@ def test_dropin_kernels_match_reference_semantics():
     assert rel_l2(f32(o8d), O.attention_ref(*deq, kv - n)) < 3e-2
 
 
-@pytest.mark.parametrize('kv_cache,scale_mode', [(False, 'tensor'), (True, 'tensor'), (True, 'head')])
-def test_try_sparse_forward_paged(ksp, monkeypatch, kv_cache, scale_mode):
+@pytest.mark.parametrize('kernel,kv_cache,scale_mode,page', [('sm120fp8', False, 'tensor', 16),
+                                                               ('sm120fp8', True, 'tensor', 16),
+                                                               ('sm120fp8', True, 'head', 16),
+                                                               ('sm120', False, 'tensor', 16),
+                                                               ('sm120', False, 'tensor', 24)])
+def test_try_sparse_forward_paged(ksp, monkeypatch, kernel, kv_cache, scale_mode, page):
     """The vLLM hook with a paged KV cache and fake metadata: eligible requests go through the sparse path
-    and match a direct forward_sm120fp8 call (with and without the FP8 KV cache, per-tensor or per-head
-    e4m3 scales); the ineligible one is handed to _dense_request."""
+    and match a direct forward_sm120fp8 / forward_sm120 call on the gathered history (FP8 with and
+    without the FP8 KV cache, per-tensor or per-head e4m3 scales; BF16 reading the pages in place, and
+    gathering them for a page size the kernel does not read in place); the ineligible one is handed to
+    _dense_request."""
     ksp.BLOCK = 64
     monkeypatch.setattr(ksp, '_CONFIG', {'enabled': True, 'tau': 0.95, 'min_kv': 2048, 'min_q': 512,
-                                         'kernel': 'sm120fp8', 'fp8_pipeline': 'tma', 'fp8_kv_cache': kv_cache,
+                                         'kernel': kernel, 'fp8_pipeline': 'tma', 'fp8_kv_cache': kv_cache,
                                          'fp8_scales': scale_mode})
     ksp._STATE.clear()
     dense_calls = []
     monkeypatch.setattr(ksp, '_dense_request', lambda *a: dense_calls.append(a[-2:]))
-    H, Hk, D, page = 8, 2, 128, 16
+    H, Hk, D = 8, 2, 128
     reqs = [(1024, 3072), (16, 4000), (600, 2600)]          # (query len, kv len)
     npages = [-(-kv // page) for _, kv in reqs]
     nblocks = sum(npages) + 4
@@ -379,17 +385,21 @@ def test_try_sparse_forward_paged(ksp, monkeypatch, kv_cache, scale_mode):
         kfull = key_cache[bt[r, :npages[r]].long()].reshape(-1, Hk, D)
         vfull = value_cache[bt[r, :npages[r]].long()].reshape(-1, Hk, D)
         q_r = query[qsl[r]:qsl[r + 1]]
+        full = kv // 64
+        km = torch.zeros(Hk, -(-kv // 64), D, device=DEV)
+        km[:, :full] = kfull[:full * 64].float().view(full, 64, Hk, D).mean(1).transpose(0, 1)
+        if kv % 64:      # the hook's cache path averages a partial last block over its present rows
+            km[:, full] = kfull[full * 64:kv].float().mean(0)
+        if kernel == 'sm120':
+            o = sp2.forward_sm120(q_r, kfull, vfull, kv - ql, km=km.contiguous())
+            assert rel_l2(f32(output[qsl[r]:qsl[r + 1]]), f32(o)) < 1e-6
+            continue
         if scale_mode == 'head':
             scales = tuple(tuple(float(a) * ksp.SCALE_MARGIN / 448.0 for a in t.float().abs().amax(dim=(0, 2)).tolist())
                            for t in (q_r, kfull[:kv], vfull[:kv]))
         else:
             scales = tuple(float(t.float().abs().amax()) * ksp.SCALE_MARGIN / 448.0
                            for t in (q_r, kfull[:kv], vfull[:kv]))
-        full = kv // 64
-        km = torch.zeros(Hk, -(-kv // 64), D, device=DEV)
-        km[:, :full] = kfull[:full * 64].float().view(full, 64, Hk, D).mean(1).transpose(0, 1)
-        if kv % 64:      # the hook's cache path averages a partial last block over its present rows
-            km[:, full] = kfull[full * 64:kv].float().mean(0)
         o = sp2.forward_sm120fp8(q_r, kfull, vfull, kv - ql, km=km.contiguous(), scales=scales)
         assert rel_l2(f32(output[qsl[r]:qsl[r + 1]]), f32(o)) < 1e-6
     assert torch.all(output[qsl[1]:qsl[2]] == 0)
@@ -398,9 +408,10 @@ def test_try_sparse_forward_paged(ksp, monkeypatch, kv_cache, scale_mode):
 
 def test_hook_fp8_kv_cache_reads_only_chunk_pages(ksp, monkeypatch):
     """Three chunks of one request through the vLLM hook (1000-row chunks: boundaries off the page
-    and block grid).  With the FP8 KV cache on, chunks after the first read only their own pages of
-    the paged cache (the block means, scales and e4m3 history are cached) and give the same output,
-    bit for bit, as the path that gathers and re-quantises the whole history every chunk."""
+    and block grid).  With the FP8 KV cache on, chunks after the first read only their own rows (the
+    block means, scales and e4m3 history are cached): the chunk's keys once, for their block means
+    and e4m3 copy together, and its values from the pages.  The output is the same, bit for bit, as
+    the path that re-quantises the whole history from the pages every chunk."""
     ksp.BLOCK = 64
     H, Hk, D, page, n, chunks = 8, 2, 128, 16, 1000, 3
     total = n * chunks
@@ -414,13 +425,18 @@ def test_hook_fp8_kv_cache_reads_only_chunk_pages(ksp, monkeypatch):
     value_cache[perm.long()] = F.pad(vd, (0, 0, 0, 0, 0, npages_all * page - total)).view(npages_all, page, Hk, D)
     bt = perm.to(torch.int32).view(1, -1)
     calls = []
-    real = ksp._cached_kv8
+    real_q, real_m = ksp.ops.quantize_paged, ksp.ops.block_means
 
-    def spy(*a, **kw):
-        calls.append((a[2].shape[0], kw.get('k_row0', 0)))
-        return real(*a, **kw)
-    monkeypatch.setattr(ksp, '_cached_kv8', spy)
-    outs = {}
+    def spy_q(cache, table, row0, scale, mode, out):
+        calls.append(('q', row0, out.shape[0]))
+        return real_q(cache, table, row0, scale, mode, out)
+
+    def spy_m(x, pos0, block, out, out_block0, q8=None, inv_scale=None, fixed_divisor=0):
+        calls.append(('m', pos0, x.shape[0], q8 is not None))
+        return real_m(x, pos0, block, out, out_block0, q8=q8, inv_scale=inv_scale, fixed_divisor=fixed_divisor)
+    monkeypatch.setattr(ksp.ops, 'quantize_paged', spy_q)
+    monkeypatch.setattr(ksp.ops, 'block_means', spy_m)
+    outs, log = {}, {}
     for kv_cache in (False, True):
         monkeypatch.setattr(ksp, '_CONFIG', {'enabled': True, 'tau': 0.95, 'min_kv': 512, 'min_q': 512,
                                              'kernel': 'sm120fp8', 'fp8_pipeline': 'tma', 'fp8_kv_cache': kv_cache})
@@ -433,13 +449,19 @@ def test_hook_fp8_kv_cache_reads_only_chunk_pages(ksp, monkeypatch):
                                          query_start_loc=torch.tensor([0, n], dtype=torch.int32, device=DEV),
                                          seq_lens=torch.tensor([kv_len], dtype=torch.int32, device=DEV), block_table=bt)
             out = torch.zeros(n, H, D, dtype=torch.bfloat16, device=DEV)
+            calls.clear()
             assert ksp.try_sparse_forward(impl, qd[c0:kv_len], kd[c0:kv_len], key_cache, value_cache, out, meta)
             outs[kv_cache].append(out)
+            log[kv_cache, c] = list(calls)
     torch.cuda.synchronize()
     for a, b in zip(outs[False], outs[True]):
         assert torch.equal(a, b)
-    # cache on: chunk 0 builds the entry from the full gather, chunks 1 and 2 pass only their pages
-    assert calls[0] == (-(-n // page) * page, 0)
-    for c in (1, 2):
-        p0 = c * n // page
-        assert calls[c] == ((-(-(c + 1) * n // page) - p0) * page, p0 * page)
+    for c in range(chunks):
+        c0, kv_len = c * n, (c + 1) * n
+        # cache off: every chunk quantises the whole history from the pages (no gather)
+        assert [x for x in log[False, c] if x[0] == 'q'] == [('q', 0, kv_len), ('q', 0, kv_len)]
+        if c == 0:                 # cache on, first chunk: the entry is built from the pages
+            assert [x for x in log[True, c] if x[0] == 'q'] == [('q', 0, kv_len), ('q', 0, kv_len)]
+        else:                      # later chunks: keys once (means + e4m3 together), values' own rows
+            assert [x for x in log[True, c] if x[0] == 'q'] == [('q', c0, n)]
+            assert ('m', c0, n, True) in log[True, c]

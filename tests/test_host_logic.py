@@ -36,8 +36,19 @@ def ksp(monkeypatch):
         a = x.float().abs()
         return a.amax(dim=(0, 2)) if per_head else a.amax().reshape(1)
 
+    def gathered(cache, table):
+        return cache[table.long()].reshape(-1, cache.shape[2], cache.shape[3])
+
+    def fake_block_means_paged(cache, table, pos0, n, block, out, out_block0):
+        fake_block_means(gathered(cache, table)[pos0:pos0 + n], pos0, block, out, out_block0)
+
+    def fake_absmax_paged(cache, table, row0, rows, per_head, out=None):
+        return fake_absmax(gathered(cache, table)[row0:row0 + rows], per_head)
+
     monkeypatch.setattr(ops, 'block_means', fake_block_means)
     monkeypatch.setattr(ops, 'absmax', fake_absmax)
+    monkeypatch.setattr(ops, 'block_means_paged', fake_block_means_paged)
+    monkeypatch.setattr(ops, 'absmax_paged', fake_absmax_paged)
     m._KMEAN_CACHE.clear()
     m._SCALE_CACHE.clear()
     m._KV8_CACHE.clear()
@@ -280,23 +291,115 @@ def test_cached_block_means_random_sequences(ksp):
     @given(block=st.sampled_from([64, 128]),
            steps=st.lists(st.tuples(st.integers(1, 700), st.sampled_from(['next', 'restart', 'gap']),
                                     st.integers(1, 300)), min_size=1, max_size=6),
-           seed=st.integers(0, 2 ** 16))
-    def check(block, steps, seed):
+           seed=st.integers(0, 2 ** 16), page=st.sampled_from([0, 16, 48]))
+    def check(block, steps, seed, page):
         ksp.BLOCK = block
         ksp._KMEAN_CACHE.clear()
         oracle = O.KMeanCacheOracle(block)
         keys = torch.randn(6 * 1000 + 8, 2, 8, generator=torch.Generator().manual_seed(seed)).to(torch.bfloat16)
         kf = keys.float().numpy()
+        paged = _paged_copy(keys, page, seed) if page else None
         end = 0
         for n, kind, gap in steps:
             q_start = 0 if kind == 'restart' or end == 0 else end + (gap if kind == 'gap' else 0)
             kv_len = q_start + n
-            got = ksp._cached_block_means('fuzz', 7, keys[q_start:kv_len], q_start, kv_len, key_all=keys)
+            hist = ksp._PagedRows(paged[0], paged[1], kv_len) if page else keys
+            got = ksp._cached_block_means('fuzz', 7, keys[q_start:kv_len], q_start, kv_len, key_all=hist)
             ref = oracle.update('fuzz', 7, kf[q_start:kv_len], q_start, kv_len, key_all=kf)
             np.testing.assert_array_equal(got.numpy(), ref)
             assert ksp._KMEAN_CACHE[('fuzz', 7)]['last_kv'] == kv_len
             end = kv_len
     check()
+
+
+def _paged_copy(x, page, seed):
+    """x [rows, heads, D] spread over shuffled pages of a cache with spare pages: (cache, int32 table)."""
+    npages = -(-x.shape[0] // page)
+    total = npages + 3
+    perm = torch.randperm(total, generator=torch.Generator().manual_seed(seed))[:npages]
+    cache = torch.full((total, page) + tuple(x.shape[1:]), float('nan'), dtype=x.dtype)
+    padded = torch.cat([x, x.new_zeros((npages * page - x.shape[0],) + tuple(x.shape[1:]))])
+    cache[perm] = padded.view((npages, page) + tuple(x.shape[1:]))
+    return cache, perm.to(torch.int32)
+
+
+def test_paged_sources_match_gathered(ksp, monkeypatch):
+    """The hook's caches built from _PagedRows (the pages read in place) equal the ones built from the
+    gathered history: block-mean rebuilds (chunk starting on and inside a block), scales per tensor and
+    per head, and the FP8 KV cache."""
+    from sm120_attn import ops
+    quant_calls = []
+
+    def fake_quantize(x, scale, mode, out, transpose=False, rows_pad=0):
+        out.copy_((x.float() * scale.reshape(1, -1, 1)).round().clamp(-100, 100).to(torch.int8).view(torch.uint8))
+
+    def fake_quantize_paged(cache, table, row0, scale, mode, out):
+        quant_calls.append((row0, out.shape[0]))
+        rows = cache[table.long()].reshape(-1, cache.shape[2], cache.shape[3])
+        fake_quantize(rows[row0:row0 + out.shape[0]], scale, mode, out)
+
+    monkeypatch.setattr(ops, 'quantize', fake_quantize)
+    monkeypatch.setattr(ops, 'quantize_paged', fake_quantize_paged)
+    ksp.BLOCK = 64
+    g = torch.Generator().manual_seed(5)
+    k = torch.randn(3000, 2, 8, generator=g).to(torch.bfloat16)
+    v = torch.randn(3000, 2, 8, generator=g).to(torch.bfloat16)
+    q = torch.randn(500, 4, 8, generator=g).to(torch.bfloat16)
+    kc, table = _paged_copy(k, 16, 1)
+    vc, _ = _paged_copy(v, 16, 1)
+    for q_start in (1024, 1000):
+        kv_len = q_start + 500
+        kp = ksp._PagedRows(kc, table, kv_len)
+        ksp._KMEAN_CACHE.clear()
+        a = ksp._cached_block_means('P', 1, k[q_start:kv_len], q_start, kv_len, key_all=kp).clone()
+        ksp._KMEAN_CACHE.clear()
+        b = ksp._cached_block_means('P', 1, k[q_start:kv_len], q_start, kv_len, key_all=k[:kv_len])
+        assert torch.equal(a, b)
+    for per_head in (False, True):
+        ksp._SCALE_CACHE.clear()
+        sa = ksp._cached_scales('P', 1, q, ksp._PagedRows(kc, table, 1500), ksp._PagedRows(vc, table, 1500), 1000,
+                                per_head=per_head)
+        ksp._SCALE_CACHE.clear()
+        sb = ksp._cached_scales('P', 1, q, k[:1500], v[:1500], 1000, per_head=per_head)
+        assert sa == sb
+    sc = (0.1, 0.02, 0.03)
+    ksp._KV8_CACHE.clear()
+    k8a, v8a = ksp._cached_kv8('P', 1, ksp._PagedRows(kc, table, 1500), ksp._PagedRows(vc, table, 1500), 1000, 1500,
+                               sc)
+    assert quant_calls == [(0, 1500), (0, 1500)]
+    k8a, v8a = k8a.clone(), v8a.clone()
+    ksp._KV8_CACHE.clear()
+    k8b, v8b = ksp._cached_kv8('P', 1, k, v, 1000, 1500, sc)
+    assert torch.equal(k8a, k8b) and torch.equal(v8a, v8b)
+    ksp._KV8_CACHE.clear()
+
+
+def test_km_slot_written_bookkeeping(ksp):
+    """km_slot hands the producer of a chunk's keys the entry's km to write the block means into (a new
+    request, or one continuing at q_start); _cached_block_means(written=True) then records the chunk.
+    A gap gives no slot (the unfused path rebuilds), and `written` without a slot is an error."""
+    ksp.BLOCK = 64
+    k = torch.randn(3000, 2, 8, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    km = ksp.km_slot('S', 0, 0, 1000, 2, 8, 'cpu')
+    assert km is not None and km.shape[1] >= 16
+    from sm120_attn import ops
+    ops.block_means(k[:1000], 0, 64, km, 0)                  # the producer's write
+    got = ksp._cached_block_means('S', 0, k[:1000], 0, 1000, written=True)
+    entry = ksp._KMEAN_CACHE[('S', 0)]
+    assert entry['nb'] == 16 and entry['last_kv'] == 1000 and 'slot' not in entry
+    _, ref = O.block_means(k[:1000].float().numpy(), 0, 64)
+    np.testing.assert_array_equal(got.numpy(), ref)
+    km2 = ksp.km_slot('S', 0, 1000, 1800, 2, 8, 'cpu')      # continues: the same entry
+    assert km2 is entry['km']
+    ops.block_means(k[1000:1800], 1000, 64, km2, 0)
+    got2 = ksp._cached_block_means('S', 0, k[1000:1800], 1000, 1800, written=True)
+    ref2 = O.KMeanCacheOracle(64)
+    ref2.update('S', 0, k[:1000].float().numpy(), 0, 1000)
+    want = ref2.update('S', 0, k[1000:1800].float().numpy(), 1000, 1800)
+    np.testing.assert_array_equal(got2.numpy(), want)
+    assert ksp.km_slot('S', 0, 2000, 2500, 2, 8, 'cpu') is None   # gap: rebuilt by the unfused path
+    with pytest.raises(RuntimeError):
+        ksp._cached_block_means('S', 0, k[2000:2500], 2000, 2500, written=True)
 
 
 def test_host_metadata_read_once_per_step(ksp):
