@@ -412,6 +412,8 @@ def run_b200(args):
         'clocks': clk,
     }
     line['check'] = check
+    if not args.no_also and not n_failed:
+        line['config']['also'] = secondary_figures(args, h, hk, dev, rank, world)
     if args.ttft_tokens > 0 and not n_failed:
         # second half of the metric: prefill TTFT of the config-5 decoder, measured on the same ranks
         # after the chunk workload (its tensors released first)
@@ -434,6 +436,70 @@ def run_b200(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _chunk_variant(args, h, hk, dev, rank, world, strength):
+    """The default chunk step at another injection strength, device-resident: max-over-ranks ms per
+    step, kept fraction, executed-tile TFLOPS and the attention launch's ms."""
+    import torch
+    import sm120_attn.sparse_prefill as ksp
+    from sm120_attn.shard import reduce_over_ranks
+    q, k, v = make_rank_inputs(hk, 1000 + rank, strength, dev)
+    sp = ksp.SparsePrefill(h, hk, D, dev, tau=TAU, min_kv=0, min_q=0, kernel='sm120fp8')
+    out = torch.empty(N_Q, h, D, dtype=torch.bfloat16, device=dev)
+    layer = 'bench-' + strength
+    ksp._cached_block_means(layer, 0, k[:Q_START], 0, Q_START)
+    scales = ksp._cached_scales(layer, 0, q, k, v, 0)
+
+    def rewind():
+        e = ksp._KMEAN_CACHE[(layer, 0)]
+        e['last_kv'], e['nb'] = Q_START, Q_START // BLOCK
+
+    def step():
+        km = ksp._cached_block_means(layer, 0, k[Q_START:], Q_START, KV)
+        sp.forward_sm120fp8(q, k, v, Q_START, out=out, km=km, scales=scales)
+    for _ in range(args.warmup):
+        rewind()
+        step()
+    sp.kernel_events = []
+    ms = _timed(step, args.steps, dev, world, before=rewind)
+    attn = [a.elapsed_time(b) for a, b in sp.kernel_events]
+    sp.kernel_events = None
+    kept_blocks = int(sp.last_counts.sum().item())
+    causal_blocks = h * ((Q_START // BLOCK) * (N_Q // BLOCK) + (N_Q // BLOCK) * (N_Q // BLOCK + 1) // 2)
+    (ms, attn_ms), (tile_flops, kept_sum, causal_sum) = reduce_over_ranks(
+        [ms, sum(attn) / max(len(attn), 1)], [kept_blocks * 4.0 * D * 128 * 128, kept_blocks, causal_blocks],
+        device=dev)
+    del ksp._KMEAN_CACHE[(layer, 0)]
+    return {'injection': strength, 'kept_fraction': round(kept_sum / causal_sum, 4),
+            'ms_per_step': round(ms / args.steps, 4),
+            'tflops_executed': round(tile_flops * args.steps / (ms * 1e-3) / 1e12, 1),
+            'attn_ms_per_launch': round(attn_ms, 4)}
+
+
+def secondary_figures(args, h, hk, dev, rank, world):
+    """The benchmark's other configurations, measured in the same run on the same ranks (device-resident,
+    CUDA events, max over ranks): the chunk at strong injection, dense causal FP8 (tau 1, config 3) and
+    the selection of one chunk (config 2)."""
+    import types
+    from sm120_attn.shard import reduce_over_ranks
+    sub = types.SimpleNamespace(**{**vars(args), 'steps': max(3, min(args.steps, 10))})
+    also = {'strong_injection_chunk': _chunk_variant(sub, h, hk, dev, rank, world, 'strong')}
+    d = _dense(sub, h, hk, dev, rank)
+    (ms,), (work,) = reduce_over_ranks([d['ms']], [d['work']], device=dev)
+    also['dense_fp8'] = {'ms_per_step': round(ms / sub.steps, 4),
+                         'tflops': round(work * sub.steps / (ms * 1e-3) / 1e12, 1),
+                         'workload': d['config']['workload']}
+    sel = _selection(sub, h, hk, dev, rank)
+    (ms, kms), (work, kwork) = reduce_over_ranks([sel['ms'], sel['kernel_ms']], [sel['work'], sel['kernel_work']],
+                                                 device=dev)
+    hbm, _, _ = peaks()
+    also['selection'] = {'ms_per_step': round(ms / sub.steps, 4),
+                         'gbs': round(work * sub.steps / (ms * 1e-3) / 1e9, 1),
+                         'kernel': sel['kernel'], 'kernel_us': round(kms * 1e3, 1),
+                         'kernel_frac_of_hbm': round(kwork / (kms * 1e-3) / 1e9 / hbm, 4)}
+    also['steps'] = sub.steps
+    return also
 
 
 def _rank_env():
@@ -663,8 +729,10 @@ def _chunked(args, h, hk, dev, rank):
 def _hook(args, h, hk, dev, rank):
     """Config 4 through the vLLM hook: the 262144-token prefill in 32 chunks of 8192, each chunk a
     `try_sparse_forward` call over a paged K/V cache (page 16, pages in shuffled order, fake vLLM
-    metadata).  The reference's hook gathers the whole K/V history from the pages every chunk;
-    with --fp8-kv-cache the warm chunks read only their own pages."""
+    metadata).  The reference's hook gathers the whole K/V history from the pages every chunk; this
+    one reads the pages in place (FP8: the history re-quantised from the pages every chunk, or with
+    --fp8-kv-cache only the chunk's own rows; BF16 with --hook-kernel sm120: the attention kernel
+    reads the pages itself)."""
     import types
     import torch
     import sm120_attn.sparse_prefill as ksp
@@ -682,7 +750,8 @@ def _hook(args, h, hk, dev, rank):
     value_cache[perm.long()] = v.view(npages, page, hk, D)
     del v
     bt = perm.to(torch.int32).view(1, -1)
-    ksp._CONFIG = {'enabled': True, 'tau': TAU, 'min_kv': 8192, 'min_q': 1024, 'kernel': 'sm120fp8',
+    fp8 = args.hook_kernel == 'sm120fp8'
+    ksp._CONFIG = {'enabled': True, 'tau': TAU, 'min_kv': 8192, 'min_q': 1024, 'kernel': args.hook_kernel,
                    'fp8_pipeline': 'tma', 'fp8_kv_cache': bool(args.fp8_kv_cache)}
     ksp._STATE.clear()
     impl = types.SimpleNamespace(sliding_window=(-1, -1), scale=D ** -0.5)
@@ -714,15 +783,18 @@ def _hook(args, h, hk, dev, rank):
     exec_flops = sum(int(n.item()) * 4.0 * D * 128 * 128 for _, _, n in per_chunk)
     ops.check_status(dev)
     ksp._CONFIG = None
+    if fp8:
+        how = ('FP8 KV cache: warm chunks read only their own rows' if args.fp8_kv_cache else
+               'whole K/V history re-quantised from the pages in place every chunk (the reference gathers it first)')
+    else:
+        how = 'BF16 attention reading K/V from the pages in place (TMA boxes per page)'
     return {'ms': ms, 'steps': steps, 'e2e_ms': None, 'work': exec_flops, 'unit': 'TFLOPS', 'scale': 1e12,
-            'kernel': 'attn_fwd_kernel<fp8>', 'kernel_ms': None, 'kernel_work': None, 'bound': 'tensor',
-            'h2d': 0, 'd2h': 0, 'launches': 7 * (total // chunk),
+            'kernel': 'attn_fwd_kernel<fp8>' if fp8 else 'attn_fwd_kernel<bf16>', 'kernel_ms': None,
+            'kernel_work': None, 'bound': 'tensor', 'h2d': 0, 'd2h': 0, 'launches': 7 * (total // chunk),
+            'dtype': None if fp8 else 'bf16 (fp32 accumulate)',
             'config': {'workload': f'chunked prefill of {total} tokens in {total // chunk} chunks of {chunk} through '
                                    f'the vLLM hook (try_sparse_forward) over a paged K/V cache (page {page}, shuffled '
-                                   f'pages); H {h}/Hk {hk}/D {D}, block {BLOCK}, tau {TAU}; C4 injection; '
-                                   + ('FP8 KV cache: warm chunks read only their own pages'
-                                      if args.fp8_kv_cache else 'whole K/V history gathered and re-quantised every '
-                                                                'chunk (reference behaviour)'),
+                                   f'pages); H {h}/Hk {hk}/D {D}, block {BLOCK}, tau {TAU}; C4 injection; ' + how,
                        'ms_per_chunk': [round(x, 3) for x in chunk_ms],
                        'value_definition': 'executed-tile FLOPs / prefill time (host metadata reads included)'}}
 
@@ -1123,6 +1195,10 @@ def main():
                          'this many tokens (config.ttft; 0 skips it)')
     ap.add_argument('--fp8-kv-cache', action='store_true',
                     help='chunked / hook workloads: keep e4m3 K/V across chunks (SM120_SPARSE_FP8_KV_CACHE)')
+    ap.add_argument('--hook-kernel', default='sm120fp8', choices=['sm120fp8', 'sm120'],
+                    help='hook workload: the FP8 kernel (default) or the BF16 kernel reading the pages in place')
+    ap.add_argument('--no-also', action='store_true',
+                    help='default workload: skip the secondary figures (strong injection, dense, selection)')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'b200':
         print('note: warmup raised to 3', file=sys.stderr)
