@@ -29,6 +29,8 @@ struct Params {
     // plain loads of the one box that holds the last key when kv_len ends inside it.
     const int32_t* pages;
     int page, box_rows, num_pages;
+    int box_shift, page_shift, last_box0;   // log2(box_rows); log2(page) or -1; first key of the
+                                            // box holding the last key when kv_len ends inside it, or -1
     const uint16_t* kc;
     const uint16_t* vc;
     int64_t kv_ps, kv_rs, kv_hs;

@@ -73,51 +73,60 @@ struct Cfg {
 #endif
 constexpr int TILE_EXP_POLY = SA_TILE_EXP_POLY;
 
-// Paged K/V (BF16 kernel).  Page id of box `lane` of the 64-key tile at kb (0 for lanes past the
-// tile's boxes or boxes past the last key; an id outside [0, num_pages) sets SA_DEV_BAD_PAGE and
-// reads as zeros, through TMA's bounds or the guarded plain loads).
-__device__ __forceinline__ int box_page(const Params& p, int kb, int lane) {
-    const int key0 = kb + lane * p.box_rows;
-    if (lane >= 64 / p.box_rows || key0 >= p.kv_len) return 0;
-    return __ldg(p.pages + key0 / p.page);
+// Paged K/V (BF16 kernel).  The BF16 kernel has two K/V stages, so the load of tile u+2 starts
+// only once O += P(u) V_u has freed its stage and sits on the critical path: everything a paged
+// stage needs beyond the TMA issue is worked out before the stage-empty wait.  Lane i < 64 / box_rows
+// owns box i of the tile (keys kb + i * box_rows ..): the TMA coordinates of its page (slot, page),
+// or an out-of-range page coordinate (zero fill) when the box starts at or past kv_len or its page
+// id is outside [0, num_pages) (SA_DEV_BAD_PAGE).  `tail` is the box that holds the last key when
+// kv_len ends inside it (-1 otherwise).
+struct PagedBox {
+    int slot, page, tail;
+    bool bad;
+};
+
+__device__ __forceinline__ PagedBox paged_box(const Params& p, int kb, int lane) {
+    PagedBox b;
+    const int key0 = kb + (lane << p.box_shift);
+    b.slot = 0;
+    b.page = p.num_pages;
+    bool bad = false;
+    if (lane < (64 >> p.box_shift) && key0 < p.kv_len) {
+        const int pi = p.page_shift >= 0 ? key0 >> p.page_shift : key0 / p.page;
+        const int id = __ldg(p.pages + pi);
+        bad = static_cast<unsigned>(id) >= static_cast<unsigned>(p.num_pages);
+        b.page = bad ? p.num_pages : id;
+        b.slot = key0 - pi * p.page;
+    }
+    b.bad = __any_sync(0xffffffffu, bad);
+    b.tail = (p.last_box0 >= kb && p.last_box0 < kb + 64) ? (p.last_box0 - kb) >> p.box_shift : -1;
+    return b;
 }
 
-// One K/V stage of a paged cache: box i of the tile (keys kb + i * box_rows ..) is a 4D TMA load
-// from page pages[key / page] at slot key % page, or an out-of-range page coordinate (zero fill)
-// when the box starts at or past kv_len.  The box that holds the last key when kv_len ends inside
-// it is read by the warp's lanes with plain loads instead (rows past kv_len written as zeros, as
-// TMA's bounds would give a contiguous K/V), stored at the 128-byte-swizzled places TMA would use
-// (16-byte chunk c of tile row R at chunk c ^ (R % 8) of the row), then fenced for the tensor
-// cores before the stage barrier is armed with the remaining bytes.
+// One K/V stage of a paged cache, after the stage-empty wait.  The tail box is read by the warp's
+// lanes with plain 16-byte loads instead of TMA (rows past kv_len written as zeros, as TMA's bounds
+// give a contiguous K/V), stored at the 128-byte-swizzled places TMA would use (16-byte chunk c of
+// tile row R at chunk c ^ (R % 8) of the row) and fenced for the tensor cores.  Lane 0 then arms the
+// stage barrier with the remaining bytes and every lane issues the 4D TMA loads of its own box.
 template <class C>
 __device__ __forceinline__ void load_paged_stage(const Params& p, uint8_t* dst, uint32_t full, const CUtensorMap* tmK,
-                                                 const CUtensorMap* tmV, int kb, int hk, int lane, int my_page,
+                                                 const CUtensorMap* tmV, int kb, int hk, int lane, const PagedBox& b,
                                                  volatile int* kb_slot) {
     static_assert(C::E == 2, "paged stages are bf16");
-    const int br = p.box_rows;
-    const int nbox = 64 / br;
-    const bool bad = static_cast<unsigned>(my_page) >= static_cast<unsigned>(p.num_pages);
-    if (__any_sync(0xffffffffu, bad) && lane == 0 && p.status) atomicOr(p.status, SA_DEV_BAD_PAGE);
-    if (bad) my_page = p.num_pages;                          // TMA: out of range, zero fill
-    int pg[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) pg[i] = __shfl_sync(0xffffffffu, my_page, i);
-    const int last0 = ((p.kv_len - 1) / br) * br;           // first key of the box holding the last key
-    const int tail = (p.kv_len % br != 0 && last0 >= kb && last0 < kb + 64) ? (last0 - kb) / br : -1;
+    const int br = 1 << p.box_shift;
+    if (b.bad && lane == 0 && p.status) atomicOr(p.status, SA_DEV_BAD_PAGE);
     uint32_t tail_bytes = 0;
-    if (tail >= 0) {
-        int tp = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) if (i == tail) tp = pg[i];
+    if (b.tail >= 0) {
+        const int tp = __shfl_sync(0xffffffffu, b.page, b.tail);
+        const int slot0 = __shfl_sync(0xffffffffu, b.slot, b.tail);
         const bool tp_ok = tp < p.num_pages;
-        const int valid = p.kv_len - last0;
-        const int slot0 = last0 % p.page;
+        const int valid = p.kv_len - p.last_box0;
         const int chunks = br * 16;                          // 16-byte chunks of the box's K rows (and V rows)
         for (int i = lane; i < 2 * chunks; i += 32) {
             const bool isv = i >= chunks;
             const int ii = isv ? i - chunks : i;
             const int rr = ii >> 4, c = ii & 15;
-            const int R = tail * br + rr;                    // row of the 64-key tile
+            const int R = b.tail * br + rr;                  // row of the 64-key tile
             uint4 val = make_uint4(0u, 0u, 0u, 0u);
             if (rr < valid && tp_ok) {
                 const uint16_t* base = isv ? p.vc : p.kc;
@@ -133,22 +142,17 @@ __device__ __forceinline__ void load_paged_stage(const Params& p, uint8_t* dst, 
         tail_bytes = static_cast<uint32_t>(2 * br * 256);
     }
     __syncwarp();
-    if (elect_one()) {
+    if (lane == 0) {
         *kb_slot = kb;
         mbar_arrive_expect_tx(full, C::STAGE - tail_bytes);
+    }
+    __syncwarp();
+    if (lane < (64 >> p.box_shift) && lane != b.tail) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (i >= nbox) break;
-            if (i == tail) continue;
-            const int key0 = kb + i * br;
-            const bool past = key0 >= p.kv_len;
-            const int page = past ? p.num_pages : pg[i];
-            const int slot = past ? 0 : key0 % p.page;
-            for (int r = 0; r < C::NREG; ++r) {
-                tma_load_4d(smem_u32(dst + r * C::K_REG + i * br * 128), tmK, full, r * C::REG_ELEMS, hk, slot, page);
-                tma_load_4d(smem_u32(dst + C::K_BYTES + r * C::V_REG + i * br * 128), tmV, full, r * C::REG_ELEMS, hk,
-                            slot, page);
-            }
+        for (int r = 0; r < C::NREG; ++r) {
+            tma_load_4d(smem_u32(dst + r * C::K_REG + lane * br * 128), tmK, full, r * C::REG_ELEMS, hk, b.slot, b.page);
+            tma_load_4d(smem_u32(dst + C::K_BYTES + r * C::V_REG + lane * br * 128), tmV, full, r * C::REG_ELEMS, hk,
+                        b.slot, b.page);
         }
     }
     __syncwarp();
@@ -233,9 +237,9 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
             if constexpr (!FP8) paged = p.pages != nullptr;
             for (int t = 0;; ++t, have = w.next(kb, rm)) {
                 const int st = t % C::NST;
-                // paged K/V: lane i fetches the page id of the tile's box i while the stage drains
-                int my_page = 0;
-                if (paged && have) my_page = box_page(p, kb, lane);
+                // paged K/V: the tile's boxes are worked out while the stage drains
+                PagedBox pbox{0, 0, -1, false};
+                if (paged && have) pbox = paged_box(p, kb, lane);
                 if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bEmpty + st), ((t / C::NST) & 1) ^ 1, abort_flag,
                                                         p.status, SA_DEV_WAIT_KV)))
                     break;
@@ -250,7 +254,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                 uint8_t* dst = sKV + st * C::STAGE;
                 if constexpr (!FP8) {
                     if (paged) {
-                        load_paged_stage<C>(p, dst, smem_u32(bFull + st), &tmK, &tmV, kb, hk, lane, my_page,
+                        load_paged_stage<C>(p, dst, smem_u32(bFull + st), &tmK, &tmV, kb, hk, lane, pbox,
                                             tile_kb + st);
                         par[st] = (t / C::NST) & 1;
                         used[st] = true;
@@ -618,6 +622,11 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
         p.kv_ps = paged->page_stride;
         p.kv_rs = krs;
         p.kv_hs = khs;
+        p.box_shift = box_rows == 8 ? 3 : box_rows == 16 ? 4 : box_rows == 32 ? 5 : 6;
+        p.page_shift = -1;
+        for (int sh = 0; sh < 31; ++sh)
+            if (paged->page == (1 << sh)) p.page_shift = sh;
+        p.last_box0 = kv_len % box_rows ? ((kv_len - 1) / box_rows) * box_rows : -1;
     }
     p.counts = counts;
     p.lists = lists;
