@@ -1072,7 +1072,8 @@ def cpu_sample(strength, seconds_budget=20.0):
     while m >= 0 and t_attn < seconds_budget:
         r0 = m * BLOCK
         t0 = time.perf_counter()
-        O.attention_ref(qf[r0:r0 + BLOCK], kf, vf, Q_START + r0, masks[:, m:m + 1], q_block=BLOCK, kv_block=BLOCK)
+        O.attention_ref_threaded(qf[r0:r0 + BLOCK], kf, vf, Q_START + r0, masks[:, m:m + 1], q_block=BLOCK,
+                                 kv_block=BLOCK)
         t_attn += time.perf_counter() - t0
         kept = masks[:, m].sum()
         flops += 4.0 * D * BLOCK * BLOCK * kept
@@ -1082,9 +1083,10 @@ def cpu_sample(strength, seconds_budget=20.0):
             break
     tflops = flops / (t_attn + t_sel * done_rows / N_Q) / 1e12
     threads = torch.get_num_threads()
-    desc = (f'oracle (numpy fp32, BLAS threads) selection of 1 KV head x 8 query heads over the full chunk '
-            f'({t_sel:.2f} s) + masked fp32 attention of the last {done_rows} query rows x 8 heads '
-            f'({t_attn:.2f} s); selection time pro-rated to the sampled rows')
+    desc = (f'oracle: selection (numpy fp32) of 1 KV head x 8 query heads over the full chunk ({t_sel:.2f} s) + '
+            f'masked fp32 attention of the last {done_rows} query rows x 8 heads on all intra-op threads '
+            f'(attention_ref_threaded, the arithmetic of the reference\'s reference(); {t_attn:.2f} s); selection '
+            f'time pro-rated to the sampled rows')
     return tflops, desc, threads
 
 

@@ -231,6 +231,34 @@ SA_API int sa_attn_fwd_fp8(const uint8_t* q, int64_t q_row_stride, int64_t q_hea
                     const float* q_scale, int q_scale_stride, const float* k_scale, int k_scale_stride,
                     const float* v_scale, int v_scale_stride, float softmax_scale, int32_t* status, void* stream);
 
+/*
+ * sa_attn_fwd_fp8 with the partial last wave split.  The (query tile, head) units that fill whole
+ * waves of the GPU's resident CTAs (2 per SM) run as in sa_attn_fwd_fp8; each unit of the partial
+ * last wave (tail_units < 0; else the last tail_units units of the launch order: tiles from the last
+ * to the first, heads in order) has its walk cut into `splits` contiguous ranges of its 64-key
+ * steps, run as separate CTAs; the last of them to finish combines the ranges (the rescaled sums of
+ * their unnormalised outputs), counting arrivals in the workspace (zeroed by a memset on the stream).
+ * With few units of nearly equal cost (a tensor-parallel rank holding one or two KV heads) that last
+ * wave is otherwise mostly idle; the reference's grid has no such split (kai_fa_fp8_tma.py:447-490
+ * launches one CTA per tile and head).  Tail units whose walk has fewer than 32 * splits steps run
+ * whole.  workspace: device memory of sa_attn_split_workspace_bytes(n_q, q_front, num_heads, splits,
+ * tail_units) bytes (0 when nothing splits), 16-byte aligned; splits 1..16 (1: as sa_attn_fwd_fp8).
+ * P is rounded to e4m3 against each range's own running max, so split rows differ from the unsplit
+ * kernel's within the FP8 tolerance.  sa_attn_split_count suggests a split count for this GPU (1 when
+ * the units fill less than one wave, or no split shortens the launch by 5% or more).
+ */
+SA_API int sa_attn_split_count(int n_q, int q_front, int num_heads);
+SA_API int64_t sa_attn_split_workspace_bytes(int n_q, int q_front, int num_heads, int splits, int tail_units);
+SA_API int sa_attn_fwd_fp8_split(const uint8_t* q, int64_t q_row_stride, int64_t q_head_stride, const uint8_t* k,
+                                 int64_t k_row_stride, int64_t k_head_stride, const uint8_t* v, int64_t v_row_stride,
+                                 int64_t v_head_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,
+                                 int num_heads, int num_kv_heads, int head_dim, int kv_len, int q_front, int q_offset,
+                                 const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block,
+                                 int kv_block, const float* q_scale, int q_scale_stride, const float* k_scale,
+                                 int k_scale_stride, const float* v_scale, int v_scale_stride, float softmax_scale,
+                                 int32_t* status, int splits, int tail_units, void* workspace, int64_t workspace_bytes,
+                                 void* stream);
+
 SA_API int sa_attn_fwd_bf16(const void* q, int64_t q_row_stride, int64_t q_head_stride, const void* k,
                      int64_t k_row_stride, int64_t k_head_stride, const void* v, int64_t v_row_stride,
                      int64_t v_head_stride, void* out, int64_t o_row_stride, int64_t o_head_stride, int n_q,

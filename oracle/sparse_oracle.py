@@ -27,7 +27,7 @@ __all__ = [
     'VT_KEY_PERM', 'vt_key_index', 'permute_vt_keys',
     'block_means', 'q_block_means', 'KMeanCacheOracle', 'ScaleCacheOracle',
     'select_masks', 'pair_union', 'masks_to_lists', 'compare_masks',
-    'quantize_glue', 'quantize_per_tensor', 'attention_ref', 'attention_fp8_kernel_model',
+    'quantize_glue', 'quantize_per_tensor', 'attention_ref', 'attention_ref_threaded', 'attention_fp8_kernel_model',
     'causal_blocks', 'causal_flops',
 ]
 
@@ -404,9 +404,44 @@ def attention_ref(q, k, v, q_pos0: int, masks=None, q_block: int = 64, kv_block:
     return out
 
 
+def attention_ref_threaded(q, k, v, q_pos0: int, masks=None, q_block: int = 64, kv_block: int = 64, q_front: int = 0,
+                           scale: float | None = None):
+    """attention_ref with the same fp32 arithmetic run through PyTorch on the host cores (all intra-op
+    threads), as the reference's own CPU path runs (`reference()`, sparse_prefill.py:262-279: per
+    head, fp32 scores, masked fill, softmax, P.V).  The CPU baseline of the benchmark times this so
+    that the restatement runs at the reference's own CPU speed (numpy's elementwise passes are single
+    threaded).  Same arguments and result as attention_ref."""
+    import torch
+    qt = torch.from_numpy(np.ascontiguousarray(q, dtype=F32))
+    kt = torch.from_numpy(np.ascontiguousarray(k, dtype=F32))
+    vt = torch.from_numpy(np.ascontiguousarray(v, dtype=F32))
+    n, H, D = qt.shape
+    N, Hk, _ = kt.shape
+    g = H // Hk
+    sc = float(F32(D ** -0.5 if scale is None else scale))
+    allowed = torch.arange(N)[None, :] <= (q_pos0 + torch.arange(n))[:, None]
+    rows = (torch.arange(n) + q_front) // q_block                 # mask row of each query row
+    out = torch.empty((n, H, D), dtype=torch.float32)
+    for h in range(H):
+        s_ = (qt[:, h] @ kt[:, h // g].T) * sc
+        if masks is None:
+            m = allowed
+        else:
+            mh = torch.from_numpy(np.ascontiguousarray(masks[h], dtype=bool))[rows]          # [n, NBc]
+            nbc = mh.shape[1]
+            full = mh[:, :, None].expand(n, nbc, kv_block).reshape(n, nbc * kv_block)     # key j -> j // kv_block
+            if full.shape[1] < N:
+                full = torch.cat([full, full.new_zeros(n, N - full.shape[1])], 1)
+            m = allowed & full[:, :N]
+        s_.masked_fill_(~m, float('-inf'))
+        out[:, h] = torch.softmax(s_, -1) @ vt[:, h // g]
+    return out.numpy()
+
+
 def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None, lists=None,
                                q_block: int = 128, kv_block: int = 64, q_front: int = 0, tile: int = 128,
-                               key_tile: int = 64, group: int = 1, partner_of=None):
+                               key_tile: int = 64, group: int = 1, partner_of=None, splits: int = 1,
+                               split_min_steps: int = 0, split_units=None):
     """Numerical model of the block-sparse FP8 forward (kai_fa_fp8.py:248-292, kai_fa_fp8_tma.py:256-272).
 
     Walks each (head, 128-row tile)'s block list from the last entry to the first in `key_tile`-key
@@ -419,7 +454,11 @@ def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None,
     P is rounded, so they follow the CUDA kernel.  `partner_of(h, t)` -> (h2, t2) or None models a
     kernel that walks two query tiles together: the steps are formed from the union of both tiles'
     64-key blocks (descending, `group` per step), and each tile takes the keys of its own blocks in
-    every step that holds any (the partner's blocks are masked out for it).
+    every step that holds any (the partner's blocks are masked out for it).  `splits` > 1 models the
+    split walks of sa_attn_fwd_fp8_split: a walk of a split unit (`split_units(h, t)` true, all units
+    when it is None) of at least split_min_steps steps is cut into
+    `splits` contiguous step ranges, each run from a fresh online-softmax state, and the ranges are
+    combined with weights 2^(m_s - max m) on their unnormalised outputs and row sums.
     Inputs are e4m3 bit patterns q8 [n, H, D],
     k8 [N, Hk, D], v8 [N, Hk, D]; per-head scale arrays or scalars.  Dense when counts is None.
     Returns fp32 [n, H, D].
@@ -463,26 +502,37 @@ def attention_fp8_kernel_model(q8, k8, v8, sq, sk, sv, q_pos0: int, counts=None,
                 mine = set(starts)
                 steps = [[k0 for k0 in union[gi:gi + group] if k0 in mine] for gi in range(0, len(union), group)]
                 steps = [st for st in steps if st]
-            m = np.full(tile, -np.inf)
-            l = np.zeros(tile)
-            o = np.zeros((tile, D))
-            for step in steps:
-                keys = np.concatenate([np.arange(k0, k0 + key_tile) for k0 in step])
-                kk = np.zeros((len(keys), D))
-                vk = np.zeros((len(keys), D))
-                inr = keys < N
-                kk[inr] = kv[keys[inr], hk]
-                vk[inr] = vv[keys[inr], hk]
-                sc = (qt @ kk.T) * c
-                sc = np.where(keys[None, :] <= qpos[:, None], sc, -np.inf)
-                mn = np.maximum(m, sc.max(1))
-                ms = np.where(np.isneginf(mn), 0.0, mn)
-                alpha = np.where(np.isneginf(m), 0.0, np.exp2(m - ms))
-                p = np.exp2(sc - ms[:, None])
-                l = l * alpha + p.sum(1)
-                p8 = e4m3_round(p * 448.0).astype(np.float64)
-                o = o * alpha[:, None] + p8 @ vk
-                m = mn
+            def run(range_steps):
+                m = np.full(tile, -np.inf)
+                l = np.zeros(tile)
+                o = np.zeros((tile, D))
+                for step in range_steps:
+                    keys = np.concatenate([np.arange(k0, k0 + key_tile) for k0 in step])
+                    kk = np.zeros((len(keys), D))
+                    vk = np.zeros((len(keys), D))
+                    inr = keys < N
+                    kk[inr] = kv[keys[inr], hk]
+                    vk[inr] = vv[keys[inr], hk]
+                    sc = (qt @ kk.T) * c
+                    sc = np.where(keys[None, :] <= qpos[:, None], sc, -np.inf)
+                    mn = np.maximum(m, sc.max(1))
+                    ms = np.where(np.isneginf(mn), 0.0, mn)
+                    alpha = np.where(np.isneginf(m), 0.0, np.exp2(m - ms))
+                    p = np.exp2(sc - ms[:, None])
+                    l = l * alpha + p.sum(1)
+                    p8 = e4m3_round(p * 448.0).astype(np.float64)
+                    o = o * alpha[:, None] + p8 @ vk
+                    m = mn
+                return m, l, o
+            if splits > 1 and len(steps) >= split_min_steps and (split_units is None or split_units(h, t)):
+                parts = [run(steps[len(steps) * s_ // splits:len(steps) * (s_ + 1) // splits]) for s_ in range(splits)]
+                with np.errstate(invalid='ignore'):
+                    M = np.max([pm for pm, _, _ in parts], axis=0)
+                    ws = [np.where(pl > 0, np.exp2(pm - np.where(np.isneginf(M), 0.0, M)), 0.0) for pm, pl, _ in parts]
+                l = sum(w * pl for w, (_, pl, _) in zip(ws, parts))
+                o = sum(w[:, None] * np.where(pl[:, None] > 0, po, 0.0) for w, (_, pl, po) in zip(ws, parts))
+            else:
+                _, l, o = run(steps)
             bad = (l == 0) | np.isnan(l)
             inv = np.where(bad, 0.0, sv[hk] / 448.0 / np.where(bad, 1.0, l))
             res = o * inv[:, None]

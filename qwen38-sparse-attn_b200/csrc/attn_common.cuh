@@ -3,6 +3,7 @@
 #pragma once
 #include <cudaTypedefs.h>
 
+#include <climits>
 #include <mutex>
 
 #include "sa_common.cuh"
@@ -23,6 +24,14 @@ struct Params {
     int qss, kss, vss;
     float softmax_scale;
     int32_t* status;
+    // Split walks (splits > 1, 1D grid): units u = h * n_tiles + i (tile n_tiles-1-i of head h, the
+    // launch order of the unsplit grid) below n_whole run whole, one CTA each; the n_tail units after
+    // them (the partial last wave) run as `splits` CTAs each.  A tail unit whose walk has at least
+    // split_min_steps steps is cut into `splits` contiguous step ranges, each writing its unnormalised
+    // fp32 O, running max and row sum to `part`, the last range to finish combining them; a shorter
+    // walk runs whole in its first CTA, which writes the output itself, and the others exit at once.
+    int splits, split_min_steps, n_whole, n_tail;
+    float* part;
     // Paged K/V (BF16 kernel; pages == nullptr: contiguous K/V): key j of the request is slot j % page
     // of cache page pages[j / page].  The tensor maps are then 4D {head_dim, Hk, page, num_pages}
     // with box_rows-row boxes (box_rows = min(page, 64)); kc / vc and the element strides serve the
@@ -67,12 +76,19 @@ struct Walker {
     int blk_lim;         // block ids at or above this are invalid (their key base would overflow)
     int half;            // 128-key blocks: which half of the current block comes next (1 = upper)
     int mode;            // 0 dense, 1 one list, 2 two lists
+    int remaining;       // steps left in this walk (a split takes a contiguous range of the steps)
     bool bad;
 
     __device__ __forceinline__ int load(const int32_t* p, int i) const { return i >= 0 ? __ldg(p + i) : -1; }
 
+    // LIMIT: stop after `remaining` steps (a split walk); whole walks skip the count
+    template <bool LIMIT = false>
     __device__ __forceinline__ bool next(int& kbase, uint32_t& rowmask) {
         rowmask = 3u;
+        if constexpr (LIMIT) {
+            if (remaining <= 0) return false;
+            --remaining;
+        }
         if (mode == 0) {
             if (dense_next < 0) return false;
             kbase = dense_next;
@@ -112,8 +128,32 @@ struct Walker {
     }
 };
 
-__device__ __forceinline__ Walker make_walker(const Params& p, int h, int m) {
+// Steps of the whole walk of (head h, tile m) in modes 0 and 1 (64-key tiles); -1 in mode 2.
+__device__ __forceinline__ int walk_steps(const Params& p, int h, int m) {
+    if (!p.counts) {
+        const int keys = min(p.q_offset + (m + 1) * 128, p.kv_len);
+        return keys > 0 ? (keys + 63) / 64 : 0;
+    }
+    if (p.q_block != 128) return -1;
+    const int64_t row = static_cast<int64_t>(h) * p.list_rows_per_head + m;
+    return max(__ldg(p.counts + row), 0) * (p.kv_block == 128 ? 2 : 1);
+}
+
+// Step range [begin, end) of split s for a walk of `steps` steps (the whole walk when the unit is
+// not split: splits == 1, mode 2, or fewer than split_min_steps steps; empty for s > 0 then).
+__device__ __forceinline__ void split_range(const Params& p, int steps, int s, int& begin, int& end) {
+    if (p.splits <= 1 || steps < p.split_min_steps) {
+        begin = 0;
+        end = s == 0 ? INT_MAX : 0;
+        return;
+    }
+    begin = static_cast<int>(static_cast<int64_t>(steps) * s / p.splits);
+    end = static_cast<int>(static_cast<int64_t>(steps) * (s + 1) / p.splits);
+}
+
+__device__ __forceinline__ Walker make_walker(const Params& p, int h, int m, int skip = 0, int take = INT_MAX) {
     Walker w;
+    w.remaining = take;
     w.bad = false;
     w.kvb = p.kv_block;
     w.blk_lim = KEY_NONE / p.kv_block;
@@ -127,11 +167,18 @@ __device__ __forceinline__ Walker make_walker(const Params& p, int h, int m) {
         const int last = p.q_offset + (m + 1) * 128;              // one past the tile's last position
         const int keys = min(last, p.kv_len);
         w.dense_next = keys > 0 ? ((keys + 63) / 64 - 1) * 64 : -1;
+        w.dense_next -= 64 * skip;
     } else if (p.q_block == 128) {
         w.mode = 1;
         const int64_t row = static_cast<int64_t>(h) * p.list_rows_per_head + m;
         w.a = p.lists + row * p.list_stride;
         w.ia = max(__ldg(p.counts + row), 0) - 1;
+        if (p.kv_block == 128) {              // two 64-key steps per entry, upper half first
+            w.ia -= skip / 2;
+            w.half = (skip & 1) ? 0 : 1;
+        } else {
+            w.ia -= skip;
+        }
         w.va = w.load(w.a, w.ia);
     } else {
         w.mode = 2;

@@ -158,7 +158,42 @@ __device__ __forceinline__ void load_paged_stage(const Params& p, uint8_t* dst, 
     __syncwarp();
 }
 
-template <bool FP8>
+// Row r of split tail unit tu (tile m, head h): combines the step ranges' partial outputs, one warp
+// per row, lane l holding head_dim columns 4l..4l+3.  With M the largest running max of the ranges
+// and w_s = 2^(m_s - M): out = (sum_s w_s O_s) * out_scale / (sum_s w_s l_s), 0 for a row with no
+// visible key (as the unsplit epilogue).  The partials of the other CTAs are read past L1.
+__device__ __forceinline__ void merge_split_row(const Params& p, int tu, int h, int m, int r, int lane,
+                                                float out_scale) {
+    const int qrow = m * 128 + r - p.q_front;
+    if (qrow < 0 || qrow >= p.n_q) return;
+    const float* ml_base = p.part + static_cast<int64_t>(p.n_tail) * p.splits * (128 * 128);
+    const int64_t u0 = static_cast<int64_t>(tu) * p.splits;
+    float M = -INFINITY;
+    for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(ml_base + ((u0 + sp) * 128 + r) * 2));
+    float L = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < p.splits; ++sp) {
+        const float ms = __ldcg(ml_base + ((u0 + sp) * 128 + r) * 2);
+        const float ls = __ldcg(ml_base + ((u0 + sp) * 128 + r) * 2 + 1);
+        if (!(ls > 0.f)) continue;
+        const float w = ex2_approx(ms - M);
+        L += w * ls;
+        const float4 o = __ldcg(reinterpret_cast<const float4*>(p.part + ((u0 + sp) * 128 + r) * 128) + lane);
+        acc.x += w * o.x;
+        acc.y += w * o.y;
+        acc.z += w * o.z;
+        acc.w += w * o.w;
+    }
+    const float inv = L > 0.f ? out_scale / L : 0.f;
+    uint16_t* orow = reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(qrow) * p.o_row_stride +
+                     static_cast<int64_t>(h) * p.o_head_stride;
+    *reinterpret_cast<uint2*>(orow + 4 * lane) =
+        make_uint2(pack_bf16x2(acc.x * inv, acc.y * inv), pack_bf16x2(acc.z * inv, acc.w * inv));
+}
+
+// SPLIT: the split-launch instantiation (1D grid of whole and tail units, step ranges, partial
+// outputs); the default instantiation keeps the 2D grid and whole walks with none of that code.
+template <bool FP8, bool SPLIT>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ,
                                                           const __grid_constant__ CUtensorMap tmK,
                                                           const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -186,10 +221,32 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     volatile int* tile_kb = const_cast<int*>(reinterpret_cast<volatile int*>(abort_flag + 1));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m = p.n_tiles - 1 - static_cast<int>(blockIdx.x);     // late (heavier) tiles first
-    const int h = blockIdx.y;
+    // unit (tile m, head h) and, for a tail unit of a split launch, this CTA's range of its walk
+    int m, h, split = 0, tail_unit = -1;
+    if constexpr (SPLIT) {
+        int u = static_cast<int>(blockIdx.x);
+        if (u >= p.n_whole) {
+            const int j = u - p.n_whole;
+            tail_unit = j / p.splits;
+            split = j - tail_unit * p.splits;
+            u = p.n_whole + tail_unit;
+        }
+        h = u / p.n_tiles;
+        m = p.n_tiles - 1 - (u - h * p.n_tiles);                     // late (heavier) tiles first
+    } else {
+        m = p.n_tiles - 1 - static_cast<int>(blockIdx.x);
+        h = blockIdx.y;
+    }
     const int g = p.H / p.Hk;
     const int hk = h / g;
+    int step0 = 0, step1 = INT_MAX;
+    bool partial = false;                                            // write O, max, sum to `part`
+    if constexpr (SPLIT) {
+        const int steps = tail_unit >= 0 ? walk_steps(p, h, m) : 0;
+        if (tail_unit >= 0) split_range(p, steps, split, step0, step1);
+        if (step1 <= step0) return;                                  // a split of an unsplit unit
+        partial = tail_unit >= 0 && steps >= p.split_min_steps;
+    }
 
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(bQ), 1);
@@ -217,10 +274,10 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         // ---------------------------------------------------------------- TMA producer (warp-uniform;
         // one elected lane issues)
         {
-            Walker w = make_walker(p, h, m);
+            Walker w = make_walker(p, h, m, step0, step1 - step0);
             int kb;
             uint32_t rm;
-            bool have = w.next(kb, rm);
+            bool have = w.template next<SPLIT>(kb, rm);
             int par[C::NST];
             bool used[C::NST];
             for (int i = 0; i < C::NST; ++i) { par[i] = 0; used[i] = false; }
@@ -235,7 +292,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
             __syncwarp();
             bool paged = false;
             if constexpr (!FP8) paged = p.pages != nullptr;
-            for (int t = 0;; ++t, have = w.next(kb, rm)) {
+            for (int t = 0;; ++t, have = w.template next<SPLIT>(kb, rm)) {
                 const int st = t % C::NST;
                 // paged K/V: the tile's boxes are worked out while the stage drains
                 PagedBox pbox{0, 0, -1, false};
@@ -389,15 +446,15 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         int t = 0;
         // The softmax threads walk the block lists themselves (the same walk as the producer's), one
         // tile ahead, instead of waiting on the stage barrier for the producer's tile descriptor.
-        Walker walk = make_walker(p, h, m);
+        Walker walk = make_walker(p, h, m, step0, step1 - step0);
         int kb_next;
         uint32_t rm_next;
-        bool have_next = walk.next(kb_next, rm_next);
+        bool have_next = walk.template next<SPLIT>(kb_next, rm_next);
         for (;; ++t) {
             if (!have_next) break;
             const int kb = kb_next;
             const uint32_t rm = rm_next;
-            have_next = walk.next(kb_next, rm_next);
+            have_next = walk.template next<SPLIT>(kb_next, rm_next);
             const int b = t & 1;
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bS + b), (t >> 1) & 1, abort_flag, p.status, SA_DEV_WAIT_S));
             if (!ok) break;
@@ -502,13 +559,34 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         const bool have_o = __all_sync(0xffffffffu, ok && T > 0 &&
                                        mbar_wait(smem_u32(bOF), 0, abort_flag, p.status, SA_DEV_WAIT_O));
         if (have_o) tc_fence_after();
+        if (SPLIT && partial) {
+            // unnormalised fp32 O row, running max (log2 units) and row sum of this step range
+            const int64_t u = static_cast<int64_t>(tail_unit) * p.splits + split;
+            float* ml = p.part + static_cast<int64_t>(p.n_tail) * p.splits * (128 * 128) + (u * 128 + r) * 2;
+            ml[0] = have_o ? m_run : -INFINITY;
+            ml[1] = have_o ? l_run : 0.f;
+            if (have_o) {
+                float4* orow4 = reinterpret_cast<float4*>(p.part + (u * 128 + r) * 128);
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t u32[32];
+                    tmem_ld32(tO + c * 32, u32);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        orow4[c * 8 + i] = make_float4(__uint_as_float(u32[4 * i]), __uint_as_float(u32[4 * i + 1]),
+                                                       __uint_as_float(u32[4 * i + 2]), __uint_as_float(u32[4 * i + 3]));
+                }
+            }
+            __threadfence();                              // partials visible before the arrival count
+        }
         const float inv = (have_o && l_run > 0.f) ? out_scale / l_run : 0.f;
         const int qrow = m * 128 + r - p.q_front;
-        const bool row_ok = qrow >= 0 && qrow < p.n_q;
+        const bool row_ok = !partial && qrow >= 0 && qrow < p.n_q;
         uint16_t* orow = reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(qrow) * p.o_row_stride +
                          static_cast<int64_t>(h) * p.o_head_stride;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < (partial ? 0 : 4); ++c) {
             uint32_t u[32];
             if (have_o) {
                 tmem_ld32(tO + c * 32, u);
@@ -533,6 +611,23 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     if (warp == 5) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+    if constexpr (SPLIT) {
+        // the last range of a split unit to finish combines the unit's rows (no second launch)
+        if (partial) {
+            __shared__ int merge_here;
+            if (threadIdx.x == 0) {
+                int* arrived = reinterpret_cast<int*>(p.part + static_cast<int64_t>(p.n_tail) * p.splits * (128 * 128 + 256));
+                merge_here = atomicAdd(arrived + tail_unit, 1) == p.splits - 1;
+            }
+            __syncthreads();
+            if (merge_here) {
+                __threadfence();
+                float out_scale = 1.f;
+                if constexpr (FP8) out_scale = __ldg(p.v_scale + hk * p.vss);
+                for (int r = warp; r < 128; r += C::THREADS / 32) merge_split_row(p, tail_unit, h, m, r, lane, out_scale);
+            }
+        }
     }
 }
 
@@ -560,12 +655,46 @@ struct PagedKV {
     int64_t page_stride;
 };
 
+// Split walks: `splits` step ranges per tail unit over a caller-provided fp32 workspace (`part`);
+// tail_units < 0: the partial last wave of this GPU.
+struct SplitOpts {
+    int splits, tail_units;
+    void* part;
+    int64_t part_bytes;
+};
+
+// Units run whole and tail units (split) of a split launch: the last tail_units units of the
+// launch order, or (tail_units < 0) the partial last wave of 2 resident CTAs per SM on the current
+// device (none for less than one wave).
+void split_plan(int n_tiles, int H, int splits, int tail_units, int* n_whole, int* n_tail) {
+    const int units = n_tiles * H;
+    *n_whole = units;
+    *n_tail = 0;
+    if (splits <= 1) return;
+    if (tail_units >= 0) {
+        *n_tail = std::min(tail_units, units);
+    } else {
+        const int slots = 2 * num_sms();
+        if (units >= slots) *n_tail = units - (units / slots) * slots;
+    }
+    *n_whole = units - *n_tail;
+}
+
+int64_t split_workspace_bytes(int n_tiles, int H, int splits, int tail_units) {
+    int n_whole, n_tail;
+    split_plan(n_tiles, H, splits, tail_units, &n_whole, &n_tail);
+    // per tail unit and range: O rows and (max, sum) pairs; then one arrival counter per tail unit
+    const int64_t floats = static_cast<int64_t>(n_tail) * splits * (128 * 128 + 256);
+    return floats * static_cast<int64_t>(sizeof(float)) + ((static_cast<int64_t>(n_tail) * 4 + 15) & ~15ll);
+}
+
 template <bool FP8>
 int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t krs, int64_t khs, const void* v,
                 int64_t vrs, int64_t vhs, void* out, int64_t ors, int64_t ohs, int n_q, int H, int Hk, int D, int kv_len,
                 int q_front, int q_offset, const int32_t* counts, const int32_t* lists, int64_t list_stride, int q_block,
                 int kv_block, const float* qsc, int qss, const float* ksc, int kss, const float* vsc, int vss,
-                float softmax_scale, int32_t* status, cudaStream_t stream, const PagedKV* paged = nullptr) {
+                float softmax_scale, int32_t* status, cudaStream_t stream, const PagedKV* paged = nullptr,
+                const SplitOpts* split = nullptr) {
     using C = Cfg<FP8>;
     const char* name = paged ? "sa_attn_fwd_bf16_paged" : FP8 ? "sa_attn_fwd_fp8" : "sa_attn_fwd_bf16";
     if (D != 128) return fail(SA_ERR_UNSUPPORTED, "%s: head_dim %d (only 128)", name, D);
@@ -652,6 +781,23 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     p.vss = vss;
     p.softmax_scale = softmax_scale;
     p.status = status;
+    p.splits = 1;
+    if (split && split->splits > 1) {
+        if (split->splits > 16) return fail(SA_ERR_ARG, "%s: splits %d (at most 16)", name, split->splits);
+        const int64_t need = split_workspace_bytes(n_tiles, H, split->splits, split->tail_units);
+        if (need > 0 && (!split->part || (reinterpret_cast<uintptr_t>(split->part) & 15) || split->part_bytes < need))
+            return fail(SA_ERR_ARG, "%s: split workspace needs %lld bytes (16-byte aligned)", name,
+                        static_cast<long long>(need));
+        int n_whole, n_tail;
+        split_plan(n_tiles, H, split->splits, split->tail_units, &n_whole, &n_tail);
+        if (n_tail > 0 && !(FP8 && use_pair_kernel())) {   // the paired-tile kernel runs its units whole
+            p.splits = split->splits;
+            p.split_min_steps = 32 * split->splits;
+            p.n_whole = n_whole;
+            p.n_tail = n_tail;
+            p.part = static_cast<float*>(split->part);
+        }
+    }
     if constexpr (FP8) {
         if (use_pair_kernel()) return launch_attn_pair<true>(tmQ, tmK, tmV, p, stream, name);
     }
@@ -662,14 +808,24 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     {
         std::lock_guard<std::mutex> lock(attr.mu);
         if (attr.ctx[dev] != ctx) {
-            cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 C::SMEM_BYTES);
+            cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<FP8, false>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute(attn_fwd_kernel<FP8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::SMEM_BYTES);
             if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
             attr.ctx[dev] = ctx;
         }
     }
-    dim3 grid(n_tiles, H);
-    attn_fwd_kernel<FP8><<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, p);
+    if (p.splits > 1) {
+        cudaError_t e = cudaMemsetAsync(p.part + static_cast<int64_t>(p.n_tail) * p.splits * (128 * 128 + 256), 0,
+                                        sizeof(int) * static_cast<size_t>(p.n_tail), stream);
+        if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+        attn_fwd_kernel<FP8, true><<<p.n_whole + p.n_tail * p.splits, C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK,
+                                                                                                        tmV, p);
+    } else {
+        attn_fwd_kernel<FP8, false><<<dim3(n_tiles, H), C::THREADS, C::SMEM_BYTES, stream>>>(tmQ, tmK, tmV, p);
+    }
     return check_launch(name);
 }
 
@@ -689,6 +845,52 @@ extern "C" int sa_attn_fwd_fp8(const uint8_t* q, int64_t q_row_stride, int64_t q
                                  kv_len, q_front, q_offset, counts, lists, list_stride, q_block, kv_block, q_scale,
                                  q_scale_stride, k_scale, k_scale_stride, v_scale, v_scale_stride, softmax_scale, status,
                                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sa_attn_split_count(int n_q, int q_front, int num_heads) {
+    if (n_q <= 0 || num_heads <= 0 || q_front < 0) return 1;
+    // (tile, head) units of nearly equal cost T over 2 resident CTAs per SM: the full waves run
+    // whole; the partial last wave's units run as k pieces of T / k, taking ceil(tail * k / slots)
+    // rounds.  The k with the shortest total, if it saves at least 5%; 1 for less than one wave.
+    const int64_t units = static_cast<int64_t>((q_front + n_q + 127) / 128) * num_heads;
+    const int64_t slots = 2ll * sa::num_sms();
+    if (units < slots) return 1;
+    const int64_t waves = units / slots, tail = units - waves * slots;
+    if (tail == 0) return 1;
+    int best = 1;
+    double best_t = static_cast<double>(waves + 1);
+    const double base = best_t;
+    for (int k = 2; k <= 8; ++k) {
+        const double t = static_cast<double>(waves) + static_cast<double>((tail * k + slots - 1) / slots) / k;
+        if (t < best_t - 1e-9) {
+            best = k;
+            best_t = t;
+        }
+    }
+    return best_t <= base * 0.95 ? best : 1;
+}
+
+extern "C" int64_t sa_attn_split_workspace_bytes(int n_q, int q_front, int num_heads, int splits, int tail_units) {
+    if (n_q <= 0 || num_heads <= 0 || splits <= 1) return 0;
+    return sa::split_workspace_bytes((q_front + n_q + 127) / 128, num_heads, splits, tail_units);
+}
+
+extern "C" int sa_attn_fwd_fp8_split(const uint8_t* q, int64_t q_row_stride, int64_t q_head_stride, const uint8_t* k,
+                                     int64_t k_row_stride, int64_t k_head_stride, const uint8_t* v,
+                                     int64_t v_row_stride, int64_t v_head_stride, void* out, int64_t o_row_stride,
+                                     int64_t o_head_stride, int n_q, int num_heads, int num_kv_heads, int head_dim,
+                                     int kv_len, int q_front, int q_offset, const int32_t* counts,
+                                     const int32_t* lists, int64_t list_stride, int q_block, int kv_block,
+                                     const float* q_scale, int q_scale_stride, const float* k_scale,
+                                     int k_scale_stride, const float* v_scale, int v_scale_stride,
+                                     float softmax_scale, int32_t* status, int splits, int tail_units,
+                                     void* workspace, int64_t workspace_bytes, void* stream) {
+    const sa::SplitOpts so{splits, tail_units, workspace, workspace_bytes};
+    return sa::launch_attn<true>(q, q_row_stride, q_head_stride, k, k_row_stride, k_head_stride, v, v_row_stride,
+                                 v_head_stride, out, o_row_stride, o_head_stride, n_q, num_heads, num_kv_heads, head_dim,
+                                 kv_len, q_front, q_offset, counts, lists, list_stride, q_block, kv_block, q_scale,
+                                 q_scale_stride, k_scale, k_scale_stride, v_scale, v_scale_stride, softmax_scale, status,
+                                 static_cast<cudaStream_t>(stream), nullptr, &so);
 }
 
 extern "C" int sa_attn_fwd_bf16_paged(const void* q, int64_t q_row_stride, int64_t q_head_stride, const void* k_cache,

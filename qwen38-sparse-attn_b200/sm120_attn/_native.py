@@ -50,13 +50,18 @@ SIGNATURES = {
     'sa_absmax_paged_bf16': [_p, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p],
     'sa_quantize_paged_e4m3': [_p, _i64, _i64, _i64, _p, _i32, _i32, _i32, _i32, _i32, _p, _i32, _i32, _p, _i64, _i64,
                                _p],
+    'sa_attn_split_count': [_i32, _i32, _i32],
+    'sa_attn_split_workspace_bytes': [_i32, _i32, _i32, _i32, _i32],
+    'sa_attn_fwd_fp8_split': [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32,
+                              _i32, _i32, _i32, _p, _p, _i64, _i32, _i32, _p, _i32, _p, _i32, _p, _i32, _f32, _p,
+                              _i32, _i32, _p, _i64, _p],
     'sa_attn_fwd_bf16_paged': [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _p, _i32, _i32, _p, _i64, _i64, _i32, _i32,
                                _i32, _i32, _i32, _i32, _i32, _p, _p, _i64, _i32, _i32, _f32, _p, _p],
 }
 
 
 # entry points that return a size instead of a status code
-SIZE_QUERIES = {'sa_select_workspace_bytes': _sz}
+SIZE_QUERIES = {'sa_select_workspace_bytes': _sz, 'sa_attn_split_workspace_bytes': _i64}
 
 
 class NativeLibraryError(RuntimeError):

@@ -203,15 +203,45 @@ def absmax(x, per_head: bool, out=None):
     return out
 
 
+_SPLITS: dict = {}
+
+
+def attn_splits(n: int, q_front: int, num_heads: int, device) -> int:
+    """Split count for an FP8 attention launch: SA_ATTN_SPLITS (an integer; 0 or 1 = never split) or,
+    unset / `auto`, sa_attn_split_count's choice for the current GPU (cached per shape and device)."""
+    env = os.environ.get('SA_ATTN_SPLITS', 'auto').strip().lower()
+    if env not in ('', 'auto'):
+        return max(1, int(env))
+    key = (n, q_front, num_heads, torch.device(device).index)
+    if key not in _SPLITS:
+        _SPLITS[key] = int(N.lib().sa_attn_split_count(n, q_front, num_heads))
+    return _SPLITS[key]
+
+
 def attn_fp8(q8, k8, v8, out, kv_len: int, q_front: int, q_offset: int, counts, lists, kv_block: int,
-             q_scale, k_scale, v_scale, softmax_scale: float, q_block: int = 128):
+             q_scale, k_scale, v_scale, softmax_scale: float, q_block: int = 128, splits=None,
+             tail_units: int = -1):
     """Block-sparse (counts/lists) or dense causal FP8 attention; see sa_attn_fwd_fp8.
 
-    q8 [n, H, D], k8 / v8 [kv, Hk, D] e4m3 bytes (last dim contiguous), out [n, H, D] bf16."""
+    q8 [n, H, D], k8 / v8 [kv, Hk, D] e4m3 bytes (last dim contiguous), out [n, H, D] bf16.
+    splits: step ranges per walk of the split units (sa_attn_fwd_fp8_split, with a workspace from
+    torch's caching allocator); None = attn_splits' choice.  tail_units: how many units (the last of
+    the launch order) are split; -1 = the partial last wave of this GPU."""
     _need_cuda('attn_fp8', q8, k8, v8, out, counts, lists, q_scale, k_scale, v_scale)
     n, H, D = q8.shape
     Hk = k8.shape[1]
     st = status_word(q8.device)
+    k = attn_splits(n, q_front, H, q8.device) if splits is None else max(1, int(splits))
+    if k > 1 and q_block == 128:
+        nbytes = int(N.lib().sa_attn_split_workspace_bytes(n, q_front, H, k, int(tail_units)))
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q8.device)
+        N.call('sa_attn_fwd_fp8_split', _p(q8), q8.stride(0), q8.stride(1), _p(k8), k8.stride(0), k8.stride(1),
+               _p(v8), v8.stride(0), v8.stride(1), _p(out), out.stride(0), out.stride(1), n, H, Hk, D, kv_len,
+               q_front, q_offset, _p(counts), _p(lists), lists.stride(0) if lists is not None else 0, q_block,
+               kv_block, _p(q_scale), 0 if q_scale.numel() == 1 else 1, _p(k_scale), 0 if k_scale.numel() == 1 else 1,
+               _p(v_scale), 0 if v_scale.numel() == 1 else 1, float(softmax_scale), _p(st), k, int(tail_units),
+               _p(ws), nbytes, _stream(q8.device))
+        return
     N.call('sa_attn_fwd_fp8', _p(q8), q8.stride(0), q8.stride(1), _p(k8), k8.stride(0), k8.stride(1), _p(v8),
            v8.stride(0), v8.stride(1), _p(out), out.stride(0), out.stride(1), n, H, Hk, D, kv_len, q_front,
            q_offset, _p(counts), _p(lists), lists.stride(0) if lists is not None else 0, q_block, kv_block,

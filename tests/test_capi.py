@@ -14,7 +14,7 @@ ROOT = Path(__file__).resolve().parent.parent
 def declared_symbols():
     names = set()
     for h in (ROOT / 'include').glob('*.h'):
-        names |= set(re.findall(r'^SA_API\s+(?:const\s+char\s*\*|int|size_t)\s+(sa_\w+)\s*\(', h.read_text(), flags=re.M))
+        names |= set(re.findall(r'^SA_API\s+(?:const\s+char\s*\*|int|int64_t|size_t)\s+(sa_\w+)\s*\(', h.read_text(), flags=re.M))
     return names
 
 

@@ -114,6 +114,28 @@ def test_attention_reference(golden):
     np.testing.assert_allclose(out, golden['attn_sparse/out'], rtol=1e-4, atol=2e-5)
 
 
+def test_threaded_attention_matches_golden(golden):
+    """attention_ref_threaded (the CPU baseline's attention, PyTorch on all host threads) gives the
+    reference's outputs like attention_ref, dense and block-masked, including a chunk starting inside
+    a query block (q_front) and a mask narrower than the keys."""
+    for name, n, kv in (('attn_dense_a', 100, 300), ('attn_dense_b', 128, 128)):
+        q, k, v, _ = synth.make_qkv(n, kv, 4, 2, D, seed=41 + n)
+        out = O.attention_ref_threaded(f32(q), f32(k), f32(v), kv - n)
+        np.testing.assert_allclose(out, golden[f'{name}/out'], rtol=1e-4, atol=2e-5)
+    n, kv = 256, 1024
+    q, k, v, _ = synth.make_qkv(n, kv, 4, 2, D, seed=51)
+    masks = unpack_mask(golden, 'attn_sparse/masks')
+    out = O.attention_ref_threaded(f32(q), f32(k), f32(v), kv - n, masks, q_block=64, kv_block=64)
+    np.testing.assert_allclose(out, golden['attn_sparse/out'], rtol=1e-4, atol=2e-5)
+    rng = np.random.default_rng(3)
+    q, k, v, _ = synth.make_qkv(300, 1500, 4, 2, D, seed=9)
+    m = rng.random((4, 4, 23)) < 0.5                     # 23 blocks of 64 < 1500 keys: the rest masked
+    m[:, :, 0] = True
+    a = O.attention_ref(f32(q), f32(k), f32(v), 1200, m, q_block=128, kv_block=64, q_front=77)
+    b = O.attention_ref_threaded(f32(q), f32(k), f32(v), 1200, m, q_block=128, kv_block=64, q_front=77)
+    np.testing.assert_allclose(b, a, rtol=1e-5, atol=1e-6)
+
+
 def test_fp8_reference_operands(golden):
     n, kv = 128, 512
     q, k, v, _ = synth.make_qkv(n, kv, 4, 2, D, seed=61)
