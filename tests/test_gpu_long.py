@@ -53,6 +53,11 @@ def _slice_lists(counts, lists, heads, tiles_total):
     return c[rows].astype(np.int32), li[rows].astype(np.int32)
 
 
+def _launch(heads):
+    """The whole attention launch behind the checked slice (for the split walks of its last wave)."""
+    return (H, N, 0, lambda h: heads[h], lambda t: N // 128 - TILES + t)
+
+
 def _masks_from_lists(cs, ls, nheads, nb):
     m = np.zeros((nheads * TILES, nb), dtype=bool)
     for r in range(nheads * TILES):
@@ -93,7 +98,7 @@ def test_fp8_sparse_65536_keys(inputs):
     assert np.isfinite(got).all()
     ref = O.attention_ref(*deq, KV - TILES * 128, masks, q_block=128, kv_block=BLK)
     model = O.attention_fp8_kernel_model(q8, k8, v8, *scales, KV - TILES * 128, cs, ls, q_block=128, kv_block=BLK,
-                                         **fp8_model_kwargs(len(heads), 1, TILES))
+                                         **fp8_model_kwargs(len(heads), 1, TILES, launch=_launch(heads)))
     print(f'fp8 65536 keys: kept {cs.sum() / (len(heads) * TILES * nb):.3f}, rel-L2 vs fp32 {rel_l2(got, ref):.3e}, '
           f'vs P-rounding model {rel_l2(got, model):.3e}')
     assert rel_l2(got, model) < 1e-2
@@ -125,7 +130,7 @@ def test_fp8_dense_65536_keys_per_head_scales(inputs):
     got = f32(out)[-TILES * 128:, heads]
     ref = O.attention_ref(*deq, KV - TILES * 128)
     model = O.attention_fp8_kernel_model(q8s, k8s, v8s, sqs, sks, svs, KV - TILES * 128, q_block=128, kv_block=64,
-                                         **fp8_model_kwargs(len(heads), 1, TILES))
+                                         **fp8_model_kwargs(len(heads), 1, TILES, launch=_launch(heads)))
     print(f'fp8 dense 65536 keys: rel-L2 vs fp32 {rel_l2(got, ref):.3e}, vs P-rounding model {rel_l2(got, model):.3e}')
     assert rel_l2(got, model) < 1e-2
     assert rel_l2(got, ref) < 3e-2
