@@ -1091,6 +1091,8 @@ def cpu_sample(strength, seconds_budget=20.0):
 
 
 def cpu_baseline(strength):
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)                 # all host threads (rank 0 at N = 1)
     val, desc, threads = cpu_sample(strength)
     return {'value': round(val, 6), 'unit': 'TFLOPS', 'cores': os.cpu_count(), 'threads': threads, 'kind': 'port',
             'sample': desc}
@@ -1132,6 +1134,9 @@ def run_reference(args):
         print(json.dumps({'impl': 'reference', 'unavailable': f'no CPU arm for the {args.workload} workload: the '
                           'reference CPU path is timed for the default (chunk) and selection workloads'}), flush=True)
         return
+    import torch
+    # torchrun sets OMP_NUM_THREADS=1 for every rank; rank 0 alone runs this arm and uses all host threads
+    torch.set_num_threads(os.cpu_count() or 1)
     sample = cpu_sample if args.workload == 'chunk' else (lambda st, seconds_budget=0: cpu_selection_sample(st))
     unit = 'TFLOPS' if args.workload == 'chunk' else 'GB/s'
     # every one of the K timed steps is a bounded sample of the workload, sized so that the whole
@@ -1153,8 +1158,10 @@ def run_reference(args):
         'config': base,
         'cpu_baseline': {'value': round(value, 6), 'unit': unit, 'cores': os.cpu_count(), 'threads': threads,
                          'kind': 'port', 'sample': desc,
-                         'arm': 'host cores of rank 0 (the other ranks exit); the reference algorithm restated in '
-                                'numpy (oracle/), the reference checkout itself does not travel to the GPU host'},
+                         'arm': 'host cores of rank 0, all threads (the other ranks exit); the reference algorithm '
+                                'restated in oracle/ (selection in numpy, attention with the fp32 arithmetic of the '
+                                'reference\'s reference() on all intra-op threads); the reference checkout itself '
+                                'does not travel to the GPU host'},
         'e2e': {'value': round(value, 6), 'unit': unit, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
