@@ -123,6 +123,16 @@ class Clocks:
                 'samples': len(sm)}
 
 
+def rank_shape_kv_heads(n):
+    """KV heads of rank 0 of an n-GPU strong split of the benchmark's 8 KV heads."""
+    from sm120_attn.shard import kv_head_range
+    try:
+        lo, hi = kv_head_range(0, n, HK_FULL)
+    except ValueError as e:
+        raise SystemExit(f'--rank-shape: {e}')
+    return hi - lo
+
+
 def make_rank_inputs(hk, seed, strength, device):
     import synth
     q, k, v, _ = synth.make_qkv(N_Q, KV, hk * (H_FULL // HK_FULL), hk, D, block=BLOCK, q_start=Q_START, seed=seed,
@@ -240,6 +250,8 @@ def run_b200(args):
         hk = hi - lo
     else:
         hk = HK_FULL                                         # every rank runs a full problem
+    if args.rank_shape > 1 and world == 1:                   # one rank's share of an N-GPU strong split
+        hk = rank_shape_kv_heads(args.rank_shape)
     h = hk * (H_FULL // HK_FULL)
     q, k, v = make_rank_inputs(hk, 1000 + rank, args.strength, dev)
     sp = ksp.SparsePrefill(h, hk, D, dev, tau=TAU, min_kv=0, min_q=0, kernel='sm120fp8')
@@ -799,10 +811,58 @@ def _hook(args, h, hk, dev, rank):
                        'value_definition': 'executed-tile FLOPs / prefill time (host metadata reads included)'}}
 
 
+def _paged(args, h, hk, dev, rank):
+    """BF16 attention over a paged K/V cache read in place (sa_attn_fwd_bf16_paged): the configs[1]
+    chunk dense causal (q 8192 @ 57344 vs 65536 keys), pages of --page rows in shuffled order.  Beside
+    it (config): the contiguous kernel on the same keys and the gather of the history out of the
+    pages that the reference's hook does every chunk."""
+    import torch
+    from sm120_attn import ops
+    q, k, v = make_rank_inputs(hk, 5000 + rank, args.strength, dev)
+    page = args.page
+    npages = KV // page
+    perm = torch.randperm(npages + 64, generator=torch.Generator().manual_seed(7))[:npages].to(dev)
+    kc = torch.zeros(npages + 64, page, hk, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    kc[perm.long()] = k.view(npages, page, hk, D)
+    vc[perm.long()] = v.view(npages, page, hk, D)
+    table = perm.to(torch.int32)
+    out = torch.empty(N_Q, h, D, dtype=torch.bfloat16, device=dev)
+
+    def paged():
+        ops.attn_bf16_paged(q, kc, vc, table, out, KV, 0, Q_START, None, None, 64, D ** -0.5)
+
+    def contiguous():
+        ops.attn_bf16(q, k, v, out, KV, 0, Q_START, None, None, 64, D ** -0.5)
+
+    def gather():
+        return kc[perm.long()].reshape(-1, hk, D), vc[perm.long()].reshape(-1, hk, D)
+    for fn in (paged, contiguous, gather):
+        for _ in range(args.warmup):
+            fn()
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    ms = _timed(paged, args.steps, dev, world)
+    ms_c = _timed(contiguous, args.steps, dev, world)
+    ms_g = _timed(gather, args.steps, dev, world)
+    ops.check_status(dev)
+    flops = causal_flops(h, D, N_Q, KV)
+    return {'ms': ms, 'e2e_ms': None, 'work': flops, 'unit': 'TFLOPS', 'scale': 1e12,
+            'kernel': 'attn_fwd_kernel<bf16> (paged)', 'kernel_ms': ms / args.steps, 'kernel_work': flops,
+            'bound': 'tensor', 'h2d': 0, 'd2h': 0, 'launches': 1, 'dtype': 'bf16 (fp32 accumulate)',
+            'peak_scale': 0.5,
+            'config': {'workload': f'dense causal BF16 attention through a paged K/V cache (page {page}, shuffled '
+                                   f'pages): q {N_Q} @ {Q_START} vs {KV} keys, H {h}/Hk {hk}/D {D}',
+                       'contiguous_ms_per_step': round(ms_c / args.steps, 4),
+                       'paged_over_contiguous': round(ms / ms_c, 4),
+                       'gather_ms_per_step': round(ms_g / args.steps, 4),
+                       'value_definition': 'causal FLOPs / time of the paged kernel'}}
+
+
 def _decoder_kernels(args, h, hk, dev, rank):
     """The config-5 harness kernels at one 8192-token chunk of the full decoder (1 GPU widths):
-    fused residual add + RMSNorm over [8192, 5120], RoPE + K/V cache write of qkv [8192, 80 x 128],
-    SwiGLU of gate_up [8192, 2 x 25600].  Inputs are larger than L2 except rope's table rows."""
+    fused residual add + RMSNorm over [8192, 5120], RoPE + K/V cache write of qkv [8192, 80 x 128]
+    with the key block means, SwiGLU of gate_up [8192, 2 x 25600].  Inputs are larger than L2 except
+    rope's table rows."""
     import torch
     from sm120_attn import ops
     from sm120_attn.decoder import DecoderConfig, rope_table
@@ -823,10 +883,13 @@ def _decoder_kernels(args, h, hk, dev, rank):
     table = rope_table(3 * n, D, cfg.rope_theta, dev)
     gu = torch.randn(n, 2 * I, generator=g, device=dev).to(bf)
     act = torch.empty(n, I, dtype=bf, device=dev)
+    km = torch.empty(Hkv, 3 * n // 128, D, dtype=torch.float32, device=dev)
+    # the decoder's RoPE launch also writes the chunk's key block means (sa_rope_qkv_means_bf16)
     kernels = [
         ('add_rmsnorm_kernel', lambda: ops.add_rmsnorm(hbuf, w, x, cfg.eps, delta=delta), 8 * n * E),
-        ('rope_qkv_kernel', lambda: ops.rope_qkv(qkv, Hq, Hkv, D, table, 2 * n, q, kc[2 * n:], vc[2 * n:]),
-         4 * n * (Hq + 2 * Hkv) * D),
+        ('rope_qkv_kernel', lambda: ops.rope_qkv(qkv, Hq, Hkv, D, table, 2 * n, q, kc[2 * n:], vc[2 * n:], km=km,
+                                                 block=128),
+         4 * n * (Hq + 2 * Hkv) * D + 4 * Hkv * (n // 128) * D),
         ('silu_mul_kernel', lambda: ops.silu_mul(gu, act), 6 * n * I),
     ]
     per = {}
@@ -834,6 +897,12 @@ def _decoder_kernels(args, h, hk, dev, rank):
         for _ in range(3):
             fn()
         per[name] = (_kernel_ms(fn, dev, reps=20), nbytes)
+    # the same RoPE write without the means, and the separate block-means pass over the written keys
+    unfused = [lambda: ops.rope_qkv(qkv, Hq, Hkv, D, table, 2 * n, q, kc[2 * n:], vc[2 * n:]),
+               lambda: ops.block_means(kc[2 * n:], 2 * n, 128, km, 0)]
+    for fn in unfused:
+        fn()
+    unfused_ms = [_kernel_ms(fn, dev, reps=20) for fn in unfused]
     steps = max(1, args.steps)
     ms = _timed(lambda: [fn() for _, fn, _ in kernels], steps, dev, int(os.environ.get('WORLD_SIZE', '1')))
     total = sum(b for _, (_, b) in per.items())
@@ -845,6 +914,9 @@ def _decoder_kernels(args, h, hk, dev, rank):
                                    f'rope_qkv [{n}, {Hq}+2x{Hkv} heads x {D}], silu_mul [{n}, 2x{I}]',
                        'per_kernel': {k: {'us': round(t * 1000, 1), 'MB': round(b / 1e6, 1),
                                           'GB/s': round(b / (t * 1e-3) / 1e9, 1)} for k, (t, b) in per.items()},
+                       'rope_with_key_means': 'rope_qkv_kernel writes the chunk\'s key block means in the same pass; '
+                                              f'unfused: rope {unfused_ms[0] * 1000:.1f} us + block means '
+                                              f'{unfused_ms[1] * 1000:.1f} us',
                        'value_definition': 'algorithmic bytes of the three kernels / their time'}}
 
 
@@ -1003,10 +1075,12 @@ def run_other(args):
         hk = hi - lo
     else:
         hk = HK_FULL
+    if args.rank_shape > 1 and world == 1:
+        hk = rank_shape_kv_heads(args.rank_shape)
     h = hk * (H_FULL // HK_FULL)
     clocks = Clocks(local)
     clocks.start()
-    res = {'dense': _dense, 'selection': _selection, 'chunked': _chunked, 'hook': _hook,
+    res = {'dense': _dense, 'selection': _selection, 'chunked': _chunked, 'hook': _hook, 'paged': _paged,
            'decoder_kernels': _decoder_kernels}[args.workload](
         args, h, hk, dev, rank)
     clk = clocks.stop()
@@ -1028,11 +1102,13 @@ def run_other(args):
     line['config']['l2'] = 'inputs larger than L2; no flush'
     if res['kernel_work'] is not None and kms > 0:
         ach = res['kernel_work'] / (kms * 1e-3) / res['scale']
-        peak = 2.0 * bf16 if res['bound'] == 'tensor' else hbm
+        peak = 2.0 * bf16 * res.get('peak_scale', 1.0) if res['bound'] == 'tensor' else hbm
         line['roofline'] = {'bound': res['bound'], 'kernel': res['kernel'], 'achieved': round(ach, 1),
                             'peak': round(peak, 1), 'unit': 'TFLOP/s' if res['bound'] == 'tensor' else 'GB/s',
                             'frac': round(ach / peak, 4), 'traffic': None,
-                            'peak_source': f'{how} (MEASURED_PEAKS.json)' + (' x2 for e4m3' if res['bound'] == 'tensor' else '')}
+                            'peak_source': f'{how} (MEASURED_PEAKS.json)' + (
+                                ' x2 for e4m3' if res['bound'] == 'tensor' and res.get('peak_scale', 1.0) == 1.0
+                                else ' bf16' if res['bound'] == 'tensor' else '')}
     if res['e2e_ms'] is not None:
         line['e2e'] = {'value': round(work * steps / (e2e_ms * 1e-3) / res['scale'], 2), 'unit': res['unit'],
                        'h2d_bytes_per_step': res['h2d'], 'd2h_bytes_per_step': res['d2h'],
@@ -1169,8 +1245,10 @@ def run_reference(args):
 
 def chunk_config(args, world):
     """`config` of the default (chunk) workload, shared by both arms."""
+    shape = (f'; one GPU running the per-rank share of a {args.rank_shape}-GPU strong split'
+             if args.rank_shape > 1 and world == 1 else '')
     return {'workload': f'sparse FP8 prefill chunk (configs[1] shape): q {N_Q} @ {Q_START} vs {KV} keys, '
-                        f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection',
+                        f'H {H_FULL}/Hk {HK_FULL}/D {D}, block {BLOCK}, tau {TAU}, {args.strength} injection' + shape,
             'global_batch': 1, 'seq_len': KV, 'chunk': N_Q,
             'parallelism': f'kv-head shards x{world} ({args.scaling}), no collective on the data path'}
 
@@ -1194,7 +1272,12 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--profile-range', action='store_true',
                     help='bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)')
-    ap.add_argument('--workload', default='chunk', choices=['chunk', 'dense', 'selection', 'chunked', 'hook', 'ttft', 'decoder_kernels'])
+    ap.add_argument('--workload', default='chunk',
+                    choices=['chunk', 'dense', 'selection', 'chunked', 'hook', 'paged', 'ttft', 'decoder_kernels'])
+    ap.add_argument('--page', type=int, default=16, help='paged workload: rows per page of the K/V cache')
+    ap.add_argument('--rank-shape', type=int, default=1,
+                    help='one GPU runs the per-rank share of an N-GPU strong split (8/N KV heads and their '
+                         'query heads), e.g. to measure the last-wave split walks of 8-GPU ranks')
     ap.add_argument('--comm-blocks', type=int, default=2,
                     help='ttft workload: row blocks whose all-reduces overlap the next block\'s GEMMs (1: none)')
     ap.add_argument('--contexts', default='65536,131072,262144',

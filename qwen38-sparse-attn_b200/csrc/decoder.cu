@@ -120,18 +120,16 @@ struct RopeArgs {
     int km_block0;
 };
 
-// One launch: rotary embedding of the q and k heads of qkv rows (positions pos0 + row), q to q_out
-// [rows, Hq, D], rotated k and copied v to the cache rows.  With kctas > 0 the k heads are done by
-// CTAs [0, kctas) that also write the key block means: CTA (b, head group) owns the rows of block b
-// within [pos0, pos0 + rows); thread (head, pair group j, row group g) rotates rows lo+g, lo+g+rg, ...
-// and sums the bf16 results in that order; the rg partial sums are then added in group order and
-// divided by the row count.  That is block_means_kernel's order for the same launch shape, so the
-// means equal sa_block_means_bf16's over the written k rows bit for bit.  The remaining CTAs rotate
-// the q heads (and the k heads when kctas == 0) and copy the v heads, grid-strided, one thread per
-// 8 pairs of one head of one row.
-__global__ void __launch_bounds__(256) rope_qkv_kernel(const RopeArgs a) {
+// Rotary embedding of the k heads with their key block means (kctas > 0): CTA (b, head group) owns
+// the rows of block b within [pos0, pos0 + rows); thread (head, pair group j, row group g) rotates
+// rows lo+g, lo+g+rg, ... into the cache rows and sums the bf16 results in that order; the rg
+// partial sums are then added in group order and divided by the row count.  That is
+// block_means_kernel's order for the same launch shape, so the means equal sa_block_means_bf16's
+// over the written k rows bit for bit.  A kernel of its own: its per-thread row batches need far more
+// registers than the elementwise rotation, whose occupancy they would otherwise cap.
+__global__ void __launch_bounds__(256) rope_k_means_kernel(const RopeArgs a) {
     const int D = a.D, half = D / 2, jn = D / 16;
-    if (static_cast<int>(blockIdx.x) < a.kctas) {
+    {
         extern __shared__ float partial[];                       // [rg - 1][threads in use][16]
         const int txp = a.hpc * jn;
         const int tid = threadIdx.x, tx = tid % txp, ty = tid / txp;
@@ -199,13 +197,19 @@ __global__ void __launch_bounds__(256) rope_qkv_kernel(const RopeArgs a) {
             o[8 * j + i] = __fdiv_rn(acc[i], cnt);
             o[half + 8 * j + i] = __fdiv_rn(acc[8 + i], cnt);
         }
-        return;
     }
+}
+
+// Rotary embedding of the q heads of qkv rows (positions pos0 + row) into q_out [rows, Hq, D], of the
+// k heads into the cache rows unless rope_k_means_kernel does them (kctas > 0), and the v heads
+// copied to theirs: grid-strided, one thread per 8 pairs of one head of one row.
+__global__ void __launch_bounds__(256) rope_qkv_kernel(const RopeArgs a) {
+    const int D = a.D, half = D / 2, jn = D / 16;
     const int nk = a.kctas ? 0 : a.hk;                           // k heads rotated here
     const int heads = a.hq + nk + a.hk;
     const int64_t total = static_cast<int64_t>(a.rows) * heads * jn;
-    const int64_t first = (static_cast<int64_t>(blockIdx.x) - a.kctas) * blockDim.x + threadIdx.x;
-    const int64_t stride = static_cast<int64_t>(gridDim.x - a.kctas) * blockDim.x;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     for (int64_t idx = first; idx < total; idx += stride) {
         const int j = static_cast<int>(idx % jn);
         const int64_t rest = idx / jn;
@@ -343,7 +347,12 @@ int rope_qkv(const char* who, const void* qkv, int64_t qkv_row_stride, int rows,
     if (rows == 0) return SA_OK;
     const int64_t work = static_cast<int64_t>(rows) * (num_heads + (a.kctas ? 0 : num_kv_heads) + num_kv_heads) *
                          (head_dim / 16);
-    rope_qkv_kernel<<<a.kctas + grid_for(work, 256), 256, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (a.kctas) {
+        rope_k_means_kernel<<<a.kctas, 256, smem, st>>>(a);
+        if (int rc = check_launch("rope_k_means_kernel")) return rc;
+    }
+    rope_qkv_kernel<<<grid_for(work, 256), 256, 0, st>>>(a);
     return check_launch("rope_qkv_kernel");
 }
 
