@@ -158,6 +158,118 @@ __device__ __forceinline__ void load_paged_stage(const Params& p, uint8_t* dst, 
     __syncwarp();
 }
 
+// One 64-key tile of a softmax warp (thread r owns query row r = TMEM lane r): waits for S(gt),
+// loads its 64 columns, masks invisible keys (diagonal, kv_len, rows outside the tile's list half),
+// updates the running max (exp2 domain, scale folded) and row sum, writes P into the S columns (e4m3
+// x448 or bf16), rescales O in TMEM when the max grew (not on a unit's first tile), and arrives on
+// P(gt).  gt counts the tiles the CTA has walked (S/P buffer and barrier parities).  Returns false
+// when a bounded wait gave up.
+template <bool FP8>
+__device__ __forceinline__ bool softmax_tile(const Params& p, int gt, bool first, int kb, uint32_t rm, uint32_t tS0,
+                                             uint32_t tO, int qpos_min, int vis, uint32_t my_half, float sl2,
+                                             float pbias, float& m_run, float& l_run, uint64_t* bS, uint64_t* bP,
+                                             uint64_t* bO, volatile int* abort_flag) {
+    using C = Cfg<FP8>;
+        const int b = gt & 1;
+        bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bS + b), (gt >> 1) & 1, abort_flag, p.status, SA_DEV_WAIT_S));
+        if (!ok) return false;
+        tc_fence_after();
+        const uint32_t tS = tS0 + b * C::BN;
+        float x[64];
+        {
+            uint32_t u[64];
+            tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(u));
+            tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(u[i]);
+        }
+        if (rm != 3u || kb + 63 > qpos_min || kb + 63 >= p.kv_len) {
+            const int lim = (rm & my_half) ? vis - kb : -1;      // visible columns: c <= lim
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+                if (c > lim) x[c] = -INFINITY;
+        }
+        float mx;
+        {
+            float a[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[i] = fmax3(x[i], x[8 + i], x[16 + i]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], x[24 + i], x[32 + i]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], x[40 + i], x[48 + i]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[i] = fmaxf(a[i], x[56 + i]);
+            mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+        }
+        // running max used for the exponentials; grows (with an O rescale) only past the slack
+        const float cand = mx * sl2;
+        const bool grow = cand > m_run + C::RESCALE_SLACK || m_run == -INFINITY;
+        const float m_new = grow ? fmaxf(m_run, cand) : m_run;
+        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+        const float alpha = ex2_approx(m_run - m_use);
+        const float2 sl2v = make_float2(sl2, sl2), biasv = make_float2(pbias - m_use, pbias - m_use);
+        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                         make_float2(0.f, 0.f)};
+        auto exp_pair = [&](int c) -> float2 {
+            const float2 e = ffma2(make_float2(x[c], x[c + 1]), sl2v, biasv);
+            // FP8: TILE_EXP_POLY pairs in eight on the FMA pipe, easing the MUFU unit (exp2_poly's
+            // 7.5e-5 relative error is far below e4m3's rounding)
+            const bool on_fma = FP8 && ((c >> 1) & 7) >= 8 - TILE_EXP_POLY;
+            const float2 pr = on_fma ? exp2_poly2(e) : make_float2(ex2_approx(e.x), ex2_approx(e.y));
+            acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pr);
+            return pr;
+        };
+        if constexpr (FP8) {
+            // 64 keys -> 16 columns of 4 e4m3 values (key 4c+i in byte i of column c)
+            uint32_t pk[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                const float2 p01 = exp_pair(4 * c);
+                const float2 p23 = exp_pair(4 * c + 2);
+                pk[c] = static_cast<uint32_t>(pack_e4m3x2(p01.x, p01.y)) |
+                        (static_cast<uint32_t>(pack_e4m3x2(p23.x, p23.y)) << 16);
+            }
+            tmem_st16(tS, pk);
+        } else {
+            // 64 keys -> 32 columns of 2 bf16 values (key 2c+i in half i of column c)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const float2 pr = exp_pair(32 * hh + 2 * c);
+                    pk[c] = pack_bf16x2(pr.x, pr.y);
+                }
+                tmem_st16(tS + 16 * hh, pk);
+            }
+        }
+        const float2 s01 = fadd2(acc[0], acc[1]), s23 = fadd2(acc[2], acc[3]);
+        l_run = l_run * alpha + ((s01.x + s01.y) + (s23.x + s23.y));
+        m_run = m_new;
+        if (!first && __any_sync(0xffffffffu, alpha < 1.f)) {
+            // O rescale: wait until O += P(gt-1) V has completed, then scale in TMEM.  S(gt)
+            // being complete implies O += P(gt-2) V is, so the barrier is at most one phase
+            // behind and the parity wait is unambiguous.
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bO), (gt - 1) & 1, abort_flag, p.status, SA_DEV_WAIT_O));
+            if (!ok) return false;
+            tc_fence_after();
+            uint32_t u[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 128; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_st32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(smem_u32(bP + b));
+    return ok;
+}
+
 // Row r of split tail unit tu (tile m, head h): combines the step ranges' partial outputs, one warp
 // per row, lane l holding head_dim columns 4l..4l+3.  With M the largest running max of the ranges
 // and w_s = 2^(m_s - M): out = (sum_s w_s O_s) * out_scale / (sum_s w_s l_s), 0 for a row with no
@@ -455,103 +567,9 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
             const int kb = kb_next;
             const uint32_t rm = rm_next;
             have_next = walk.template next<SPLIT>(kb_next, rm_next);
-            const int b = t & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bS + b), (t >> 1) & 1, abort_flag, p.status, SA_DEV_WAIT_S));
+            ok = softmax_tile<FP8>(p, t, t == 0, kb, rm, tmem + lane_off + C::S_COL0, tO, qpos_min, vis, my_half, sl2,
+                                   pbias, m_run, l_run, bS, bP, bO, abort_flag);
             if (!ok) break;
-            tc_fence_after();
-            const uint32_t tS = tmem + lane_off + C::S_COL0 + b * C::BN;
-            float x[64];
-            {
-                uint32_t u[64];
-                tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(u));
-                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32));
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(u[i]);
-            }
-            if (rm != 3u || kb + 63 > qpos_min || kb + 63 >= p.kv_len) {
-                const int lim = (rm & my_half) ? vis - kb : -1;      // visible columns: c <= lim
-#pragma unroll
-                for (int c = 0; c < 64; ++c)
-                    if (c > lim) x[c] = -INFINITY;
-            }
-            float mx;
-            {
-                float a[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) a[i] = fmax3(x[i], x[8 + i], x[16 + i]);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], x[24 + i], x[32 + i]);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], x[40 + i], x[48 + i]);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) a[i] = fmaxf(a[i], x[56 + i]);
-                mx = fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
-            }
-            // running max used for the exponentials; grows (with an O rescale) only past the slack
-            const float cand = mx * sl2;
-            const bool grow = cand > m_run + C::RESCALE_SLACK || m_run == -INFINITY;
-            const float m_new = grow ? fmaxf(m_run, cand) : m_run;
-            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-            const float alpha = ex2_approx(m_run - m_use);
-            const float2 sl2v = make_float2(sl2, sl2), biasv = make_float2(pbias - m_use, pbias - m_use);
-            float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                             make_float2(0.f, 0.f)};
-            auto exp_pair = [&](int c) -> float2 {
-                const float2 e = ffma2(make_float2(x[c], x[c + 1]), sl2v, biasv);
-                // FP8: TILE_EXP_POLY pairs in eight on the FMA pipe, easing the MUFU unit (exp2_poly's
-                // 7.5e-5 relative error is far below e4m3's rounding)
-                const bool on_fma = FP8 && ((c >> 1) & 7) >= 8 - TILE_EXP_POLY;
-                const float2 pr = on_fma ? exp2_poly2(e) : make_float2(ex2_approx(e.x), ex2_approx(e.y));
-                acc[(c >> 1) & 3] = fadd2(acc[(c >> 1) & 3], pr);
-                return pr;
-            };
-            if constexpr (FP8) {
-                // 64 keys -> 16 columns of 4 e4m3 values (key 4c+i in byte i of column c)
-                uint32_t pk[16];
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const float2 p01 = exp_pair(4 * c);
-                    const float2 p23 = exp_pair(4 * c + 2);
-                    pk[c] = static_cast<uint32_t>(pack_e4m3x2(p01.x, p01.y)) |
-                            (static_cast<uint32_t>(pack_e4m3x2(p23.x, p23.y)) << 16);
-                }
-                tmem_st16(tS, pk);
-            } else {
-                // 64 keys -> 32 columns of 2 bf16 values (key 2c+i in half i of column c)
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    uint32_t pk[16];
-#pragma unroll
-                    for (int c = 0; c < 16; ++c) {
-                        const float2 pr = exp_pair(32 * hh + 2 * c);
-                        pk[c] = pack_bf16x2(pr.x, pr.y);
-                    }
-                    tmem_st16(tS + 16 * hh, pk);
-                }
-            }
-            const float2 s01 = fadd2(acc[0], acc[1]), s23 = fadd2(acc[2], acc[3]);
-            l_run = l_run * alpha + ((s01.x + s01.y) + (s23.x + s23.y));
-            m_run = m_new;
-            if (t > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
-                // O rescale: wait until O += P(t-1) V_{t-1} has completed, then scale in TMEM.  S(t)
-                // being complete implies O += P(t-2) V_{t-2} is, so the barrier is at most one phase
-                // behind and the parity wait is unambiguous.
-                ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bO), (t - 1) & 1, abort_flag, p.status, SA_DEV_WAIT_O));
-                if (!ok) break;
-                tc_fence_after();
-                uint32_t u[128];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) tmem_ld32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 128; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) tmem_st32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(u + 32 * c));
-            }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(smem_u32(bP + b));
         }
         const int T = t;
         // ---------------------------------------------------------------- epilogue
