@@ -1,14 +1,15 @@
 """Times the reference's own CPU path beside this repository's restatement of it (test infrastructure).
 
 The GPU host has no reference checkout, so bench.py's CPU baseline (`cpu_baseline`, `--impl reference`)
-times the restatement in oracle/ (numpy).  This script, run where the reference checkout exists, times
+times the restatement in oracle/ (numpy selection, fp32 attention on all host threads).  This script,
+run where the reference checkout exists, times
 the reference's own PyTorch path on the same bounded sample -- `SparsePrefill.block_masks` (selection,
 sm120_attn/sparse_prefill.py:42-85) over the whole configs[1] chunk of one KV-head group, then
 `reference()` (masked fp32 attention, sparse_prefill.py:262-279) of the last query blocks -- and the
 oracle on the identical sample, and prints both rates (executed-block TFLOPS, the benchmark's metric)
 with the agreement of their masks.
 
-    python oracle/time_reference_cpu.py [--reference PATH] [--strength unit|strong] [--rows 256]
+    python oracle/time_reference_cpu.py --reference PATH [--strength unit|strong] [--rows 256]
 """
 from __future__ import annotations
 
@@ -34,7 +35,7 @@ Q_START = KV - N_Q
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument('--reference', default='/root/reference')
+    ap.add_argument('--reference', required=True, help='checkout of the reference repository')
     ap.add_argument('--strength', default='unit', choices=['unit', 'strong'])
     ap.add_argument('--rows', type=int, default=256)
     args = ap.parse_args()
