@@ -730,6 +730,13 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     if (!a16(q) || !a16(k) || !a16(v) || !a16(out) || (qrs * E) % 16 || (qhs * E) % 16 || (krs * E) % 16 ||
         (khs * E) % 16 || (vrs * E) % 16 || (vhs * E) % 16 || (ors * 2) % 16 || (ohs * 2) % 16)
         return fail(SA_ERR_ALIGN, "%s: pointers must be 16-byte aligned and strides multiples of 16 bytes", name);
+    if (split && split->splits > 1) {                   // checked before any driver or device call
+        if (split->splits > 16) return fail(SA_ERR_ARG, "%s: splits %d (at most 16)", name, split->splits);
+        const int64_t need = split_workspace_bytes((q_front + n_q + 127) / 128, H, split->splits, split->tail_units);
+        if (need > 0 && (!split->part || (reinterpret_cast<uintptr_t>(split->part) & 15) || split->part_bytes < need))
+            return fail(SA_ERR_ARG, "%s: split workspace needs %lld bytes (16-byte aligned)", name,
+                        static_cast<long long>(need));
+    }
     int box_rows = 0;
     if (paged) {
         if (FP8) return fail(SA_ERR_UNSUPPORTED, "%s: paged K/V is bf16 only", name);
@@ -801,11 +808,6 @@ int launch_attn(const void* q, int64_t qrs, int64_t qhs, const void* k, int64_t 
     p.status = status;
     p.splits = 1;
     if (split && split->splits > 1) {
-        if (split->splits > 16) return fail(SA_ERR_ARG, "%s: splits %d (at most 16)", name, split->splits);
-        const int64_t need = split_workspace_bytes(n_tiles, H, split->splits, split->tail_units);
-        if (need > 0 && (!split->part || (reinterpret_cast<uintptr_t>(split->part) & 15) || split->part_bytes < need))
-            return fail(SA_ERR_ARG, "%s: split workspace needs %lld bytes (16-byte aligned)", name,
-                        static_cast<long long>(need));
         int n_whole, n_tail;
         split_plan(n_tiles, H, split->splits, split->tail_units, &n_whole, &n_tail);
         if (n_tail > 0 && !(FP8 && use_pair_kernel())) {   // the paired-tile kernel runs its units whole

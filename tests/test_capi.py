@@ -38,12 +38,39 @@ def test_library_exports_every_declared_symbol():
     (lambda L: L.sa_attn_fwd_bf16(None, 0, 0, None, 0, 0, None, 0, 0, None, 0, 0, 10, 8, 3, 128, 100, 0, 0, None,
                                   None, 0, 128, 64, 1.0, None, None), -1),
     (lambda L: L.sa_quantize_e4m3(None, 0, 0, 4, 2, 128, None, 0, 9, None, 0, 0, 0, 0, None), -1),
+    # paged entries: no page table
+    (lambda L: L.sa_block_means_paged_bf16(None, 0, 0, 0, None, 16, 10, 2, 128, 0, 64, None, 0, 0, 0, None), -1),
+    (lambda L: L.sa_absmax_paged_bf16(None, 0, 0, 0, None, 16, 0, 10, 2, 128, 1, None, None), -1),
+    (lambda L: L.sa_quantize_paged_e4m3(None, 0, 0, 0, None, 16, 0, 4, 2, 128, None, 0, 1, None, 0, 0, None), -1),
+    (lambda L: L.sa_rope_qkv_means_bf16(None, 0, 4, 8, 2, 128, None, 0, 8, None, None, 0, None, 0, 128, None, 0, 0,
+                                        0, None), -1),
 ])
 def test_argument_validation_without_gpu(call, code):
     from sm120_attn import _native as N
     L = N.lib()
     assert call(L) == code
     assert L.sa_last_error()
+
+
+def test_paged_attention_and_split_refusals():
+    """sa_attn_fwd_bf16_paged refuses page sizes it does not read in place, and sa_attn_fwd_fp8_split
+    too many splits or a short workspace, before any device work (host buffers stand in for device
+    pointers: nothing is dereferenced)."""
+    from sm120_attn import _native as N
+    L = N.lib()
+    buf = (ctypes.c_uint8 * 4096)()
+    b = (ctypes.addressof(buf) + 15) // 16 * 16
+    rc = L.sa_attn_fwd_bf16_paged(b, 1024, 128, b, b, 24 * 256, 256, 128, b, 24, 4, b, 1024, 128, 10, 8, 2, 128, 60,
+                                  0, 50, None, None, 0, 128, 64, 0.1, None, None)
+    assert rc == -3 and b'page_size' in L.sa_last_error()
+    args = [b, 1024, 128, b, 256, 128, b, 256, 128, b, 1024, 128, 10, 8, 2, 128, 60, 0, 50, None, None, 0, 128, 64,
+            b, 0, b, 0, b, 0, 0.1, None]
+    assert L.sa_attn_fwd_fp8_split(*args, 20, 8, b, 1 << 30, None) == -1
+    assert b'splits' in L.sa_last_error()
+    need = L.sa_attn_split_workspace_bytes(10, 0, 8, 4, 8)
+    assert need == 8 * 4 * (128 * 128 + 256) * 4 + 32
+    assert L.sa_attn_fwd_fp8_split(*args, 4, 8, b, need - 16, None) == -1
+    assert b'workspace' in L.sa_last_error()
 
 
 def test_native_error_message():
