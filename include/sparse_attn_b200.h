@@ -45,6 +45,7 @@ extern "C" {
 #define SA_DEV_WAIT_O 0x10       /* a wait for the output accumulator expired             */
 #define SA_DEV_BAD_LIST 0x20     /* a block index in a list was out of range              */
 #define SA_DEV_BAD_PAGE 0x40     /* a page id in a page table was out of range (read as 0) */
+#define SA_DEV_WAIT_KM 0x80      /* a wait for key means staged by the one-pass selection expired */
 
 /* selection modes for sa_select */
 #define SA_SELECT_PER_HEAD 0     /* one row per (query head, q block): union=False         */
@@ -145,6 +146,8 @@ SA_API size_t sa_select_workspace_bytes(int num_heads, int MB, int nb_total);
  * of q it holds (0 for a block without rows).  km, nb_km, nb_total, scale, tau, mode, counts,
  * lists, list_stride, masks: as sa_select (query block m is block qblk0 + m).  q8 (optional):
  * e4m3 copy of every query row as in sa_block_means_bf16 (inv_scale per head or scalar).
+ * status (device int32, may be NULL): SA_DEV_WAIT_KM is set there if a wait for key means staged in
+ * shared memory expires (the unit's rows are then not written).
  * Returns SA_ERR_UNSUPPORTED, launching nothing, for shapes outside the kernel's limits (head_dim
  * 128; at most 16 query heads per KV head; rows of at most 1024 key blocks; query blocks per unit
  * x query heads per KV head x nb_total rounded up to 32 at most 16384); use sa_block_means_bf16 +
@@ -155,7 +158,7 @@ SA_API int sa_select_q(const void* q, int64_t q_row_stride, int64_t q_head_strid
               int num_heads, int num_kv_heads, int head_dim, int nb_total, float scale, float tau, int mode,
               int32_t* counts, int32_t* lists, int64_t list_stride, uint8_t* masks, uint8_t* q8,
               int64_t q8_row_stride, int64_t q8_head_stride, const float* inv_scale, int inv_scale_stride,
-              void* stream);
+              int32_t* status, void* stream);
 
 /*
  * sa_select without a workspace argument: the same selection, with its scratch taken from a

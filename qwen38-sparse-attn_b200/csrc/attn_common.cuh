@@ -204,19 +204,6 @@ __device__ __forceinline__ Walker make_walker(const Params& p, int h, int m, int
 // ------------------------------------------------------------------------------------------------
 // Host side: tensor maps
 // ------------------------------------------------------------------------------------------------
-inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    });
-    return fn;
-}
-
 inline int encode_nd(CUtensorMap* map, bool fp8, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle sw, const char* what) {
     auto fn = encode_fn();

@@ -8,6 +8,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -43,6 +44,21 @@ struct PerContext {
 // The calling thread's current device and context (the context is created if the runtime has not
 // made it yet).  Returns SA_OK, or an SA_ERR_* code with the error text set.
 int current_device_context(const char* who, int* dev, void** ctx);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda);
+// nullptr when the driver does not provide it.
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
 
 // ------------------------------------------------------------------------------------------
 // Small device utilities

@@ -19,6 +19,8 @@
 //      (sparse_prefill.py:78-84, :223), then the row is emitted as count / ascending list / 0-1
 //      mask.  Rows longer than 2048 blocks take a shared-memory path with the same arithmetic.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "sa_common.cuh"
@@ -639,6 +641,11 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel_split(const SelArgs
 //     diagonal and the sink forced per query block, then the union of the mode and the list emission.
 constexpr int FU_THREADS = 256;
 constexpr int FU_MAX_FLOATS = 16384;                              // logits rows x padded blocks
+// key-means staging of the scores: slices of FS_COLS columns of up to FS_ROWS key blocks, loaded by
+// TMA in boxes of FS_BOX rows (32-byte swizzle) into FS_STAGES buffers
+constexpr int FS_COLS = 8, FS_ROWS = 2 * FU_THREADS, FS_STAGES = 3, FS_BOX = 256;
+constexpr int FS_SLICES = 128 / FS_COLS;
+constexpr int FS_STAGE_FLOATS = FS_ROWS * FS_COLS;
 
 // Selection of one row held in shared memory, for the one-pass kernel: the same decision rule as
 // select_row_regs with cheaper fp32 arithmetic around it - exponentials as ex2.approx of the
@@ -708,9 +715,20 @@ __device__ uint32_t select_row_lean(const float* L, int nbc, float tau_f, int la
     };
     const uint32_t top = __float_as_uint(warp_max_f(pmax)) + 1u;
     uint32_t lo = 0u, hi = top;
-    while (hi - lo > 1u) {
+    // The bisection keeps mass(lo) >= tau > mass(hi).  Once no probability lies strictly between
+    // lo and hi, lo is one of the probabilities (else {p >= lo} = {p >= hi}) and the largest whose
+    // mass reaches tau - what the remaining steps would converge to - so from the 8th step on the
+    // search stops there (checked every 4th step).
+    for (int it = 1; hi - lo > 1u; ++it) {
         const uint32_t mid = lo + ((hi - lo) >> 1);
         if (mass32(__uint_as_float(mid)) >= tau_f) lo = mid; else hi = mid;
+        if (it >= 8 && (it & 3) == 0) {
+            const uint32_t span = hi - lo - 1u;                   // bit patterns strictly inside
+            bool inside = false;
+#pragma unroll
+            for (int c = 0; c < NPL; ++c) inside |= __float_as_uint(p[c]) - lo - 1u < span;
+            if (!__any_sync(0xffffffffu, inside)) break;
+        }
     }
     if (!(pred64(lo) && (hi == top || !pred64(hi)))) {
         lo = 0u;
@@ -759,6 +777,8 @@ struct FusedArgs {
     int64_t q8rs, q8hs;
     const float* inv_scale;
     int iss;
+    int* status;                                                  // device status word (SA_DEV_WAIT_KM)
+    int n_whole, split;                                           // units run whole; head subsets of the rest
 };
 
 __device__ __forceinline__ void emit_row(const FusedArgs& a, int64_t unit, uint32_t keep, int npl, int lane) {
@@ -774,28 +794,59 @@ __device__ __forceinline__ void emit_row(const FusedArgs& a, int64_t unit, uint3
     if (a.counts && lane == 0) a.counts[unit] = total;
 }
 
+// One slice of key means (columns sl*FS_COLS.., key blocks p0..) as `boxes` TMA boxes into the stage
+// buffer at `dst`, completing on `bar`.  Out of line: only thread 0 runs it, and inlined its
+// registers would count against the scores loop of every thread.
+__device__ __noinline__ void issue_key_slice(const CUtensorMap* map, uint32_t bar, uint32_t dst, int sl, int p0, int boxes,
+                                             int hk) {
+    mbar_arrive_expect_tx(bar, boxes * FS_BOX * FS_COLS * 4);
+    for (int k = 0; k < boxes; ++k) tma_load_3d(dst + k * FS_BOX * FS_COLS * 4, map, bar, sl * FS_COLS, p0 + k * FS_BOX, hk);
+}
+
 template <int NPL, int MODE>
-__global__ void __launch_bounds__(FU_THREADS, NPL >= 32 ? 2 : 3) select_fused_kernel(const FusedArgs a) {
+__global__ void __launch_bounds__(FU_THREADS, NPL >= 32 ? 2 : 3)
+select_fused_kernel(const FusedArgs a, const __grid_constant__ CUtensorMap km_map) {
     constexpr int QB = MODE == SA_SELECT_PAIR_UNION ? 2 : 1;
     extern __shared__ __align__(16) float fu_smem[];
     const int g = a.H / a.Hk;
-    const int R = QB * g;
     const int D = 128;
-    float* qm = fu_smem;                                          // [R rounded up to 8][D]
-    float* logits = qm + ((R + 7) & ~7) * D;                      // [R][nbp]; the pooling partials first
-    uint32_t* keepw = reinterpret_cast<uint32_t*>(logits + R * a.nbp);   // [R][32] (unions)
-    const int hk = blockIdx.y;
-    const int m0 = blockIdx.x * QB;                               // first query block of the unit
+    // Work unit: (QB query blocks, KV head) in launch order u = hk * units_per_head + i.  The first
+    // n_whole CTAs run one unit each; every later unit is run by `split` CTAs, each for gs = g /
+    // split of its query heads (per-head lists only, where heads are independent), so that a partial
+    // last wave of whole units becomes split times as many smaller CTAs.
+    const int ub = blockIdx.x < a.n_whole ? blockIdx.x : a.n_whole + (blockIdx.x - a.n_whole) / a.split;
+    const int sub = blockIdx.x < a.n_whole ? 0 : (blockIdx.x - a.n_whole) % a.split;
+    const int gs = blockIdx.x < a.n_whole ? g : g / a.split;     // query heads of this CTA
+    const int h0s = sub * gs;                                     // the first of them within the group
+    const int R = QB * gs;                                        // rows of this CTA (layout below: QB * g)
+    const int Rf = QB * g;
+    float* qm = fu_smem;                                          // [rows rounded up to 8][D]
+    float* logits = qm + ((Rf + 7) & ~7) * D;                     // [rows][nbp]; the pooling partials first
+    uint32_t* keepw = reinterpret_cast<uint32_t*>(logits + Rf * a.nbp);  // [rows][32] (unions)
+    float* kstage = reinterpret_cast<float*>(keepw + Rf * 32);   // [FS_STAGES][FS_ROWS][FS_COLS] key means,
+    kstage += ((1024u - (smem_u32(kstage) & 1023u)) & 1023u) / 4;   // 1024-byte aligned (TMA swizzle atoms)
+    __shared__ __align__(8) uint64_t kbar[FS_STAGES];            // stage s full (TMA bytes landed)
+    __shared__ int abort_word;
+    volatile int* abort_flag = &abort_word;
+    const int units_per_head = a.MB / QB;
+    const int hk = ub / units_per_head;
+    const int m0 = (ub - hk * units_per_head) * QB;              // first query block of the unit
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {                                               // ordered before use by the pooling's barriers
+        for (int b = 0; b < FS_STAGES; ++b) mbar_init(smem_u32(&kbar[b]), 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        if (a.nb_km > 0) tma_prefetch_desc(&km_map);
+    }
 
     // ---------------------------------------------------------------- 1. pool
     for (int i = R * D + tid; i < ((R + 7) & ~7) * D; i += FU_THREADS) qm[i] = 0.f;   // zero pad rows
     {
-        const int per_row = g * 16;                               // (head, 16-byte chunk) pairs of a row
+        const int per_row = gs * 16;                              // (head, 16-byte chunk) pairs of a row
         const int RG = FU_THREADS / per_row;                      // row groups
         const int ty = tid / per_row, tx = tid - ty * per_row;
         const int hl = tx >> 4, c = tx & 15;
-        const int h = hk * g + hl;
+        const int h = hk * g + h0s + hl;
         float* partial = logits;                                  // [RG - 1][per_row][8]
         const float inv = a.q8 ? __ldg(a.inv_scale + h * a.iss) : 0.f;
         for (int qb = 0; qb < QB; ++qb) {
@@ -841,7 +892,7 @@ __global__ void __launch_bounds__(FU_THREADS, NPL >= 32 ? 2 : 3) select_fused_ke
                     for (int i = 0; i < 8; ++i) acc[i] += partial[((k - 1) * per_row + tx) * 8 + i];
                 }
                 const float cnt = static_cast<float>(max(hi - lo, 1));
-                float* o = qm + (qb * g + hl) * D + c * 8;
+                float* o = qm + (qb * gs + hl) * D + c * 8;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) o[i] = hi > lo ? __fdiv_rn(acc[i], cnt) : 0.f;
             }
@@ -851,58 +902,93 @@ __global__ void __launch_bounds__(FU_THREADS, NPL >= 32 ? 2 : 3) select_fused_ke
     // the key means may come from the kernel launched just before (programmatic dependent launch)
     grid_dependency_wait();
     // ---------------------------------------------------------------- 2. scores
-    // Lanes split head_dim: lane l holds columns 4l..4l+3 of 8 query rows in registers and reads the
-    // same columns of each key-means row (one coalesced 512-byte row per warp load).  Every 4 key
-    // blocks the 32 partial sums per lane (4 blocks x 8 rows) are reduced across the warp by a
-    // transposing butterfly (31 shuffles), after which lane l holds the score of block l >> 3, row
-    // l & 7.  Rows go in groups of 8 (qm is zero-padded to a multiple of 8 rows).
+    // Register tiles: in each pass over up to FS_ROWS key blocks, thread t owns blocks p0 + t and
+    // p0 + t + FU_THREADS and, per group of 8 query rows, their 8 x 2 dot products over head_dim,
+    // accumulated as (even column, odd column) pairs with packed f32x2 FMAs and added at the end.
+    // The pass's key-means rows stream through shared memory in slices of FS_COLS columns (one
+    // 32-byte piece of each row), FS_STAGES deep: thread 0 issues the TMA boxes of a slice two
+    // slices ahead (rows past nb_km arrive as zeros: the driver's zero padding).  The 32-byte
+    // swizzle swaps row j's two 16-byte halves when bit 2 of j is set, so the 8 lanes of a
+    // quarter-warp (rows j..j+7) read 8 distinct bank groups.  The query means are read as
+    // shared-memory broadcasts.  Waits are bounded: on expiry the CTA records SA_DEV_WAIT_KM, waits
+    // (bounded) for the boxes in flight and exits without writing the unit's rows.
     const int nb_max = min(a.qblk0 + m0 + QB, a.nb_total);       // causal blocks of the unit's last q block
-    {
+    if (a.nb_km == 0) {                                           // no key means: every score is 0
+        for (int i = tid; i < R * nb_max; i += FU_THREADS) logits[(i / nb_max) * a.nbp + i % nb_max] = 0.f;
+    } else {
         const int R8 = (R + 7) & ~7;
-        const float* kmh = a.km + static_cast<int64_t>(hk) * a.khs;
-        const int nwarp = FU_THREADS / 32;
-        const int groups = (nb_max + 3) >> 2;                     // 4-block groups
-        for (int r0 = 0; r0 < R8; r0 += 8) {
-            float4 qv[8];
-#pragma unroll
-            for (int r = 0; r < 8; ++r) qv[r] = reinterpret_cast<const float4*>(qm + (r0 + r) * D)[lane];
-            for (int grp = warp; grp < groups; grp += nwarp) {
-                float v[32];                                      // v[b * 8 + r]: block 4grp+b, row r
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int j = 4 * grp + b;
-                    const bool real = j < nb_max && j < a.nb_km;
-                    const float4 kv = real ? __ldg(reinterpret_cast<const float4*>(kmh + static_cast<int64_t>(j) * a.kbs) + lane)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                    for (int r = 0; r < 8; ++r)
-                        v[b * 8 + r] = fmaf(qv[r].x, kv.x, fmaf(qv[r].y, kv.y, fmaf(qv[r].z, kv.z, qv[r].w * kv.w)));
+        const int ja = tid, jb = tid + FU_THREADS;                // the thread's rows of a stage buffer
+        const int ha = ((ja >> 2) & 1) * 4, hb = ((jb >> 2) & 1) * 4;   // where their columns 0-3 sit
+        uint32_t issued = 0, used = 0;                            // slices issued (thread 0) / consumed
+        auto issue = [&](int p0, int rows, int sl) {
+            const uint32_t b = issued % FS_STAGES;
+            issue_key_slice(&km_map, smem_u32(&kbar[b]), smem_u32(kstage + b * FS_STAGE_FLOATS), sl, p0,
+                            (rows + FS_BOX - 1) / FS_BOX, hk);
+            ++issued;
+        };
+        bool aborted = false;
+        for (int r0 = 0; r0 < R8 && !aborted; r0 += 8) {
+            for (int p0 = 0; p0 < nb_max; p0 += FS_ROWS) {
+                const int rows = min(FS_ROWS, nb_max - p0);
+                if (tid == 0) {
+                    issue(p0, rows, 0);
+                    issue(p0, rows, 1);
                 }
-                // transposing butterfly: at step w (16, 8, 4, 2, 1) lanes exchange the half of their
-                // values selected by their lane bit w and keep the sum of the other half
+                float2 acc[8][2];
 #pragma unroll
-                for (int w = 16; w >= 1; w >>= 1) {
-                    const bool upper = (lane & w) != 0;
+                for (int r = 0; r < 8; ++r) acc[r][0] = acc[r][1] = make_float2(0.f, 0.f);
+                for (int sl = 0; sl < FS_SLICES; ++sl) {
+                    const uint32_t b = used % FS_STAGES;
+                    mbar_wait(smem_u32(&kbar[b]), (used / FS_STAGES) & 1, abort_flag, a.status, SA_DEV_WAIT_KM);
+                    __syncthreads();                              // all waited; slice sl - 1 consumed by all
+                    if (*abort_flag) {                            // the same value for every thread
+                        aborted = true;
+                        break;
+                    }
+                    ++used;
+                    if (tid == 0 && sl + 2 < FS_SLICES) issue(p0, rows, sl + 2);   // into slice sl - 1's buffer
+                    const float* kb = kstage + b * FS_STAGE_FLOATS;
+                    const float4 a0 = *reinterpret_cast<const float4*>(kb + ja * FS_COLS + ha);
+                    const float4 a1 = *reinterpret_cast<const float4*>(kb + ja * FS_COLS + (ha ^ 4));
+                    const float4 b0 = *reinterpret_cast<const float4*>(kb + jb * FS_COLS + hb);
+                    const float4 b1 = *reinterpret_cast<const float4*>(kb + jb * FS_COLS + (hb ^ 4));
 #pragma unroll
-                    for (int i = 0; i < w; ++i) {
-                        const float send = upper ? v[i] : v[i + w];
-                        const float keep = upper ? v[i + w] : v[i];
-                        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, w);
+                    for (int r = 0; r < 8; ++r) {
+                        if (r0 + r >= R) break;                   // padding rows (CTA-uniform)
+                        const float4 q0 = *reinterpret_cast<const float4*>(qm + (r0 + r) * D + sl * FS_COLS);
+                        const float4 q1 = *reinterpret_cast<const float4*>(qm + (r0 + r) * D + sl * FS_COLS + 4);
+                        acc[r][0] = ffma2(make_float2(q0.x, q0.y), make_float2(a0.x, a0.y), acc[r][0]);
+                        acc[r][1] = ffma2(make_float2(q0.x, q0.y), make_float2(b0.x, b0.y), acc[r][1]);
+                        acc[r][0] = ffma2(make_float2(q0.z, q0.w), make_float2(a0.z, a0.w), acc[r][0]);
+                        acc[r][1] = ffma2(make_float2(q0.z, q0.w), make_float2(b0.z, b0.w), acc[r][1]);
+                        acc[r][0] = ffma2(make_float2(q1.x, q1.y), make_float2(a1.x, a1.y), acc[r][0]);
+                        acc[r][1] = ffma2(make_float2(q1.x, q1.y), make_float2(b1.x, b1.y), acc[r][1]);
+                        acc[r][0] = ffma2(make_float2(q1.z, q1.w), make_float2(a1.z, a1.w), acc[r][0]);
+                        acc[r][1] = ffma2(make_float2(q1.z, q1.w), make_float2(b1.z, b1.w), acc[r][1]);
                     }
                 }
-                // lane l now holds value index l (block l >> 3, row l & 7) in v[0]
-                const int b = lane >> 3, r = lane & 7;
-                const int j = 4 * grp + b;
-                if (j < nb_max && r0 + r < R)
-                    logits[(r0 + r) * a.nbp + j] = (j < a.nb_km) ? v[0] * a.scale : 0.f;
+                if (aborted) break;
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    if (r0 + r >= R) break;
+                    float* out = logits + (r0 + r) * a.nbp + p0;
+                    if (ja < rows) out[ja] = (p0 + ja < a.nb_km) ? (acc[r][0].x + acc[r][0].y) * a.scale : 0.f;
+                    if (jb < rows) out[jb] = (p0 + jb < a.nb_km) ? (acc[r][1].x + acc[r][1].y) * a.scale : 0.f;
+                }
+                __syncthreads();                                  // the next pass refills the stage buffers
             }
+        }
+        if (aborted) {                                            // boxes still in flight land before exit
+            if (tid == 0)
+                for (uint32_t sl = used; sl < issued; ++sl) mbar_drain(smem_u32(&kbar[sl % FS_STAGES]), (sl / FS_STAGES) & 1);
+            return;
         }
     }
     __syncthreads();
     // ---------------------------------------------------------------- 3. select
     const int npl_used = (a.nb_total + 31) >> 5;
     for (int r = warp; r < R; r += FU_THREADS / 32) {
-        const int qb = r / g, i = r - qb * g;
+        const int qb = r / gs, i = r - qb * gs;
         const int m = m0 + qb;
         const int gi = a.qblk0 + m;
         const int nbc = min(gi + 1, a.nb_total);
@@ -910,7 +996,7 @@ __global__ void __launch_bounds__(FU_THREADS, NPL >= 32 ? 2 : 3) select_fused_ke
         if (gi < a.nb_total && (gi & 31) == lane) keep |= 1u << (gi >> 5);     // diagonal
         if (lane == 0) keep |= 1u;                                             // sink
         if (MODE == SA_SELECT_PER_HEAD)
-            emit_row(a, static_cast<int64_t>(hk * g + i) * a.MB + m, keep, npl_used, lane);
+            emit_row(a, static_cast<int64_t>(hk * g + h0s + i) * a.MB + m, keep, npl_used, lane);
         else
             keepw[r * 32 + lane] = keep;
     }
@@ -928,6 +1014,12 @@ __global__ void __launch_bounds__(FU_THREADS, NPL >= 32 ? 2 : 3) select_fused_ke
             emit_row(a, static_cast<int64_t>(hk * g + i) * (a.MB / 2) + m0 / 2, keep, npl_used, lane);
         }
     }
+}
+
+// Head-subset tail units of sa_select_q: on unless the environment sets SA_SELECT_SPLIT=0.
+bool select_split_enabled() {
+    const char* e = getenv("SA_SELECT_SPLIT");
+    return !(e && e[0] == '0' && e[1] == 0);
 }
 
 int64_t logits_row_stride(int nb_total) { return (static_cast<int64_t>(nb_total) + 31) / 32 * 32; }
@@ -1021,7 +1113,7 @@ extern "C" int sa_select_q(const void* q, int64_t q_row_stride, int64_t q_head_s
                            int nb_km, int num_heads, int num_kv_heads, int head_dim, int nb_total, float scale,
                            float tau, int mode, int32_t* counts, int32_t* lists, int64_t list_stride, uint8_t* masks,
                            uint8_t* q8, int64_t q8_row_stride, int64_t q8_head_stride, const float* inv_scale,
-                           int inv_scale_stride, void* stream) {
+                           int inv_scale_stride, int32_t* status, void* stream) {
     const char* name = "sa_select_q";
     if (num_heads <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || MB <= 0 || nb_total <= 0 || qblk0 < 0 ||
         nb_km < 0 || n < 0 || q_start < 0 || block <= 0)
@@ -1045,13 +1137,32 @@ extern "C" int sa_select_q(const void* q, int64_t q_row_stride, int64_t q_head_s
         km_head_stride % 4 || (q8 && ((reinterpret_cast<uintptr_t>(q8) & 7) || q8_row_stride % 8 || q8_head_stride % 8)))
         return fail(SA_ERR_ALIGN, "%s: q and km 16-byte aligned, strides of 8 elements (q8: 8 bytes)", name);
     const int per_row = 16 * g, RG = FU_THREADS / per_row;
+    // logits region: also holds the pooling partials, (FU_THREADS / (16 gs) - 1) x 16 gs x 8 floats
+    // (below 2048) for a CTA of gs query heads
     const size_t smem = (static_cast<size_t>((R + 7) & ~7) * 128 + std::max<size_t>(static_cast<size_t>(R) * nbp,
-                         static_cast<size_t>(RG - 1) * per_row * 8) + static_cast<size_t>(R) * 32) * 4;
+                         std::max<size_t>(static_cast<size_t>(RG - 1) * per_row * 8, 2048)) + static_cast<size_t>(R) * 32 +
+                         static_cast<size_t>(FS_STAGES) * FS_STAGE_FLOATS) * 4 + 1024;   // + stage alignment
     FusedArgs fa{static_cast<const uint16_t*>(q), q_row_stride, q_head_stride, n, q_start, block, qblk0, MB, km,
                  km_head_stride, km_block_stride, nb_km, num_heads, num_kv_heads, nb_total, nbp, scale,
                  static_cast<float>(tau), counts, lists, list_stride, masks, q8, q8_row_stride, q8_head_stride,
-                 inv_scale, inv_scale_stride};
-    void (*kern)(const FusedArgs) = nullptr;
+                 inv_scale, inv_scale_stride, status, 0, 1};
+    // key means [Hk][nb_km][128] fp32 as a 3D tensor map: boxes of FS_COLS columns x FS_BOX key
+    // blocks, rows past nb_km read as zeros
+    CUtensorMap km_map;
+    memset(&km_map, 0, sizeof(km_map));
+    if (nb_km > 0) {
+        auto fn = encode_fn();
+        if (!fn) return fail(SA_ERR_TMA, "%s: cuTensorMapEncodeTiled unavailable", name);
+        const cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(nb_km), static_cast<cuuint64_t>(num_kv_heads)};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(km_block_stride) * 4,
+                                       static_cast<cuuint64_t>(km_head_stride) * 4};
+        const cuuint32_t box[3] = {FS_COLS, FS_BOX, 1}, estr[3] = {1, 1, 1};
+        const CUresult r = fn(&km_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(km), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(SA_ERR_TMA, "%s: tensor map for the key means: error %d", name, (int)r);
+    }
+    void (*kern)(const FusedArgs, const CUtensorMap) = nullptr;
 #define SA_FUSED_PICK(NPL_)                                                                            \
     kern = mode == SA_SELECT_PER_HEAD ? select_fused_kernel<NPL_, SA_SELECT_PER_HEAD>                 \
          : mode == SA_SELECT_KV_UNION ? select_fused_kernel<NPL_, SA_SELECT_KV_UNION>                 \
@@ -1061,15 +1172,33 @@ extern "C" int sa_select_q(const void* q, int64_t q_row_stride, int64_t q_head_s
     else if (npl <= 16) { SA_FUSED_PICK(16) }
     else { SA_FUSED_PICK(32) }
 #undef SA_FUSED_PICK
-    if (smem > 48 * 1024) {
+    if (smem > 48 * 1024) {                                       // before the occupancy query below
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
     }
     // launched as a programmatic dependent of the previous kernel in the stream: the pooling of q
     // (written by earlier kernels) may overlap that kernel, whose outputs (the key means) are read
     // only after grid_dependency_wait
+    // Units (QB query blocks, KV head) in launch order; with per-head lists a partial last wave of
+    // resident CTAs is cut into head subsets (largest divisor of g whose CTAs still fit one wave), so
+    // that the units left over after the full waves do not run one CTA each on a few SMs.
+    const int units = (MB / QB) * num_kv_heads;
+    fa.n_whole = units;
+    if (mode == SA_SELECT_PER_HEAD && g > 1 && select_split_enabled()) {
+        int per_sm = 0;
+        cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, FU_THREADS, smem);
+        if (oe != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(oe));
+        const int slots = per_sm * num_sms();
+        const int rem = slots > 0 ? units % slots : 0;
+        for (int d = g; d > 1 && rem > 0; --d)
+            if (g % d == 0 && static_cast<int64_t>(rem) * d <= slots) {
+                fa.n_whole = units - rem;
+                fa.split = d;
+                break;
+            }
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(MB / QB, num_kv_heads);
+    cfg.gridDim = dim3(fa.n_whole + (units - fa.n_whole) * fa.split);
     cfg.blockDim = dim3(FU_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
@@ -1078,7 +1207,7 @@ extern "C" int sa_select_q(const void* q, int64_t q_row_stride, int64_t q_head_s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, fa);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, fa, km_map);
     if (e != cudaSuccess) return fail(SA_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
     return check_launch(name);
 }

@@ -133,7 +133,7 @@ def select_q(q, q_start: int, block: int, qblk0: int, MB: int, km, num_heads: in
            km.stride(1), km.shape[1], num_heads, num_kv_heads, D, nb_total, float(scale), float(tau), mode,
            _p(counts), _p(lists), lists.stride(0) if lists is not None else 0, _p(masks), _p(q8),
            q8.stride(0) if q8 is not None else 0, q8.stride(1) if q8 is not None else 0, _p(inv_scale), iss,
-           _stream(q.device))
+           _p(status_word(q.device)), _stream(q.device))
 
 
 def quantize(x, scale, mode: int, out, transpose: bool = False, rows_pad: int = 0):

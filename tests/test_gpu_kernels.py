@@ -219,6 +219,16 @@ def test_select_q_matches_oracle(case):
         np.testing.assert_array_equal(pc.cpu().numpy(), pmn.sum(1))
 
 
+def test_select_q_without_tail_split(monkeypatch):
+    """configs[0] and configs[1] (strong) with the head-subset CTAs switched off (SA_SELECT_SPLIT=0):
+    every (query block, KV head) unit in one CTA, same checks against the oracle.  With the default,
+    configs[1]'s 512 units leave a partial last wave that runs as CTAs of 2 query heads, and the
+    smaller cases run as head subsets throughout."""
+    monkeypatch.setenv('SA_SELECT_SPLIT', '0')
+    test_select_q_matches_oracle(SEL[0])
+    test_select_q_matches_oracle(SEL[7])
+
+
 # ------------------------------------------------------------------------------------------------
 # kernel (c): attention
 # ------------------------------------------------------------------------------------------------
