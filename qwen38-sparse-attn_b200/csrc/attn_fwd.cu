@@ -171,7 +171,7 @@ __device__ __forceinline__ bool softmax_tile(const Params& p, int gt, bool first
                                              uint64_t* bO, volatile int* abort_flag) {
     using C = Cfg<FP8>;
         const int b = gt & 1;
-        bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bS + b), (gt >> 1) & 1, abort_flag, p.status, SA_DEV_WAIT_S));
+        bool ok = __all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bS + b), (gt >> 1) & 1, abort_flag, p.status, SA_DEV_WAIT_S));
         if (!ok) return false;
         tc_fence_after();
         const uint32_t tS = tS0 + b * C::BN;
@@ -252,7 +252,7 @@ __device__ __forceinline__ bool softmax_tile(const Params& p, int gt, bool first
             // O rescale: wait until O += P(gt-1) V has completed, then scale in TMEM.  S(gt)
             // being complete implies O += P(gt-2) V is, so the barrier is at most one phase
             // behind and the parity wait is unambiguous.
-            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(bO), (gt - 1) & 1, abort_flag, p.status, SA_DEV_WAIT_O));
+            ok = __all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bO), (gt - 1) & 1, abort_flag, p.status, SA_DEV_WAIT_O));
             if (!ok) return false;
             tc_fence_after();
             uint32_t u[128];
@@ -409,7 +409,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
                 // paged K/V: the tile's boxes are worked out while the stage drains
                 PagedBox pbox{0, 0, -1, false};
                 if (paged && have) pbox = paged_box(p, kb, lane);
-                if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(bEmpty + st), ((t / C::NST) & 1) ^ 1, abort_flag,
+                if (!__all_sync(0xffffffffu, mbar_wait_spin(smem_u32(bEmpty + st), ((t / C::NST) & 1) ^ 1, abort_flag,
                                                         p.status, SA_DEV_WAIT_KV)))
                     break;
                 if (!have) {                                          // end of the walk

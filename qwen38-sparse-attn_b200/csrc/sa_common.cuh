@@ -339,8 +339,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
-// Same bound, polling without the suspend hint: for a latency-critical waiter (the MMA issuer)
-// whose wake-up after a suspension would sit on the pipeline's critical path.
+// Same bound, polling without the suspend hint: for a latency-critical waiter whose wake-up after a
+// suspension would sit on the pipeline's critical path (the attention kernel's MMA issuer, its
+// softmax warps waiting for S and O, its producer waiting for a free stage: measured 0.4-0.5%
+// faster than suspending waits there).
 __device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                                int* status, int code) {
     if (mbar_test(bar, parity)) return true;
