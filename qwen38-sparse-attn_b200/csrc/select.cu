@@ -631,12 +631,14 @@ __global__ void __launch_bounds__(SEL_THREADS) select_kernel_split(const SelArgs
 // (b') fused selection from the query rows: pooling, scores and tau selection in one launch
 // ------------------------------------------------------------------------------------------------
 // One CTA per (unit of QB consecutive query blocks, KV head): QB = 2 for the pair union, else 1; its
-// R = QB * g rows are the unit's query blocks times the g query heads of the KV head.
+// R = QB * g rows are the unit's query blocks times the g query heads of the KV head (with per-head
+// lists, the units a full wave of resident CTAs leaves over run as CTAs of a subset of the heads).
 //  1. pool: mean of the query rows of each block (rows of the chunk only) for the g heads, 16-byte
 //     loads along head_dim, rows summed in order per thread and the row groups combined in fixed
 //     order; optionally every row read is also written as e4m3 (the FP8 path's q8, fused);
-//  2. score: logits[r][j] = scale * qm[r] . km[j] for the unit's causal key blocks, fp32, into
-//     shared memory (blocks at or past nb_km score 0: the driver's zero padding);
+//  2. score: logits[r][j] = scale * qm[r] . km[j] for the unit's causal key blocks, fp32 register
+//     tiles over key means staged by TMA, into shared memory (blocks at or past nb_km score 0: the
+//     driver's zero padding);
 //  3. select: one warp per row with select_row_lean (the decision rule of select_kernel), the
 //     diagonal and the sink forced per query block, then the union of the mode and the list emission.
 constexpr int FU_THREADS = 256;
