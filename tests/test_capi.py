@@ -44,6 +44,13 @@ def test_library_exports_every_declared_symbol():
     (lambda L: L.sa_quantize_paged_e4m3(None, 0, 0, 0, None, 16, 0, 4, 2, 128, None, 0, 1, None, 0, 0, None), -1),
     (lambda L: L.sa_rope_qkv_means_bf16(None, 0, 4, 8, 2, 128, None, 0, 8, None, None, 0, None, 0, 128, None, 0, 0,
                                         0, None), -1),
+    # one-pass selection: no heads; head_dim 64 (not served: SA_ERR_UNSUPPORTED); no query pointer
+    (lambda L: L.sa_select_q(None, 0, 0, 100, 0, 128, 0, 1, None, 0, 0, 0, 0, 0, 128, 16, 0.1, 0.95, 0, None, None,
+                             0, None, None, 0, 0, None, 0, None, None), -1),
+    (lambda L: L.sa_select_q(None, 0, 0, 100, 0, 128, 0, 1, None, 0, 0, 0, 8, 2, 64, 16, 0.1, 0.95, 0, None, None,
+                             0, None, None, 0, 0, None, 0, None, None), -3),
+    (lambda L: L.sa_select_q(None, 0, 0, 100, 0, 128, 0, 1, None, 0, 0, 0, 8, 2, 128, 16, 0.1, 0.95, 0, None, None,
+                             0, None, None, 0, 0, None, 0, None, None), -1),
 ])
 def test_argument_validation_without_gpu(call, code):
     from sm120_attn import _native as N
