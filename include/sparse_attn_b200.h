@@ -46,6 +46,7 @@ extern "C" {
 #define SA_DEV_BAD_LIST 0x20     /* a block index in a list was out of range              */
 #define SA_DEV_BAD_PAGE 0x40     /* a page id in a page table was out of range (read as 0) */
 #define SA_DEV_WAIT_KM 0x80      /* a wait for key means staged by the one-pass selection expired */
+#define SA_DEV_WAIT_TEST 0x100   /* the wait of sa_wait_selftest expired (as it always does)  */
 
 /* selection modes for sa_select */
 #define SA_SELECT_PER_HEAD 0     /* one row per (query head, q block): union=False         */
@@ -58,6 +59,13 @@ SA_API const char* sa_last_error(void);
 /* Copy the device status word to the host (synchronises `stream`) and reset it to 0.
  * Returns SA_OK and stores the word in *value. */
 SA_API int sa_read_status(int32_t* status, int32_t* value, void* stream);
+
+/* Diagnostic of the failure path every waiting kernel shares: one CTA waits, with the library's
+ * bounded mbarrier wait, for a barrier phase that nothing completes.  The wait gives up after
+ * limit_ns (1000 .. about 2e9) of wall time, the kernel sets SA_DEV_WAIT_TEST in *status and
+ * returns; the context stays usable.  No reference counterpart (the reference's kernels do not
+ * bound their waits).  Asynchronous on `stream`; read the word with sa_read_status. */
+SA_API int sa_wait_selftest(int32_t* status, int64_t limit_ns, void* stream);
 
 /*
  * (a) Block summary.  Replaces the ATen pooling of

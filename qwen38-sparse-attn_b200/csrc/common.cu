@@ -66,9 +66,34 @@ int current_device_context(const char* who, int* dev, void** ctx) {
     return SA_OK;
 }
 
+// One CTA waits, with the bounded wait every kernel here uses, for a phase of an mbarrier that
+// nothing completes (count 1, no arrival): each thread gives up after limit_ns, the CTA's abort
+// flag is raised and SA_DEV_WAIT_TEST is or-ed into the status word once.
+__global__ void wait_selftest_kernel(int* status, unsigned long long limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ volatile int abort_word;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_word = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    mbar_wait_limit(smem_u32(&bar), 0, &abort_word, status, SA_DEV_WAIT_TEST, limit_ns);
+}
+
 }  // namespace sa
 
 extern "C" int sa_version(void) { return 1; }
+
+extern "C" int sa_wait_selftest(int32_t* status, int64_t limit_ns, void* stream) {
+    if (!status) return sa::fail(SA_ERR_ARG, "sa_wait_selftest: null status word");
+    if (limit_ns < 1000 || limit_ns > static_cast<int64_t>(SA_WAIT_TIMEOUT_NS))
+        return sa::fail(SA_ERR_ARG, "sa_wait_selftest: limit %lld ns outside [1000, %llu]",
+                        static_cast<long long>(limit_ns), static_cast<unsigned long long>(SA_WAIT_TIMEOUT_NS));
+    sa::wait_selftest_kernel<<<1, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        status, static_cast<unsigned long long>(limit_ns));
+    return sa::check_launch("sa_wait_selftest");
+}
 
 extern "C" const char* sa_last_error(void) { return sa::g_err; }
 

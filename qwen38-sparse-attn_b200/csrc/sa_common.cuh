@@ -320,23 +320,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity.  Returns false (and raises the CTA abort
-// flag, plus `code` in the device status word the first time) when the limit expires, or
-// false at once when another thread of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int code) {
+// flag, plus `code` in the device status word the first time) when limit_ns of wall time expire,
+// or false at once when another thread of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                                int code, uint64_t limit_ns) {
     if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 7u) == 0) {
             if (*abort_flag) return false;
-            if (globaltimer() - t0 > SA_WAIT_TIMEOUT_NS) {
+            if (globaltimer() - t0 > limit_ns) {
                 *abort_flag = 1;
                 if (status) atomicOr(status, code);
                 return false;
             }
         }
     }
+}
+
+// The same with the library's limit, SA_WAIT_TIMEOUT_NS.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int code) {
+    return mbar_wait_limit(bar, parity, abort_flag, status, code, SA_WAIT_TIMEOUT_NS);
 }
 
 // Same bound, polling without the suspend hint: for a latency-critical waiter whose wake-up after a

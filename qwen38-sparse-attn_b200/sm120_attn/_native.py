@@ -15,7 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / '_lib' / 'libsa_b200.so'
 SA_OK = 0
 SA_ERR_ARG, SA_ERR_ALIGN, SA_ERR_UNSUPPORTED, SA_ERR_CUDA, SA_ERR_TMA, SA_ERR_DEVICE = -1, -2, -3, -4, -5, -6
 SA_DEV_WAIT_Q, SA_DEV_WAIT_KV, SA_DEV_WAIT_S, SA_DEV_WAIT_P, SA_DEV_WAIT_O, SA_DEV_BAD_LIST = 1, 2, 4, 8, 16, 32
-SA_DEV_BAD_PAGE, SA_DEV_WAIT_KM = 64, 128
+SA_DEV_BAD_PAGE, SA_DEV_WAIT_KM, SA_DEV_WAIT_TEST = 64, 128, 256
 SA_SELECT_PER_HEAD, SA_SELECT_KV_UNION, SA_SELECT_PAIR_UNION = 0, 1, 2
 SA_QUANT_MUL, SA_QUANT_MUL_BF16, SA_QUANT_DIV = 0, 1, 2
 
@@ -25,6 +25,7 @@ _i32, _i64, _f32, _p, _sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctyp
 SIGNATURES = {
     'sa_version': [],
     'sa_read_status': [_p, _p, _p],
+    'sa_wait_selftest': [_p, _i64, _p],
     'sa_block_means_bf16': [_p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _p, _i64, _i64, _i32, _p, _i64, _i64, _p,
                             _i32, _i32, _p],
     'sa_select': [_p, _i64, _i64, _p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _f32, _i32, _p, _p,

@@ -44,6 +44,9 @@ def test_library_exports_every_declared_symbol():
     (lambda L: L.sa_quantize_paged_e4m3(None, 0, 0, 0, None, 16, 0, 4, 2, 128, None, 0, 1, None, 0, 0, None), -1),
     (lambda L: L.sa_rope_qkv_means_bf16(None, 0, 4, 8, 2, 128, None, 0, 8, None, None, 0, None, 0, 128, None, 0, 0,
                                         0, None), -1),
+    # wait self-test: no status word; a limit below 1 us (the pointer is never dereferenced)
+    (lambda L: L.sa_wait_selftest(None, 1000000, None), -1),
+    (lambda L: L.sa_wait_selftest(64, 10, None), -1),
     # one-pass selection: no heads; head_dim 64 (not served: SA_ERR_UNSUPPORTED); no query pointer
     (lambda L: L.sa_select_q(None, 0, 0, 100, 0, 128, 0, 1, None, 0, 0, 0, 0, 0, 128, 16, 0.1, 0.95, 0, None, None,
                              0, None, None, 0, 0, None, 0, None, None), -1),
