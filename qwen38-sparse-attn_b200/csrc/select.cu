@@ -717,6 +717,11 @@ __device__ uint32_t select_row_lean(const float* L, int nbc, float tau_f, int la
     };
     const uint32_t top = __float_as_uint(warp_max_f(pmax)) + 1u;
     uint32_t lo = 0u, hi = top;
+    {   // a lower end closer than 0: blocks below v0 = (1 - tau) / (2 nbc) hold less than half of
+        // 1 - tau, so mass(>= v0) reaches tau for a row summing to about 1 (checked once)
+        const uint32_t v0 = __float_as_uint(0.5f * (1.f - tau_f) / static_cast<float>(nbc));
+        if (v0 > 0u && v0 < hi && mass32(__uint_as_float(v0)) >= tau_f) lo = v0;
+    }
     // The bisection keeps mass(lo) >= tau > mass(hi).  Once no probability lies strictly between
     // lo and hi, lo is one of the probabilities (else {p >= lo} = {p >= hi}) and the largest whose
     // mass reaches tau - what the remaining steps would converge to - so from the 8th step on the
