@@ -67,7 +67,8 @@ struct Cfg {
 
 
 // exponential pairs in eight computed on the FMA pipe (FP8).  1 measured fastest on the power-capped
-// benchmark chunk (11.52 ms vs 11.69 / 11.70 ms for 2 / 3 on one box); short runs favour 3.
+// benchmark chunk (11.52 ms vs 11.69 / 11.70 ms for 2 / 3 on one box; with the polling waits the
+// attention launch took 11.46-11.53 ms against 11.63-11.64 for 0 and 11.60-11.64 for 2).
 #ifndef SA_TILE_EXP_POLY
 #define SA_TILE_EXP_POLY 1
 #endif
